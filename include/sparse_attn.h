@@ -1,0 +1,116 @@
+/*
+ * sparse_attn.h — C ABI of libsparse_attn.so, the B200 (sm_100a) top-k sparse
+ * attention with attention sink.
+ *
+ * Semantics are those of track-01 of inin-zou/kernelgen-challenge:
+ *   o[b,m,h,:] = sum_t softmax([s_0 .. s_{topk-1}, sink[h]])_t * kv[b, idx[b,m,t], :]
+ *   s_t        = scale * <q[b,m,h,:], kv[b, idx[b,m,t], :]>     (fp32 accumulate)
+ * (track-01/reference/reference.py:10-40).  A slot whose index is -1 is
+ * masked (score -inf, row not read), as in the reference's NVIDIA-path kernel
+ * track-01/submission.py:313-322; any other index outside [0, kv_len) is
+ * masked the same way (the reference leaves it undefined).  A row with no
+ * valid slot yields o = 0.
+ *
+ * Every entry point below replaces one piece of the reference's Python
+ * boundary, the function sparse_attn(q, kv, attn_sink, topk_idxs, scale) at
+ * track-01/submission.py:975-1021 (validation :989, contiguity :995-998,
+ * output allocation :1000, kernel launch :1006-1021).
+ *
+ * Conventions
+ *   - bf16 tensors are passed as untyped pointers to 16-bit words.
+ *   - All device pointers live on the device that is current for the calling
+ *     thread; `stream` is a cudaStream_t (NULL = legacy default stream).
+ *   - The caller owns every buffer (inputs, output, workspace).  sa_fwd never
+ *     allocates device memory and never synchronises; all work is ordered on
+ *     `stream`.
+ *   - Reentrant: concurrent calls on different streams/devices are allowed if
+ *     they use different workspaces.
+ *   - Return value 0 = success, negative = error (SA_ERR_*); sa_strerror()
+ *     gives a message, sa_last_cuda_error() the last cudaError_t seen by the
+ *     calling thread.
+ */
+#ifndef SPARSE_ATTN_H_
+#define SPARSE_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SA_OK 0
+#define SA_ERR_INVALID_ARG (-1) /* null pointer, bad shape/stride/alignment */
+#define SA_ERR_WORKSPACE (-2)   /* workspace missing or too small          */
+#define SA_ERR_CUDA (-3)        /* CUDA runtime error (see last_cuda_error) */
+#define SA_ERR_UNSUPPORTED (-4) /* h != 16, d != 512, or no sm_100 device   */
+
+/* Kernel variants for sa_fwd_ex (SA_VARIANT_AUTO picks the fastest). */
+#define SA_VARIANT_AUTO 0
+#define SA_VARIANT_MMA 1     /* warp mma.sync + cp.async gather            */
+#define SA_VARIANT_TCGEN05 2 /* tcgen05 MMA (TMEM accumulators) + TMA gather */
+
+/* Library ABI version (major * 10000 + minor * 100 + patch). */
+int sa_version(void);
+
+/* Human-readable text for an SA_* return code. */
+const char* sa_strerror(int code);
+
+/* 1 if kernel variant `variant` (SA_VARIANT_*) is built into this library and
+ * can run on the current device's architecture, else 0.  No counterpart in
+ * the reference (its backend probe is track-01/submission.py:927-969). */
+int sa_variant_available(int variant);
+
+/* Last cudaError_t observed by this thread inside the library (0 if none). */
+int sa_last_cuda_error(void);
+
+/*
+ * Bytes of device workspace sa_fwd needs for this problem on `device`
+ * (a CUDA device ordinal).  Depends only on (b*m, topk) and the device's SM
+ * count.  Replaces nothing in the reference: the reference kernel keeps all
+ * state in registers (track-01/submission.py:1006-1021); the persistent
+ * split kernels here spill per-CTA partial results for query rows that span
+ * two CTAs.  Returns 0 on error (e.g. bad device).
+ */
+size_t sa_workspace_bytes(int64_t b, int64_t m, int64_t topk, int device);
+
+/*
+ * Forward pass.  Replaces track-01/submission.py:975-1021 (the `sparse_attn`
+ * wrapper and its kernel launch) — the caller has already allocated `o`
+ * (submission.py:1000) and made the last dimension contiguous
+ * (submission.py:995-998).
+ *
+ *   q     [b, m, h, d]   bf16, strides q_strides (elements), q_strides[3] == 1
+ *   kv    [b, kv_len, d] bf16, strides kv_strides,           kv_strides[2] == 1
+ *   sink  [h]            fp32, contiguous
+ *   idx   [b, m, topk]   int32, strides idx_strides (any, elements)
+ *   o     [b, m, h, d]   bf16, strides o_strides,            o_strides[3] == 1
+ *   h == 16, d == 512; every row start 16-byte aligned (row strides multiples
+ *   of 8 elements, base pointers 16-byte aligned).
+ *   workspace: device memory of at least sa_workspace_bytes(b, m, topk, dev)
+ *   bytes, 256-byte aligned, contents arbitrary (not preserved).
+ */
+int sa_fwd(const void* q, const void* kv, const float* sink, const int32_t* idx, void* o,
+           int64_t b, int64_t m, int64_t h, int64_t d, int64_t kv_len, int64_t topk,
+           const int64_t q_strides[4], const int64_t kv_strides[3],
+           const int64_t idx_strides[3], const int64_t o_strides[4], float scale,
+           void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * sa_fwd with an explicit kernel variant (SA_VARIANT_*) and grid size
+ * (`grid_ctas` <= 0 = one CTA per SM).  For benchmarking and tests; no
+ * counterpart in the reference beyond its per-backend kernel choice at
+ * track-01/submission.py:1003-1271.
+ */
+int sa_fwd_ex(const void* q, const void* kv, const float* sink, const int32_t* idx, void* o,
+              int64_t b, int64_t m, int64_t h, int64_t d, int64_t kv_len, int64_t topk,
+              const int64_t q_strides[4], const int64_t kv_strides[3],
+              const int64_t idx_strides[3], const int64_t o_strides[4], float scale,
+              void* workspace, size_t workspace_bytes, void* stream, int variant,
+              int grid_ctas);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARSE_ATTN_H_ */

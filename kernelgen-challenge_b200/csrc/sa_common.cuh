@@ -1,0 +1,162 @@
+// sa_common.cuh — shared definitions for the sparse_attn sm_100a kernels.
+//
+// Problem (track-01/reference/reference.py:10-40): for every query row
+// (b, m) and every head h of 16,
+//   o[b,m,h,:] = sum_t softmax_t([s_0..s_{topk-1}, sink[h]]) * kv[b, idx[b,m,t], :]
+//   s_t = scale * <q[b,m,h,:], kv[b, idx[b,m,t], :]>
+// with K == V (one shared 512-wide row per slot).  Slots with idx == -1 are
+// masked (track-01/submission.py:313-322); here every idx outside
+// [0, kv_len) is masked, so the kernels never read out of bounds.
+//
+// Work schedule ("units"): the flattened (row, key-block) space.  A query
+// row ("token") has `upt` = ceil(topk / UNIT_KEYS) units of UNIT_KEYS slots.
+// The U = tokens * upt units are cut into `grid` contiguous, equal ranges,
+// one per persistent CTA: CTA g owns [g*U/grid, (g+1)*U/grid).  A CTA's range
+// may cross any number of token boundaries; each maximal piece of one token
+// inside one CTA is a "segment".  A segment that covers
+// its whole token writes the bf16 output directly; a segment that covers only
+// part of its token (at most the first and the last segment of a CTA) writes
+// an fp32 partial (unnormalised O, running max, running sum) into workspace
+// slot 2g (first segment) or 2g+1 (last segment), and a combine kernel merges
+// the partials of each split token.  This balances the gather load across all
+// SMs whatever (b*m, topk) is, which the reference's one-program-per-token
+// grid (submission.py:1005) does not.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sa {
+
+constexpr int kHeads = 16;
+constexpr int kDim = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Params {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* kv;
+  const float* sink;
+  const int32_t* idx;
+  __nv_bfloat16* o;
+  int64_t b, m, kv_len, topk;
+  int64_t q_sb, q_sm, q_sh;  // element strides, d stride is 1
+  int64_t kv_sb, kv_sn;
+  int64_t i_sb, i_sm, i_sk;
+  int64_t o_sb, o_sm, o_sh;
+  float scale_log2;  // scale * log2(e): scores are kept in the log2 domain
+  float* part_acc;   // [2*grid][16][512] fp32 unnormalised partial O
+  float* part_ml;    // [2*grid][2][16]   running max (log2 domain), running sum
+  int64_t upt;       // units per token
+  int64_t units;     // tokens * upt
+  int grid;
+};
+
+// Workspace layout shared by the host (sizing) and the kernels.
+constexpr size_t kPartAccFloats = (size_t)kHeads * kDim;
+constexpr size_t kPartMlFloats = 2 * kHeads;
+
+__host__ __device__ inline size_t workspace_bytes_for_grid(int grid) {
+  size_t acc = (size_t)2 * grid * kPartAccFloats * sizeof(float);
+  size_t ml = (size_t)2 * grid * kPartMlFloats * sizeof(float);
+  return ((acc + 255) & ~(size_t)255) + ((ml + 255) & ~(size_t)255);
+}
+
+__host__ __device__ inline int64_t unit_begin(int64_t g, int64_t units, int64_t grid) {
+  return (g * units) / grid;
+}
+
+// Largest CTA index k with unit_begin(k) <= u (requires grid <= units).
+__host__ __device__ inline int64_t cta_of_unit(int64_t u, int64_t units, int64_t grid) {
+  return ((u + 1) * grid - 1) / units;
+}
+
+// ----------------------------------------------------------------------------
+// PTX wrappers (sm_80+ instructions that remain the right tool on sm_100a for
+// scattered 16-byte row gathers and register-level bf16 MMA).
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// 16-byte async copy global->shared; src_bytes == 0 zero-fills without reading.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async16_hint(uint32_t dst, const void* src, int src_bytes,
+                                                uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;\n" ::"r"(dst),
+               "l"(src), "r"(src_bytes), "l"(policy)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + D, fp32 accumulate.
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ bool slot_valid(int64_t key, int64_t topk, int32_t id,
+                                           int64_t kv_len) {
+  return key < topk && id >= 0 && (int64_t)id < kv_len;
+}
+
+// Final normalisation with the sink as the (topk+1)-th logit
+// (track-01/reference/reference.py:34-38, submission.py:340-345): the sink adds
+// exp(sink - max) to the denominator and nothing to the numerator.
+// m_run is the running max in the log2 domain (-inf when no slot was valid),
+// l_run the running sum of exp2(s - m_run).  Returns the factor that turns the
+// unnormalised accumulator into o.
+__device__ __forceinline__ float sink_factor(float m_run, float l_run, float sink_log2) {
+  float M = fmaxf(m_run, sink_log2);
+  float alpha = exp2f(m_run - M);  // 0 when m_run == -inf
+  float den = l_run * alpha + exp2f(sink_log2 - M);
+  return alpha / den;
+}
+
+}  // namespace sa

@@ -1,0 +1,13 @@
+"""B200-native top-k sparse attention with attention sink.
+
+``sparse_attn(q, kv, attn_sink, topk_idxs, scale)`` is a drop-in for
+``track-01/submission.py:975`` of inin-zou/kernelgen-challenge; the work runs
+in hand-written sm_100a kernels in ``libsparse_attn.so`` (C ABI:
+``include/sparse_attn.h``).
+"""
+from ._lib import (SA_VARIANT_AUTO, SA_VARIANT_MMA, SA_VARIANT_TCGEN05,  # noqa: F401
+                   LIB_PATH, lib)
+from .op import sparse_attn, sparse_attn_out, workspace_bytes  # noqa: F401
+
+__all__ = ["sparse_attn", "sparse_attn_out", "workspace_bytes", "lib", "LIB_PATH",
+           "SA_VARIANT_AUTO", "SA_VARIANT_MMA", "SA_VARIANT_TCGEN05"]

@@ -1,0 +1,77 @@
+"""ctypes binding of ``libsparse_attn.so`` (C ABI in ``include/sparse_attn.h``).
+
+The library is the product: there is no Python or CPU fallback.  If the
+shared object is missing or cannot be loaded, :func:`lib` raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import threading
+
+LIB_PATH = pathlib.Path(__file__).resolve().parent / "libsparse_attn.so"
+
+SA_OK = 0
+SA_ERR_INVALID_ARG = -1
+SA_ERR_WORKSPACE = -2
+SA_ERR_CUDA = -3
+SA_ERR_UNSUPPORTED = -4
+
+SA_VARIANT_AUTO = 0
+SA_VARIANT_MMA = 1
+SA_VARIANT_TCGEN05 = 2
+
+# every function the header declares, with its ctypes signature
+_I64 = ctypes.c_int64
+_P = ctypes.c_void_p
+_I64P = ctypes.POINTER(ctypes.c_int64)
+_FWD_ARGS = [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
+             _I64P, _I64P, _I64P, _I64P, ctypes.c_float, _P, ctypes.c_size_t, _P]
+SIGNATURES = {
+    "sa_version": (ctypes.c_int, []),
+    "sa_strerror": (ctypes.c_char_p, [ctypes.c_int]),
+    "sa_last_cuda_error": (ctypes.c_int, []),
+    "sa_variant_available": (ctypes.c_int, [ctypes.c_int]),
+    "sa_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, ctypes.c_int]),
+    "sa_fwd": (ctypes.c_int, _FWD_ARGS),
+    "sa_fwd_ex": (ctypes.c_int, _FWD_ARGS + [ctypes.c_int, ctypes.c_int]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the shared library; raise if it is unavailable."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing: build it with `python -m sparse_attn.build` "
+                    "(nvcc, sm_100a); sparse_attn has no fallback implementation")
+            h = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(h, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = h
+    return _lib
+
+
+def strerror(code: int) -> str:
+    return lib().sa_strerror(code).decode()
+
+
+def check(code: int) -> None:
+    if code != SA_OK:
+        msg = strerror(code)
+        if code == SA_ERR_CUDA:
+            msg += f" (cudaError {lib().sa_last_cuda_error()})"
+        raise RuntimeError(f"sparse_attn: {msg} [status {code}]")
+
+
+def i64_array(values) -> ctypes.Array:
+    return (ctypes.c_int64 * len(values))(*values)

@@ -1,0 +1,123 @@
+"""``sparse_attn`` as a torch custom op over the C ABI.
+
+Drop-in for ``track-01/submission.py:975`` — same name, arguments, dtypes,
+shapes and return value:
+
+    sparse_attn(q[b,m,16,512] bf16, kv[b,kv_len,512] bf16, attn_sink[16] fp32,
+                topk_idxs[b,m,topk] int32, scale: float) -> o[b,m,16,512] bf16
+
+Like the reference wrapper it asserts ``q.dim() == 4`` (submission.py:989),
+makes the inputs contiguous (:995-998) and allocates the output (:1000); the
+launch goes to ``libsparse_attn.so`` on the current CUDA stream.  Anything the
+C library rejects raises ``RuntimeError`` with the library's status text.
+There is no CPU path: CPU tensors raise.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+__all__ = ["sparse_attn", "sparse_attn_out", "workspace_bytes"]
+
+
+def workspace_bytes(b: int, m: int, topk: int, device: torch.device | int | None = None) -> int:
+    dev = torch.cuda.current_device() if device is None else torch.device("cuda", device).index \
+        if isinstance(device, int) else (device.index if device.index is not None
+                                          else torch.cuda.current_device())
+    n = _lib.lib().sa_workspace_bytes(b, m, topk, dev)
+    if n == 0:
+        raise RuntimeError(f"sparse_attn: cannot size workspace on cuda:{dev}")
+    return int(n)
+
+
+def _validate(q, kv, attn_sink, topk_idxs):
+    assert q.dim() == 4
+    if kv.dim() != 3 or attn_sink.dim() != 1 or topk_idxs.dim() != 3:
+        raise RuntimeError("sparse_attn: expected kv [b,kv_len,d], attn_sink [h], "
+                           "topk_idxs [b,m,topk]")
+    for name, t in (("q", q), ("kv", kv), ("attn_sink", attn_sink), ("topk_idxs", topk_idxs)):
+        if not t.is_cuda:
+            raise RuntimeError(f"sparse_attn: {name} must be a CUDA tensor (no CPU path)")
+    if q.dtype != torch.bfloat16 or kv.dtype != torch.bfloat16:
+        raise RuntimeError("sparse_attn: q and kv must be bfloat16")
+    if attn_sink.dtype != torch.float32:
+        raise RuntimeError("sparse_attn: attn_sink must be float32")
+    if topk_idxs.dtype != torch.int32:
+        raise RuntimeError("sparse_attn: topk_idxs must be int32")
+    b, m, h, d = q.shape
+    if kv.shape[0] != b or kv.shape[2] != d or topk_idxs.shape[:2] != (b, m) \
+            or attn_sink.shape[0] != h:
+        raise RuntimeError(f"sparse_attn: inconsistent shapes q{tuple(q.shape)} "
+                           f"kv{tuple(kv.shape)} sink{tuple(attn_sink.shape)} "
+                           f"idx{tuple(topk_idxs.shape)}")
+
+
+def _row_ok(t: torch.Tensor) -> bool:
+    return t.stride(-1) == 1 and t.data_ptr() % 16 == 0 and all(
+        s % 8 == 0 for s in t.stride()[:-1])
+
+
+def sparse_attn_out(o, q, kv, attn_sink, topk_idxs, scale, workspace=None, *,
+                    variant: int = _lib.SA_VARIANT_AUTO, grid: int = 0, stream=None):
+    """Write ``sparse_attn(q, kv, attn_sink, topk_idxs, scale)`` into ``o``.
+
+    No copies: q/kv/o need a unit last-dim stride and 16-byte aligned rows.
+    ``workspace`` (uint8 CUDA tensor of at least :func:`workspace_bytes`) is
+    allocated here when omitted.  ``variant``/``grid`` select the kernel
+    variant and persistent grid size (0 = automatic).
+    """
+    b, m, h, d = q.shape
+    kv_len, topk = kv.shape[1], topk_idxs.shape[-1]
+    if workspace is None:
+        workspace = torch.empty(workspace_bytes(b, m, topk, q.device), dtype=torch.uint8,
+                                device=q.device)
+    st = torch.cuda.current_stream(q.device) if stream is None else stream
+    L = _lib.lib()
+    rc = L.sa_fwd_ex(
+        q.data_ptr(), kv.data_ptr(), attn_sink.data_ptr(), topk_idxs.data_ptr(), o.data_ptr(),
+        b, m, h, d, kv_len, topk,
+        _lib.i64_array(q.stride()), _lib.i64_array(kv.stride()),
+        _lib.i64_array(topk_idxs.stride()), _lib.i64_array(o.stride()),
+        float(scale), workspace.data_ptr(), workspace.numel(), st.cuda_stream,
+        int(variant), int(grid))
+    _lib.check(rc)
+    return o
+
+
+@torch.library.custom_op("sparse_attn_b200::fwd", mutates_args=())
+def _fwd(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor,
+         topk_idxs: torch.Tensor, scale: float) -> torch.Tensor:
+    _validate(q, kv, attn_sink, topk_idxs)
+    q_c = q if _row_ok(q) else q.contiguous()
+    kv_c = kv if _row_ok(kv) else kv.contiguous()
+    sink_c = attn_sink.contiguous()
+    b, m, h, d = q.shape
+    o = torch.empty(b, m, h, d, dtype=q.dtype, device=q.device)
+    if o.numel() == 0:
+        return o
+    with torch.cuda.device(q.device):
+        sparse_attn_out(o, q_c, kv_c, sink_c, topk_idxs, scale)
+    return o
+
+
+@_fwd.register_fake
+def _(q, kv, attn_sink, topk_idxs, scale):
+    assert q.dim() == 4
+    return q.new_empty(q.shape)
+
+
+def sparse_attn(q, kv, attn_sink, topk_idxs, scale):
+    """Top-k sparse attention with attention sink (track-01 signature).
+
+    Args:
+        q:          [b, m, h, d]   bf16 (h = 16, d = 512)
+        kv:         [b, kv_len, d] bf16 (K and V shared)
+        attn_sink:  [h]            fp32
+        topk_idxs:  [b, m, topk]   int32; -1 (or any index outside [0, kv_len))
+                    marks a masked slot
+        scale:      float
+    Returns:
+        o:          [b, m, h, d]   bf16
+    """
+    return _fwd(q, kv, attn_sink, topk_idxs, float(scale))
