@@ -61,6 +61,12 @@ const char* sa_strerror(int code);
  * the reference (its backend probe is track-01/submission.py:927-969). */
 int sa_variant_available(int variant);
 
+/* Debug/health query, synchronous: copies into *flags the error word that the
+ * tensor-core kernel sets on the current device when one of its bounded
+ * pipeline waits gave up (0 = never).  Intended for tests and health checks,
+ * not the hot path.  No counterpart in the reference. */
+int sa_device_status(int* flags);
+
 /* Last cudaError_t observed by this thread inside the library (0 if none). */
 int sa_last_cuda_error(void);
 

@@ -18,6 +18,8 @@ cudaError_t launch_tc(const Params& p, cudaStream_t st);
 int tc_unit_keys();
 int tc_ctas_per_sm();
 bool tc_available();
+bool tc_supports(const Params& p);
+int read_tc_error(int* flags);
 }  // namespace sa
 
 namespace {
@@ -84,6 +86,13 @@ const char* sa_strerror(int code) {
 
 int sa_last_cuda_error(void) { return t_last_cuda_error; }
 
+int sa_device_status(int* flags) {
+  if (flags == nullptr) return SA_ERR_INVALID_ARG;
+  const int e = sa::read_tc_error(flags);
+  if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
+  return SA_OK;
+}
+
 int sa_variant_available(int variant) {
   switch (variant) {
     case SA_VARIANT_AUTO:
@@ -141,19 +150,6 @@ int sa_fwd_ex(const void* q, const void* kv, const float* sink, const int32_t* i
   if (di->err != cudaSuccess) return fail_cuda(di->err);
   if (di->major != 10) return SA_ERR_UNSUPPORTED;
 
-  if (variant == SA_VARIANT_AUTO) variant = SA_VARIANT_MMA;
-  int unit_keys, ctas_per_sm;
-  if (variant == SA_VARIANT_MMA) {
-    unit_keys = sa::mma_unit_keys();
-    ctas_per_sm = 1;
-  } else if (variant == SA_VARIANT_TCGEN05) {
-    if (!sa::tc_available()) return SA_ERR_UNSUPPORTED;
-    unit_keys = sa::tc_unit_keys();
-    ctas_per_sm = sa::tc_ctas_per_sm();
-  } else {
-    return SA_ERR_INVALID_ARG;
-  }
-
   sa::Params p{};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.kv = static_cast<const __nv_bfloat16*>(kv);
@@ -176,6 +172,22 @@ int sa_fwd_ex(const void* q, const void* kv, const float* sink, const int32_t* i
   p.o_sm = o_strides[1];
   p.o_sh = o_strides[2];
   p.scale_log2 = scale * sa::kLog2e;
+
+  // variant: the tensor-core path whenever its TMA maps can describe the
+  // inputs, the warp-MMA path otherwise
+  if (variant == SA_VARIANT_AUTO)
+    variant = (sa::tc_available() && sa::tc_supports(p)) ? SA_VARIANT_TCGEN05 : SA_VARIANT_MMA;
+  int unit_keys, ctas_per_sm;
+  if (variant == SA_VARIANT_MMA) {
+    unit_keys = sa::mma_unit_keys();
+    ctas_per_sm = 1;
+  } else if (variant == SA_VARIANT_TCGEN05) {
+    if (!sa::tc_available() || !sa::tc_supports(p)) return SA_ERR_UNSUPPORTED;
+    unit_keys = sa::tc_unit_keys();
+    ctas_per_sm = sa::tc_ctas_per_sm();
+  } else {
+    return SA_ERR_INVALID_ARG;
+  }
   p.upt = ceil_div(topk > 0 ? topk : 1, unit_keys);  // topk == 0: one all-masked unit
   p.units = b * m * p.upt;
 

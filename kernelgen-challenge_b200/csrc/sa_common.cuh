@@ -71,6 +71,10 @@ __host__ __device__ inline int64_t cta_of_unit(int64_t u, int64_t units, int64_t
   return ((u + 1) * grid - 1) / units;
 }
 
+// Launches the LSE-combine kernel when some row is split across CTAs
+// (defined in sa_mma.cu, shared by every variant).
+cudaError_t launch_combine(const Params& p, cudaStream_t st);
+
 // ----------------------------------------------------------------------------
 // PTX wrappers (sm_80+ instructions that remain the right tool on sm_100a for
 // scattered 16-byte row gathers and register-level bf16 MMA).

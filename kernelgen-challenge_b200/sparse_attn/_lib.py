@@ -32,6 +32,7 @@ SIGNATURES = {
     "sa_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "sa_last_cuda_error": (ctypes.c_int, []),
     "sa_variant_available": (ctypes.c_int, [ctypes.c_int]),
+    "sa_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "sa_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, ctypes.c_int]),
     "sa_fwd": (ctypes.c_int, _FWD_ARGS),
     "sa_fwd_ex": (ctypes.c_int, _FWD_ARGS + [ctypes.c_int, ctypes.c_int]),
@@ -71,6 +72,13 @@ def check(code: int) -> None:
         if code == SA_ERR_CUDA:
             msg += f" (cudaError {lib().sa_last_cuda_error()})"
         raise RuntimeError(f"sparse_attn: {msg} [status {code}]")
+
+
+def device_status() -> int:
+    """Error word of the tensor-core kernel on the current device (0 = healthy)."""
+    v = ctypes.c_int(0)
+    check(lib().sa_device_status(ctypes.byref(v)))
+    return v.value
 
 
 def i64_array(values) -> ctypes.Array:
