@@ -115,6 +115,30 @@ int sa_fwd_ex(const void* q, const void* kv, const float* sink, const int32_t* i
               void* workspace, size_t workspace_bytes, void* stream, int variant,
               int grid_ctas);
 
+/* Largest persistent grid sa_fwd_noalloc serves from its built-in scratch. */
+#define SA_NOALLOC_MAX_CTAS 160
+
+/*
+ * sa_fwd for callers that cannot allocate device memory (a framework that owns
+ * every allocation, a pre-reserved serving loop, code that must not enter the
+ * allocator).  No counterpart in the reference.  Same arguments as sa_fwd
+ * without the workspace; `grid_ctas` <= 0 picks min(SM count, 160).
+ *   - The scratch is one static device array of ~10.5 MB (partials of
+ *     SA_NOALLOC_MAX_CTAS CTAs) that each GPU loading the library keeps until
+ *     the process exits.  grid_ctas > SA_NOALLOC_MAX_CTAS returns
+ *     SA_ERR_WORKSPACE.  Allocates nothing, ever.
+ *   - The first call on a device looks up the array's device address (once,
+ *     with that device current); make that first call before any stream
+ *     capture.
+ *   - All calls on a device share the array: calls that may overlap on the
+ *     GPU race, so order them (one stream, or events between streams).
+ */
+int sa_fwd_noalloc(const void* q, const void* kv, const float* sink, const int32_t* idx, void* o,
+                   int64_t b, int64_t m, int64_t h, int64_t d, int64_t kv_len, int64_t topk,
+                   const int64_t q_strides[4], const int64_t kv_strides[3],
+                   const int64_t idx_strides[3], const int64_t o_strides[4], float scale,
+                   void* stream, int grid_ctas);
+
 #ifdef __cplusplus
 }
 #endif

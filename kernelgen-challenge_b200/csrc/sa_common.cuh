@@ -56,7 +56,7 @@ struct Params {
 constexpr size_t kPartAccFloats = (size_t)kHeads * kDim;
 constexpr size_t kPartMlFloats = 2 * kHeads;
 
-__host__ __device__ inline size_t workspace_bytes_for_grid(int grid) {
+__host__ __device__ constexpr size_t workspace_bytes_for_grid(int grid) {
   size_t acc = (size_t)2 * grid * kPartAccFloats * sizeof(float);
   size_t ml = (size_t)2 * grid * kPartMlFloats * sizeof(float);
   return ((acc + 255) & ~(size_t)255) + ((ml + 255) & ~(size_t)255);

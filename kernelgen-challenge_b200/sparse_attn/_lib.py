@@ -36,6 +36,7 @@ SIGNATURES = {
     "sa_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, ctypes.c_int]),
     "sa_fwd": (ctypes.c_int, _FWD_ARGS),
     "sa_fwd_ex": (ctypes.c_int, _FWD_ARGS + [ctypes.c_int, ctypes.c_int]),
+    "sa_fwd_noalloc": (ctypes.c_int, _FWD_ARGS[:16] + [_P, ctypes.c_int]),
 }
 
 _lock = threading.Lock()
