@@ -199,10 +199,9 @@ int sa_fwd_ex(const void* q, const void* kv, const float* sink, const int32_t* i
   const size_t need = sa::workspace_bytes_for_grid(p.grid);
   if (workspace == nullptr || workspace_bytes < need) return SA_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return SA_ERR_INVALID_ARG;
-  const size_t acc_bytes =
-      ((size_t)2 * p.grid * sa::kPartAccFloats * sizeof(float) + 255) & ~(size_t)255;
-  p.part_acc = static_cast<float*>(workspace);
-  p.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + acc_bytes);
+  char* ws = static_cast<char*>(workspace);
+  p.part_acc = reinterpret_cast<float*>(ws);
+  p.part_ml = reinterpret_cast<float*>(ws + sa::ws_acc_bytes(p.grid));
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   e = (variant == SA_VARIANT_MMA) ? sa::launch_mma(p, st) : sa::launch_tc(p, st);

@@ -56,10 +56,14 @@ struct Params {
 constexpr size_t kPartAccFloats = (size_t)kHeads * kDim;
 constexpr size_t kPartMlFloats = 2 * kHeads;
 
+__host__ __device__ constexpr size_t ws_acc_bytes(int grid) {
+  return ((size_t)2 * grid * kPartAccFloats * sizeof(float) + 255) & ~(size_t)255;
+}
+__host__ __device__ constexpr size_t ws_ml_bytes(int grid) {
+  return ((size_t)2 * grid * kPartMlFloats * sizeof(float) + 255) & ~(size_t)255;
+}
 __host__ __device__ constexpr size_t workspace_bytes_for_grid(int grid) {
-  size_t acc = (size_t)2 * grid * kPartAccFloats * sizeof(float);
-  size_t ml = (size_t)2 * grid * kPartMlFloats * sizeof(float);
-  return ((acc + 255) & ~(size_t)255) + ((ml + 255) & ~(size_t)255);
+  return ws_acc_bytes(grid) + ws_ml_bytes(grid);
 }
 
 __host__ __device__ inline int64_t unit_begin(int64_t g, int64_t units, int64_t grid) {

@@ -281,11 +281,20 @@ __global__ void __launch_bounds__(NT, 1) sa_mma_fwd_kernel(const Params p) {
 }  // namespace mma_path
 
 // ----------------------------------------------------------------------------
-// LSE combine: one block per CTA range; block g merges the token whose last
-// unit it owns if that token started in an earlier CTA.  Partials come from
-// CTAs first..g in unit order (slot rule in sa_common.cuh).
+// LSE combine of split rows (shared by every variant).
+// Block (g, hg): if CTA g ends a row that started in an earlier CTA ("owns"
+// it), merge the fp32 partials of CTAs f..g of that row for heads
+// 4hg..4hg+3, with the sink as the extra logit (reference.py:34-38); partial
+// slots follow the rule in sa_common.cuh.  Thread: one head, 8 columns.  All
+// partial loads of a thread are issued together (two memory round trips for
+// up to kCombineBatch partials).  Launched as a programmatic dependent of the
+// forward kernel: griddepcontrol.wait returns once that grid has completed
+// and its stores are visible.
 // ----------------------------------------------------------------------------
+constexpr int kCombineBatch = 8;
+
 __global__ void __launch_bounds__(256) sa_combine_kernel(const Params p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int64_t G = p.grid, g = blockIdx.x, U = p.units, upt = p.upt;
   const int64_t u0 = unit_begin(g, U, G), u1 = unit_begin(g + 1, U, G);
   if (u0 >= u1) return;
@@ -293,46 +302,65 @@ __global__ void __launch_bounds__(256) sa_combine_kernel(const Params p) {
   if (u0 == ts || u1 < te) return;
   const int64_t f = cta_of_unit(ts, U, G);
   const bool f_mid = unit_begin(f, U, G) < ts;
+  const int np = static_cast<int>(g - f + 1);
+  auto slot_of = [&](int k) -> int64_t { return (k == 0 && f_mid) ? 2 * f + 1 : 2 * (f + k); };
 
-  const int tid = threadIdx.x;
-  const int h = tid >> 4, d0 = (tid & 15) * 32;
+  const int h = 4 * blockIdx.y + (threadIdx.x >> 6);
+  const int d0 = (threadIdx.x & 63) * 8;
   const float sink_l2 = __ldg(p.sink + h) * kLog2e;
-  float M = sink_l2;
-  for (int64_t k = f; k <= g; ++k) {
-    const int64_t slot = (k == f && f_mid) ? 2 * f + 1 : 2 * k;
-    M = fmaxf(M, p.part_ml[slot * kPartMlFloats + h]);
-  }
-  float den = exp2f(sink_l2 - M);
-  float acc[32];
+  float acc[8];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) acc[j] = 0.f;
-  for (int64_t k = f; k <= g; ++k) {
-    const int64_t slot = (k == f && f_mid) ? 2 * f + 1 : 2 * k;
-    const float w = exp2f(p.part_ml[slot * kPartMlFloats + h] - M);
-    den += p.part_ml[slot * kPartMlFloats + kHeads + h] * w;
-    const float4* src =
-        reinterpret_cast<const float4*>(p.part_acc + slot * kPartAccFloats + h * kDim + d0);
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  // running merge over batches of partials (one batch in practice)
+  float M = sink_l2, den = 1.f;  // den is relative to M: exp2(sink - M) with M = sink
+  for (int k0 = 0; k0 < np; k0 += kCombineBatch) {
+    float mk[kCombineBatch], lk[kCombineBatch];
+    float4 va[kCombineBatch], vb[kCombineBatch];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 v = src[j];
-      acc[4 * j + 0] += w * v.x;
-      acc[4 * j + 1] += w * v.y;
-      acc[4 * j + 2] += w * v.z;
-      acc[4 * j + 3] += w * v.w;
+    for (int k = 0; k < kCombineBatch; ++k) {
+      if (k0 + k < np) {
+        const int64_t sl = slot_of(k0 + k);
+        mk[k] = __ldcg(p.part_ml + sl * kPartMlFloats + h);
+        lk[k] = __ldcg(p.part_ml + sl * kPartMlFloats + kHeads + h);
+        const float4* src =
+            reinterpret_cast<const float4*>(p.part_acc + sl * kPartAccFloats + h * kDim + d0);
+        va[k] = __ldcg(src);
+        vb[k] = __ldcg(src + 1);
+      }
     }
+    float Mb = M;
+#pragma unroll
+    for (int k = 0; k < kCombineBatch; ++k)
+      if (k0 + k < np) Mb = fmaxf(Mb, mk[k]);
+    const float r = exp2f(M - Mb);  // rescale what was merged so far
+    den *= r;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] *= r;
+#pragma unroll
+    for (int k = 0; k < kCombineBatch; ++k) {
+      if (k0 + k < np) {
+        const float w = exp2f(mk[k] - Mb);
+        den += lk[k] * w;
+        acc[0] += w * va[k].x;
+        acc[1] += w * va[k].y;
+        acc[2] += w * va[k].z;
+        acc[3] += w * va[k].w;
+        acc[4] += w * vb[k].x;
+        acc[5] += w * vb[k].y;
+        acc[6] += w * vb[k].z;
+        acc[7] += w * vb[k].w;
+      }
+    }
+    M = Mb;
   }
   const float inv = 1.f / den;
   const int64_t tb = t / p.m, tm = t - tb * p.m;
-  __nv_bfloat16* ob = p.o + tb * p.o_sb + tm * p.o_sm + h * p.o_sh + d0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint4 w;
-    w.x = pack_bf16x2(acc[8 * j + 0] * inv, acc[8 * j + 1] * inv);
-    w.y = pack_bf16x2(acc[8 * j + 2] * inv, acc[8 * j + 3] * inv);
-    w.z = pack_bf16x2(acc[8 * j + 4] * inv, acc[8 * j + 5] * inv);
-    w.w = pack_bf16x2(acc[8 * j + 6] * inv, acc[8 * j + 7] * inv);
-    *reinterpret_cast<uint4*>(ob + 8 * j) = w;
-  }
+  uint4 w;
+  w.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+  w.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+  w.z = pack_bf16x2(acc[4] * inv, acc[5] * inv);
+  w.w = pack_bf16x2(acc[6] * inv, acc[7] * inv);
+  *reinterpret_cast<uint4*>(p.o + tb * p.o_sb + tm * p.o_sm + h * p.o_sh + d0) = w;
 }
 
 // True when some token is split across CTAs (the combine kernel has work).
@@ -344,8 +372,17 @@ bool any_split(const Params& p) {
 
 cudaError_t launch_combine(const Params& p, cudaStream_t st) {
   if (!any_split(p)) return cudaSuccess;
-  sa_combine_kernel<<<p.grid, 256, 0, st>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.grid), kHeads / 4, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, sa_combine_kernel, p);
 }
 
 int mma_unit_keys() { return mma_path::BN; }

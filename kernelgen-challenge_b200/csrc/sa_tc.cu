@@ -1,37 +1,40 @@
-// sa_tc.cu — persistent gather-attend kernel on the sm_100a tensor path:
-// tcgen05.mma with TMEM accumulators, KV rows gathered by cp.async into the
+// sa_tc.cu — persistent gather-attend kernel for sm_100a: tcgen05 tensor cores
+// for the scores, warp MMAs for P.V, KV rows gathered by cp.async into the
 // 128-byte-swizzled operand layout, Q loaded by TMA.
 //
 // Algorithm: track-01/submission.py:276-347 (math of reference.py:24-40);
 // masking of submission.py:313-322; sink in the denominator only
 // (submission.py:340-345).  Work schedule and split/combine: sa_common.cuh.
 //
-// Per 64-key unit (64 KiB of gathered rows), swap-AB so that the 16 heads sit
-// on the MMA's N dimension:
-//   S^T[64 keys x 16 heads] = K[64 x 512] . Q^T[512 x 16]    (M=64,  N=16, 32 MMAs)
-//   O^T[512 d x 16 heads]  += V^T[512 x 64] . P^T[64 x 16]    (M=128, N=16, 4x4 MMAs)
-// K and V are the same shared-memory tile: read K-major for S^T and MN-major
-// for O^T.  The tile is 8 slabs of [64 keys x 64 columns] in the 128-byte
-// swizzle; Q is 8 slabs of [16 heads x 64 columns].
+// Per 64-key unit (64 KiB of gathered rows):
+//   S^T[64 keys x 16 heads] = K[64 x 512] . Q^T[512 x 16]
+//       tcgen05.mma, M=64 (keys) N=16 (heads), accumulator in TMEM, split into
+//       4 independent partial accumulators (8 MMAs each) so the MMAs pipeline.
+//   O[16 heads x 512] += P[16 x 64] . V[64 x 512]
+//       mma.sync m16n8k16 in the four softmax warps, O in registers (each warp
+//       owns 128 columns), V read with ldmatrix.trans straight from the same
+//       swizzled tile that the tensor core read as K.
+// Why the split: a tcgen05.mma costs ~60 cycles of issue whatever M (64/128)
+// and N (<= 128) are, so at N = 16 heads the 16 P.V MMAs per unit (M=128
+// d-rows, N=16, K=16 keys) took as long as the 32 S MMAs and the single issuing
+// thread bounded the pipeline; P.V as warp MMAs costs the softmax warps about
+// 0.3 us per unit and runs concurrently with the next unit's S^T.
 //
-// Row gathers use cp.async from 128 threads: for random 1 KiB rows it moves
-// more bytes per SM than TMA tile::gather4 (whose per-instruction issue cost
-// caps a single producer warp near 2 TB/s on B200).
-//
-// Warp roles (320 threads, one CTA per SM):
-//   warps 0..3   KV producer: indices -> 32 cp.async per thread per unit into a
-//                3-deep ring of 64 KiB slots (full/empty mbarriers)
-//   warp 8       TMEM owner and MMA issuer (one thread): S^T(i) into a double-buffered TMEM
-//                tile, then O^T += V^T P^T for unit i-1 (so S(i) overlaps the
-//                softmax of unit i-1)
-//   warp 9       Q producer: one tiled TMA per 64 columns when a row starts
-//   warps 4..7   softmax + epilogue; warp 4+q reads TMEM lane quarter q.
-//                Thread = key: 16 scores per thread, no cross-thread reduction
-//                in the common case.  The running max is only raised when a
-//                score exceeds it by more than 2^8 (checked by one barrier
-//                vote per unit); then the block max is reduced and O^T in
-//                TMEM and the per-thread partial sums are rescaled.  The result
-//                is exact for any threshold: P <= 2^8 is safe in bf16/fp32.
+// Warp roles (256 threads, one CTA per SM; few enough threads that the
+// softmax warps never spill: spill reloads queue behind the producer's
+// outstanding copies in the load/store pipe and stall for microseconds):
+//   warps 0..1   KV producer: 64 cp.async (16 B) per thread per unit into a
+//                3-deep ring of 64 KiB slots; completion by hardware arrival
+//                on the slot's full barrier
+//   warp 2       TMEM owner; one thread issues S^T(i) into TMEM buffer i&1
+//   warp 3       Q producer: one tiled TMA per 64 columns when a row starts
+//   warps 4..7   softmax, P.V and epilogue; warp 4+q reads TMEM lane quarter
+//                q (keys 16q..16q+15) and owns output columns [128q, 128q+128).
+//                Thread = key for the softmax: no cross-thread reduction in the
+//                common case.  The running max is only raised when a score
+//                exceeds it by more than 2^8 (one barrier vote per unit); then
+//                the block max is reduced and O and the partial sums are
+//                rescaled.  Exact for any threshold: P <= 2^8 is safe in bf16.
 //
 // Every mbarrier wait is bounded; on a timeout the CTA records an error code
 // in sa_tc_error (readable through sa_device_status) and stops issuing work.
@@ -46,29 +49,56 @@ namespace sa {
 
 __device__ int sa_tc_error;  // nonzero after a bounded wait gave up
 
+#ifdef SA_TRACE
+// Pipeline timeline for development builds only (-DSA_TRACE): per CTA (first
+// kTraceCtas), per unit (first kTraceUnits), per event, %globaltimer in ns.
+constexpr int kTraceCtas = 4, kTraceUnits = 32, kTraceEvents = 8;
+__device__ unsigned long long sa_trace[kTraceCtas][kTraceUnits][kTraceEvents];
+__device__ __forceinline__ void trace_ev(int64_t cta, int unit, int ev) {
+  if (cta < kTraceCtas && unit < kTraceUnits) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    sa_trace[cta][unit][ev] = t;
+  }
+}
+#define SA_TRACE_EV(u, e) trace_ev(blockIdx.x, (u), (e))
+__device__ unsigned long long sa_trace_cta[1024][8];  // start, end, epilogue stages
+__device__ __forceinline__ void trace_cta(int e) {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  if (blockIdx.x < 1024) sa_trace_cta[blockIdx.x][e] = t;
+}
+#define SA_TRACE_CTA(e) trace_cta(e)
+#else
+#define SA_TRACE_EV(u, e) ((void)0)
+#define SA_TRACE_CTA(e) ((void)0)
+#endif
+
 namespace tc_path {
 using namespace tc;
 
-constexpr int UK = 64;               // keys per unit
-constexpr int NSLOT = 3;             // ring depth (units)
-constexpr int SLOT_BYTES = UK * kDim * 2;  // 64 KiB
-constexpr int SLAB_BYTES = UK * 128;       // [64 keys x 64 cols] = 8 KiB
-constexpr int Q_BYTES = kHeads * kDim * 2; // 16 KiB
-constexpr int P_BYTES = UK * kHeads * 2;   // 2 KiB
-constexpr int NT = 320;  // 4 producer, 4 softmax, MMA, Q warps
-constexpr float kRescaleThreshold = 8.0f;  // log2 domain
-constexpr uint32_t kTmemCols = 128;
-constexpr uint32_t kTmemS = 0;   // two S^T buffers: cols [0,16), [16,32)
-constexpr uint32_t kTmemO = 32;  // O^T chunks: cols [32 + 16c, 48 + 16c)
+constexpr int UK = 64;                      // keys per unit
+constexpr int NSLOT = 3;                    // ring depth (units)
+constexpr int SLOT_BYTES = UK * kDim * 2;   // 64 KiB
+constexpr int SLAB_BYTES = UK * 128;        // [64 keys x 64 cols] = 8 KiB
+constexpr int Q_BYTES = kHeads * kDim * 2;  // 16 KiB
+constexpr int P_BYTES = UK * kHeads * 2;    // 2 KiB, P^T [key][head] bf16
+constexpr int NT = 256;                     // 2 producer, MMA, Q, 4 softmax warps
+constexpr float kRescaleThreshold = 8.0f;   // log2 domain
+constexpr int kSAcc = 4;                    // independent S^T accumulators per unit
+constexpr uint32_t kTmemCols = 128;         // S^T buffer b, partial a: cols 16*(4b + a)
 
 struct __align__(1024) Smem {
   uint8_t ring[NSLOT][SLOT_BYTES];
   uint8_t q[Q_BYTES];
-  uint8_t p[2][P_BYTES];
+  uint8_t p[P_BYTES];
   uint32_t mask[NSLOT][2];  // validity: [0] keys 2l, [1] keys 2l+1 (bit l)
   float red_max[4][kHeads];
   float red_l[4][kHeads];
-  uint64_t full[NSLOT], empty[NSLOT], q_full, q_empty, s_full[2], p_full[2];
+  // full: rows landed (128 cp.async arrivals + mask writer); empty: the four
+  // softmax warps finished P.V on the slot; s_full: S^T(i) in TMEM; s_free:
+  // the softmax warps read S^T out of TMEM buffer i&1
+  uint64_t full[NSLOT], empty[NSLOT], q_full, q_empty, s_full[2], s_free[2];
   uint32_t tmem_base;
   int err;
 };
@@ -80,7 +110,7 @@ __device__ __forceinline__ void set_err(Smem& S, int code) {
 
 // Bounded wait that also gives up at once when another warp recorded an error.
 // After an error every role keeps walking its loop (so all threads reach the
-// same named barriers) but issues no more TMA or MMA work.
+// same named barriers) but issues no more copies or MMAs.
 __device__ __forceinline__ bool wait_or_err(Smem& S, uint64_t& bar, uint32_t parity, int code) {
   const uint32_t b = smem_u32(&bar);
   if (*reinterpret_cast<volatile int*>(&S.err) != 0) return false;
@@ -90,6 +120,12 @@ __device__ __forceinline__ bool wait_or_err(Smem& S, uint64_t& bar, uint32_t par
   }
   set_err(S, code);
   return false;
+}
+
+// Byte offset of P^T[key][half] (8 heads = 16 B) in the P tile: rows of 32 B,
+// halves swapped every 4 keys so ldmatrix reads of 8 keys hit 8 bank groups.
+__device__ __forceinline__ uint32_t p_off(int key, int half) {
+  return key * 32 + ((half ^ ((key >> 2) & 1)) << 4);
 }
 
 __global__ void __launch_bounds__(NT, 1)
@@ -106,38 +142,42 @@ __global__ void __launch_bounds__(NT, 1)
   const int64_t t_first = u0 / upt;
   const int64_t t_last = (u1 - 1) / upt;
   const int64_t kb_first = u0 - t_first * upt;
+  if (tid == 0) SA_TRACE_CTA(0);
+  // let the combine kernel of split rows launch now; it waits for this grid
+  // to complete before reading any partial (griddepcontrol.wait)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (tid == 0) {
     for (int s = 0; s < NSLOT; ++s) {
-      mbar_init(smem_u32(&S.full[s]), 128 + 1);
-      mbar_init(smem_u32(&S.empty[s]), 1);
+      mbar_init(smem_u32(&S.full[s]), 64 + 1);
+      mbar_init(smem_u32(&S.empty[s]), 4);
     }
     mbar_init(smem_u32(&S.q_full), 1);
     mbar_init(smem_u32(&S.q_empty), 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&S.s_full[b]), 1);
-      mbar_init(smem_u32(&S.p_full[b]), 4);
+      mbar_init(smem_u32(&S.s_free[b]), 4);
     }
     S.err = 0;
     fence_mbar_init();
   }
-  if (warp == 8) {
+  if (warp == 2) {
     tmem_alloc<kTmemCols>(smem_u32(&S.tmem_base));
     tmem_relinquish();
   }
-  if (warp == 9 && lane == 0) tma_prefetch_desc(&q_map);
+  if (warp == 3 && lane == 0) tma_prefetch_desc(&q_map);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = S.tmem_base;
 
-  if (warp < 4) {
+  if (warp < 2) {
     // ------------------------------------------------------------ KV producer
-    // 128 threads; thread pt copies 16-byte chunk c = pt & 63 of the 32 rows
-    // with parity pt >> 6, so every warp-wide cp.async reads 512 contiguous
-    // bytes of one row.  The rows land in the 128-byte-swizzled slab layout.
+    // 64 threads; thread c copies 16-byte chunk c of all 64 rows, so every
+    // warp-wide cp.async reads 512 contiguous bytes of one row.  The rows land
+    // in the 128-byte-swizzled slab layout.
     const uint64_t pol = l2_policy_evict_first();
-    const int pt = tid, c = pt & 63, par = pt >> 6, j = c >> 3, cc = c & 7;
+    const int c = tid, j = c >> 3, cc = c & 7;
     int64_t t = t_first, kb = kb_first;
     int64_t tb = t / p.m, tm = t - tb * p.m;
     auto load_ids = [&](int64_t kb_, int64_t tb_, int64_t tm_, int32_t& a, int32_t& b) {
@@ -165,6 +205,7 @@ __global__ void __launch_bounds__(NT, 1)
       const int slot = i % NSLOT;
       const bool ok = i < NSLOT || wait_or_err(S, S.empty[slot], ((i / NSLOT) - 1) & 1, 1);
       if (!__all_sync(0xffffffffu, ok)) continue;
+      if (tid == 0) SA_TRACE_EV(i, 0);
       if (warp == 0) {
         const uint32_t ma = __ballot_sync(0xffffffffu, ia >= 0 && (int64_t)ia < p.kv_len);
         const uint32_t mb = __ballot_sync(0xffffffffu, ib >= 0 && (int64_t)ib < p.kv_len);
@@ -175,88 +216,76 @@ __global__ void __launch_bounds__(NT, 1)
       }
       const __nv_bfloat16* kvb = p.kv + cur_tb * p.kv_sb + c * 8;
       const uint32_t dst0 = smem_u32(S.ring[slot]) + j * SLAB_BYTES;
-      const int32_t mine = par ? ib : ia;
 #pragma unroll 8
       for (int k = 0; k < UK / 2; ++k) {
-        const int r = par + 2 * k;
-        const int32_t id = __shfl_sync(0xffffffffu, mine, k);
-        const bool v = id >= 0 && (int64_t)id < p.kv_len;
+        const int32_t ida = __shfl_sync(0xffffffffu, ia, k);  // row 2k
+        const int32_t idb = __shfl_sync(0xffffffffu, ib, k);  // row 2k+1
+        const bool va = ida >= 0 && (int64_t)ida < p.kv_len;
+        const bool vb = idb >= 0 && (int64_t)idb < p.kv_len;
+        const int r = 2 * k;
         cp_async16_hint(dst0 + r * 128 + ((cc ^ (r & 7)) << 4),
-                        kvb + (v ? (int64_t)id : 0) * p.kv_sn, v ? 16 : 0, pol);
+                        kvb + (va ? (int64_t)ida : 0) * p.kv_sn, va ? 16 : 0, pol);
+        cp_async16_hint(dst0 + (r + 1) * 128 + ((cc ^ ((r + 1) & 7)) << 4),
+                        kvb + (vb ? (int64_t)idb : 0) * p.kv_sn, vb ? 16 : 0, pol);
       }
-      // the slot's full barrier counts 128 hardware arrivals (one per thread,
+      // the slot's full barrier counts 64 hardware arrivals (one per thread,
       // when its copies land) plus the mask writer's release arrival
       cp_async_mbar_arrive_noinc(smem_u32(&S.full[slot]));
       if (warp == 0 && lane == 0) mbar_arrive(smem_u32(&S.full[slot]));
     }
     cp_async_wait<0>();
-  } else if (warp == 8) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ S^T issuer
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(64, 16, false, false);
-      constexpr uint32_t idO = idesc_bf16(128, 16, true, true);
       const uint32_t q_base = smem_u32(S.q);
       int64_t kb = kb_first;
       int seg = 0;
-      bool seg_first = true;      // unit i is the first of its segment
-      bool prev_seg_first = true; // unit i-1 was the first of its segment
-      auto issue_pv = [&](int j, bool first) {
-        if (!wait_or_err(S, S.p_full[j & 1], (j >> 1) & 1, 2)) return;
-        tc_fence_after();
-        const uint32_t slot_base = smem_u32(S.ring[j % NSLOT]);
-        const uint32_t pb = smem_u32(S.p[j & 1]);
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad =
-                smem_desc(slot_base + 2 * c * SLAB_BYTES + kk * 2048, SLAB_BYTES, 1024,
-                          kLayoutSw128);
-            const uint64_t bd = smem_desc(pb + kk * 512, 256, 128, kLayoutNone);
-            mma_f16_ss(tmem + kTmemO + 16 * c, ad, bd, idO, !(first && kk == 0));
-          }
-        mma_commit(smem_u32(&S.empty[j % NSLOT]));
-      };
+      bool seg_first = true;
       for (int i = 0; i < n; ++i) {
         const bool seg_end = (i == n - 1) || kb == upt - 1;
-        // at a row boundary finish the previous row first: its epilogue must
-        // not wait for the next row's Q
-        if (i > 0 && seg_first) issue_pv(i - 1, prev_seg_first);
         const int slot = i % NSLOT;
         bool ok = !seg_first || wait_or_err(S, S.q_full, seg & 1, 3);
         ok = ok && wait_or_err(S, S.full[slot], (i / NSLOT) & 1, 4);
+        // TMEM buffer i&1 was last read by the softmax of unit i-2
+        ok = ok && (i < 2 || wait_or_err(S, S.s_free[i & 1], ((i - 2) >> 1) & 1, 5));
         if (ok) {
+          SA_TRACE_EV(i, 1);
           fence_proxy_async_smem();  // cp.async (generic proxy) writes -> MMA reads
           tc_fence_after();
           const uint32_t slot_base = smem_u32(S.ring[slot]);
+          const uint32_t d = tmem + 16 * kSAcc * (i & 1);
+          // partial a accumulates slabs 2a and 2a+1; consecutive MMAs target
+          // different partials so none waits for the previous one
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
+          for (int j2 = 0; j2 < 8 / kSAcc; ++j2)
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad =
-                  smem_desc(slot_base + j * SLAB_BYTES + kk * 32, 16, 1024, kLayoutSw128);
-              const uint64_t bd =
-                  smem_desc(q_base + j * 2048 + kk * 32, 16, 1024, kLayoutSw128);
-              mma_f16_ss(tmem + kTmemS + 16 * (i & 1), ad, bd, idS, (j | kk) != 0);
-            }
+            for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+              for (int a = 0; a < kSAcc; ++a) {
+                const int sl = (8 / kSAcc) * a + j2;
+                const uint64_t ad =
+                    smem_desc(slot_base + sl * SLAB_BYTES + kk * 32, 16, 1024, kLayoutSw128);
+                const uint64_t bd =
+                    smem_desc(q_base + sl * 2048 + kk * 32, 16, 1024, kLayoutSw128);
+                mma_f16_ss(d + 16 * a, ad, bd, idS, (j2 | kk) != 0);
+              }
           mma_commit(smem_u32(&S.s_full[i & 1]));
           if (seg_end) mma_commit(smem_u32(&S.q_empty));
+          SA_TRACE_EV(i, 2);
         }
-        if (i > 0 && !seg_first) issue_pv(i - 1, prev_seg_first);
-        prev_seg_first = seg_first;
         seg_first = seg_end;
         if (seg_end) ++seg;
         kb = (kb + 1 == upt) ? 0 : kb + 1;
       }
-      issue_pv(n - 1, prev_seg_first);
     }
     __syncwarp();
-  } else if (warp == 9) {
+  } else if (warp == 3) {
     // ------------------------------------------------------------ Q producer
     if (lane == 0) {
       for (int64_t t = t_first; t <= t_last; ++t) {
         const int s = static_cast<int>(t - t_first);
-        if (s > 0 && !wait_or_err(S, S.q_empty, (s - 1) & 1, 5)) continue;
+        if (s > 0 && !wait_or_err(S, S.q_empty, (s - 1) & 1, 6)) continue;
         const int64_t tb = t / p.m, tm = t - tb * p.m;
         mbar_arrive_expect_tx(smem_u32(&S.q_full), Q_BYTES);
 #pragma unroll
@@ -267,11 +296,14 @@ __global__ void __launch_bounds__(NT, 1)
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------- softmax + epilogue
-    const int qd = warp - 4;            // TMEM lane quarter
-    const int key = 16 * qd + lane;     // key of this thread (lane < 16)
+    // ------------------------------------------- softmax + P.V + epilogue
+    const int qd = warp - 4;         // TMEM lane quarter = key group = column quarter
+    const int key = 16 * qd + lane;  // key of this thread for the softmax (lane < 16)
+    const int g8 = lane >> 2, q4 = lane & 3;  // mma.sync fragment coordinates
     const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
+    const uint32_t pbase = smem_u32(S.p);
     float m_run[kHeads], l_part[kHeads];
+    float o[16][4];  // O[heads g8, g8+8][128*qd + 8*nt + 2*q4 + {0,1}]
     int64_t t = t_first, kb = kb_first, seg_kb0 = kb_first;
     bool seg_first = true;
     for (int i = 0; i < n; ++i) {
@@ -282,15 +314,36 @@ __global__ void __launch_bounds__(NT, 1)
           m_run[h] = -INFINITY;
           l_part[h] = 0.f;
         }
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
         seg_kb0 = kb;
       }
       const int slot = i % NSLOT;
-      wait_or_err(S, S.full[slot], (i / NSLOT) & 1, 6);
-      wait_or_err(S, S.s_full[i & 1], (i >> 1) & 1, 7);
+      wait_or_err(S, S.full[slot], (i / NSLOT) & 1, 7);
+      wait_or_err(S, S.s_full[i & 1], (i >> 1) & 1, 8);
+      if (qd == 0 && lane == 0) SA_TRACE_EV(i, 3);
       tc_fence_after();
       float x[kHeads];
-      tmem_ld16(tmem + lane_off + kTmemS + 16 * (i & 1), x);
-      tmem_wait_ld();
+      {
+        float y[kHeads];
+        const uint32_t sb = tmem + lane_off + 16 * kSAcc * (i & 1);
+        tmem_ld16(sb, x);
+        tmem_ld16(sb + 16, y);
+        tmem_wait_ld();
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h) x[h] += y[h];
+#pragma unroll 1
+        for (int a = 2; a < kSAcc; ++a) {
+          tmem_ld16(sb + 16 * a, y);
+          tmem_wait_ld();
+#pragma unroll
+          for (int h = 0; h < kHeads; ++h) x[h] += y[h];
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&S.s_free[i & 1]));
+
       const uint32_t mw = S.mask[slot][lane & 1];
       const bool valid = lane < 16 && ((mw >> (key >> 1)) & 1u);
       bool over = false;
@@ -299,50 +352,39 @@ __global__ void __launch_bounds__(NT, 1)
         x[h] = valid ? x[h] * p.scale_log2 : -INFINITY;
         over |= x[h] > m_run[h] + kRescaleThreshold;
       }
+      // The vote barrier also orders this unit's P^T writes after every
+      // warp's P.V of the previous unit (single P tile).
       if (named_bar_or(1, 128, over)) {
-        // raise the running max to the block max (rare after the first unit)
-        float bm[kHeads];
+        // raise the running max to the block max (rare after a row's first unit)
 #pragma unroll
         for (int h = 0; h < kHeads; ++h) {
           float v = x[h];
 #pragma unroll
           for (int off = 16; off >= 1; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
-          bm[h] = v;
+          if (lane == 0) S.red_max[qd][h] = v;
         }
-        if (lane == 0)
-#pragma unroll
-          for (int h = 0; h < kHeads; ++h) S.red_max[qd][h] = bm[h];
         named_bar(2, 128);
-        float corr[kHeads];
-        bool any_corr = false;
+        float c_lo = 1.f, c_hi = 1.f;
 #pragma unroll
         for (int h = 0; h < kHeads; ++h) {
           const float b4 = fmaxf(fmaxf(S.red_max[0][h], S.red_max[1][h]),
                                  fmaxf(S.red_max[2][h], S.red_max[3][h]));
           const float m_new = fmaxf(m_run[h], b4);
-          corr[h] = (m_new == m_run[h]) ? 1.f : exp2f(m_run[h] - m_new);
-          any_corr |= corr[h] != 1.f;
+          const float corr = (m_new == m_run[h]) ? 1.f : exp2f(m_run[h] - m_new);
           m_run[h] = m_new;
-          l_part[h] *= corr[h];
+          l_part[h] *= corr;
+          if (h == g8) c_lo = corr;
+          if (h == g8 + 8) c_hi = corr;
         }
-        if (!seg_first && any_corr) {
-          // O^T holds units up to i-1 of this segment: wait for its last PV
-          const int j = i - 1;
-          wait_or_err(S, S.empty[j % NSLOT], (j / NSLOT) & 1, 8);
-          tc_fence_after();
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            float v[16];
-            tmem_ld16(tmem + lane_off + kTmemO + 16 * c, v);
-            tmem_wait_ld();
 #pragma unroll
-            for (int h = 0; h < kHeads; ++h) v[h] *= corr[h];
-            tmem_st16(tmem + lane_off + kTmemO + 16 * c, v);
-          }
-          tmem_wait_st();
+        for (int nt = 0; nt < 16; ++nt) {
+          o[nt][0] *= c_lo;
+          o[nt][1] *= c_lo;
+          o[nt][2] *= c_hi;
+          o[nt][3] *= c_hi;
         }
       }
-      // P^T for this thread's key: bf16 [key][head] in 8x16-byte core matrices
+      // P^T row of this thread's key (bf16), l partial sums
       float pr[kHeads];
 #pragma unroll
       for (int h = 0; h < kHeads; ++h) {
@@ -360,73 +402,91 @@ __global__ void __launch_bounds__(NT, 1)
         hi.y = pack_bf16x2(pr[10], pr[11]);
         hi.z = pack_bf16x2(pr[12], pr[13]);
         hi.w = pack_bf16x2(pr[14], pr[15]);
-        uint8_t* pb = S.p[i & 1] + (key >> 3) * 256 + (key & 7) * 16;
-        *reinterpret_cast<uint4*>(pb) = lo;
-        *reinterpret_cast<uint4*>(pb + 128) = hi;
+        *reinterpret_cast<uint4*>(S.p + p_off(key, 0)) = lo;
+        *reinterpret_cast<uint4*>(S.p + p_off(key, 1)) = hi;
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
+      named_bar(3, 128);  // P^T of all 64 keys written
+      if (qd == 0 && lane == 0) SA_TRACE_EV(i, 4);
+
+      // O[16 x 128 cols of this warp] += P[16 x 64] . V[64 x 128]
+      const uint32_t slot_base = smem_u32(S.ring[slot]);
+#pragma unroll
+      for (int kst = 0; kst < 4; ++kst) {
+        uint32_t pa[4];
+        {
+          const int mtx = lane >> 3;
+          const int kr = kst * 16 + (mtx >> 1) * 8 + (lane & 7);
+          ldmatrix_x4_trans(pa, pbase + p_off(kr, mtx & 1));
+        }
+        const int kr = kst * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {
+          const int slab = 2 * qd + (np >> 2);
+          const int ch = ((np & 3) << 1) + (lane >> 4);
+          uint32_t vb[4];
+          ldmatrix_x4_trans(vb, slot_base + slab * SLAB_BYTES + kr * 128 + ((ch ^ (kr & 7)) << 4));
+          mma_16816(o[2 * np], pa, vb[0], vb[1]);
+          mma_16816(o[2 * np + 1], pa, vb[2], vb[3]);
+        }
+      }
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&S.p_full[i & 1]));
+      if (lane == 0) mbar_arrive(smem_u32(&S.empty[slot]));  // slot free for the producer
+      if (qd == 0 && lane == 0) SA_TRACE_EV(i, 5);
 
       if (seg_end) {
         // ---------------- epilogue of the segment ending at unit i ----------
-        float lt[kHeads];
+        if (qd == 0 && lane == 0) SA_TRACE_EV(i, 6);
 #pragma unroll
         for (int h = 0; h < kHeads; ++h) {
           float v = l_part[h];
 #pragma unroll
           for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-          lt[h] = v;
+          if (lane == 0) S.red_l[qd][h] = v;
         }
-        if (lane == 0)
-#pragma unroll
-          for (int h = 0; h < kHeads; ++h) S.red_l[qd][h] = lt[h];
+        if (tid == 128) SA_TRACE_CTA(6);
         named_bar(2, 128);
+        if (tid == 128) SA_TRACE_CTA(7);
+        float m_lo = 0.f, m_hi = 0.f;
 #pragma unroll
-        for (int h = 0; h < kHeads; ++h)
-          lt[h] = (S.red_l[0][h] + S.red_l[1][h]) + (S.red_l[2][h] + S.red_l[3][h]);
-        wait_or_err(S, S.empty[slot], (i / NSLOT) & 1, 9);  // PV(i) done
-        tc_fence_after();
+        for (int h = 0; h < kHeads; ++h) {
+          if (h == g8) m_lo = m_run[h];
+          if (h == g8 + 8) m_hi = m_run[h];
+        }
+        const float l_lo = (S.red_l[0][g8] + S.red_l[1][g8]) + (S.red_l[2][g8] + S.red_l[3][g8]);
+        const float l_hi = (S.red_l[0][g8 + 8] + S.red_l[1][g8 + 8]) +
+                           (S.red_l[2][g8 + 8] + S.red_l[3][g8 + 8]);
         const int64_t tb = t / p.m, tm = t - tb * p.m;
-        const bool whole = (seg_kb0 == 0) && (kb == upt - 1);
-        if (whole) {
-          float f[kHeads];
-#pragma unroll
-          for (int h = 0; h < kHeads; ++h)
-            f[h] = sink_factor(m_run[h], lt[h], __ldg(p.sink + h) * kLog2e);
+        if (seg_kb0 == 0 && kb == upt - 1) {
+          const float f_lo = sink_factor(m_lo, l_lo, __ldg(p.sink + g8) * kLog2e);
+          const float f_hi = sink_factor(m_hi, l_hi, __ldg(p.sink + g8 + 8) * kLog2e);
           __nv_bfloat16* ob = p.o + tb * p.o_sb + tm * p.o_sm;
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            float v[16];
-            tmem_ld16(tmem + lane_off + kTmemO + 16 * c, v);
-            tmem_wait_ld();
-            const int d = 128 * c + 32 * qd + lane;
 #pragma unroll
-            for (int h = 0; h < kHeads; ++h) ob[h * p.o_sh + d] = __float2bfloat16_rn(v[h] * f[h]);
+          for (int nt = 0; nt < 16; ++nt) {
+            const int d = 128 * qd + 8 * nt + 2 * q4;
+            *reinterpret_cast<uint32_t*>(ob + g8 * p.o_sh + d) =
+                pack_bf16x2(o[nt][0] * f_lo, o[nt][1] * f_lo);
+            *reinterpret_cast<uint32_t*>(ob + (g8 + 8) * p.o_sh + d) =
+                pack_bf16x2(o[nt][2] * f_hi, o[nt][3] * f_hi);
           }
         } else {
+          if (tid == 128) SA_TRACE_CTA(2);
           const int64_t pslot = 2 * g + (t == t_first ? 0 : 1);
           float* pacc = p.part_acc + pslot * kPartAccFloats;
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            float v[16];
-            tmem_ld16(tmem + lane_off + kTmemO + 16 * c, v);
-            tmem_wait_ld();
-            const int d = 128 * c + 32 * qd + lane;
 #pragma unroll
-            for (int h = 0; h < kHeads; ++h) pacc[h * kDim + d] = v[h];
+          for (int nt = 0; nt < 16; ++nt) {
+            const int d = 128 * qd + 8 * nt + 2 * q4;
+            *reinterpret_cast<float2*>(pacc + g8 * kDim + d) = make_float2(o[nt][0], o[nt][1]);
+            *reinterpret_cast<float2*>(pacc + (g8 + 8) * kDim + d) =
+                make_float2(o[nt][2], o[nt][3]);
           }
-          if (qd == 0 && lane == 0) {
-#pragma unroll
-            for (int h = 0; h < kHeads; ++h) {
-              p.part_ml[pslot * kPartMlFloats + h] = m_run[h];
-              p.part_ml[pslot * kPartMlFloats + kHeads + h] = lt[h];
-            }
+          if (qd == 0 && q4 == 0) {
+            p.part_ml[pslot * kPartMlFloats + g8] = m_lo;
+            p.part_ml[pslot * kPartMlFloats + g8 + 8] = m_hi;
+            p.part_ml[pslot * kPartMlFloats + kHeads + g8] = l_lo;
+            p.part_ml[pslot * kPartMlFloats + kHeads + g8 + 8] = l_hi;
           }
         }
-        tc_fence_before();
-        named_bar(2, 128);  // O^T fully read before the next segment's first PV
+        if (qd == 0 && lane == 0) SA_TRACE_EV(i, 7);
       }
       seg_first = seg_end;
       if (++kb == upt) {
@@ -439,10 +499,11 @@ __global__ void __launch_bounds__(NT, 1)
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == 2) {
     tc_fence_after();
     tmem_dealloc<kTmemCols>(tmem);
   }
+  if (tid == 0) SA_TRACE_CTA(1);
 }
 
 }  // namespace tc_path
@@ -504,6 +565,21 @@ cudaError_t launch_tc(const Params& p, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   return launch_combine(p, st);
 }
+
+#ifdef SA_TRACE
+extern "C" int sa_trace_read(unsigned long long* out, size_t bytes) {
+  if (bytes < sizeof(sa_trace)) return -1;
+  return (int)cudaMemcpyFromSymbol(out, sa_trace, sizeof(sa_trace));
+}
+extern "C" int sa_trace_cta_read(unsigned long long* out, size_t bytes) {
+  if (bytes < sizeof(sa_trace_cta)) return -1;
+  return (int)cudaMemcpyFromSymbol(out, sa_trace_cta, sizeof(sa_trace_cta));
+}
+extern "C" int sa_trace_clear() {
+  static unsigned long long zero[kTraceCtas * kTraceUnits * kTraceEvents] = {};
+  return (int)cudaMemcpyToSymbol(sa_trace, zero, sizeof(zero));
+}
+#endif
 
 int read_tc_error(int* flags) {
   int v = 0;
