@@ -52,7 +52,7 @@ __device__ int sa_tc_error;  // nonzero after a bounded wait gave up
 #ifdef SA_TRACE
 // Pipeline timeline for development builds only (-DSA_TRACE): per CTA (first
 // kTraceCtas), per unit (first kTraceUnits), per event, %globaltimer in ns.
-constexpr int kTraceCtas = 4, kTraceUnits = 32, kTraceEvents = 8;
+constexpr int kTraceCtas = 160, kTraceUnits = 16, kTraceEvents = 8;
 __device__ unsigned long long sa_trace[kTraceCtas][kTraceUnits][kTraceEvents];
 __device__ __forceinline__ void trace_ev(int64_t cta, int unit, int ev) {
   if (cta < kTraceCtas && unit < kTraceUnits) {
@@ -63,6 +63,7 @@ __device__ __forceinline__ void trace_ev(int64_t cta, int unit, int ev) {
 }
 #define SA_TRACE_EV(u, e) trace_ev(blockIdx.x, (u), (e))
 __device__ unsigned long long sa_trace_cta[1024][8];  // start, end, epilogue stages
+
 __device__ __forceinline__ void trace_cta(int e) {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -94,7 +95,6 @@ struct __align__(1024) Smem {
   uint8_t p[P_BYTES];
   uint32_t mask[NSLOT][2];  // validity: [0] keys 2l, [1] keys 2l+1 (bit l)
   float red_max[4][kHeads];
-  float red_l[4][kHeads];
   // full: rows landed (128 cp.async arrivals + mask writer); empty: the four
   // softmax warps finished P.V on the slot; s_full: S^T(i) in TMEM; s_free:
   // the softmax warps read S^T out of TMEM buffer i&1
@@ -302,20 +302,20 @@ __global__ void __launch_bounds__(NT, 1)
     const int g8 = lane >> 2, q4 = lane & 3;  // mma.sync fragment coordinates
     const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
     const uint32_t pbase = smem_u32(S.p);
-    float m_run[kHeads], l_part[kHeads];
+    float m_run[kHeads];
     float o[16][4];  // O[heads g8, g8+8][128*qd + 8*nt + 2*q4 + {0,1}]
+    float lacc[4];   // running sums: [0],[1] head g8, [2],[3] head g8+8 (P . 1)
+    const uint32_t kOnes = 0x3F803F80u;  // bf16 pair (1, 1)
     int64_t t = t_first, kb = kb_first, seg_kb0 = kb_first;
     bool seg_first = true;
     for (int i = 0; i < n; ++i) {
       const bool seg_end = (i == n - 1) || kb == upt - 1;
       if (seg_first) {
 #pragma unroll
-        for (int h = 0; h < kHeads; ++h) {
-          m_run[h] = -INFINITY;
-          l_part[h] = 0.f;
-        }
+        for (int h = 0; h < kHeads; ++h) m_run[h] = -INFINITY;
 #pragma unroll
         for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+        lacc[0] = lacc[1] = lacc[2] = lacc[3] = 0.f;
         seg_kb0 = kb;
       }
       const int slot = i % NSLOT;
@@ -372,7 +372,6 @@ __global__ void __launch_bounds__(NT, 1)
           const float m_new = fmaxf(m_run[h], b4);
           const float corr = (m_new == m_run[h]) ? 1.f : exp2f(m_run[h] - m_new);
           m_run[h] = m_new;
-          l_part[h] *= corr;
           if (h == g8) c_lo = corr;
           if (h == g8 + 8) c_hi = corr;
         }
@@ -383,14 +382,17 @@ __global__ void __launch_bounds__(NT, 1)
           o[nt][2] *= c_hi;
           o[nt][3] *= c_hi;
         }
+        lacc[0] *= c_lo;
+        lacc[1] *= c_lo;
+        lacc[2] *= c_hi;
+        lacc[3] *= c_hi;
       }
-      // P^T row of this thread's key (bf16), l partial sums
+      // P^T row of this thread's key (bf16)
       float pr[kHeads];
 #pragma unroll
       for (int h = 0; h < kHeads; ++h) {
         const float base = (m_run[h] == -INFINITY) ? 0.f : m_run[h];
         pr[h] = exp2f(x[h] - base);
-        l_part[h] += pr[h];
       }
       if (lane < 16) {
         uint4 lo, hi;
@@ -418,6 +420,7 @@ __global__ void __launch_bounds__(NT, 1)
           const int kr = kst * 16 + (mtx >> 1) * 8 + (lane & 7);
           ldmatrix_x4_trans(pa, pbase + p_off(kr, mtx & 1));
         }
+        mma_16816(lacc, pa, kOnes, kOnes);  // row sums of the bf16 P actually used
         const int kr = kst * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
         for (int np = 0; np < 8; ++np) {
@@ -431,30 +434,26 @@ __global__ void __launch_bounds__(NT, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&S.empty[slot]));  // slot free for the producer
+#ifdef SA_TRACE
+      {  // development builds: wait for the P.V results before stamping
+        float dep = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) dep += o[nt][0] + o[nt][3];
+        if (dep == 1.2345e-30f) sa_trace[0][0][0] = 1;
+      }
+#endif
       if (qd == 0 && lane == 0) SA_TRACE_EV(i, 5);
 
       if (seg_end) {
         // ---------------- epilogue of the segment ending at unit i ----------
         if (qd == 0 && lane == 0) SA_TRACE_EV(i, 6);
-#pragma unroll
-        for (int h = 0; h < kHeads; ++h) {
-          float v = l_part[h];
-#pragma unroll
-          for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-          if (lane == 0) S.red_l[qd][h] = v;
-        }
-        if (tid == 128) SA_TRACE_CTA(6);
-        named_bar(2, 128);
-        if (tid == 128) SA_TRACE_CTA(7);
         float m_lo = 0.f, m_hi = 0.f;
 #pragma unroll
         for (int h = 0; h < kHeads; ++h) {
           if (h == g8) m_lo = m_run[h];
           if (h == g8 + 8) m_hi = m_run[h];
         }
-        const float l_lo = (S.red_l[0][g8] + S.red_l[1][g8]) + (S.red_l[2][g8] + S.red_l[3][g8]);
-        const float l_hi = (S.red_l[0][g8 + 8] + S.red_l[1][g8 + 8]) +
-                           (S.red_l[2][g8 + 8] + S.red_l[3][g8 + 8]);
+        const float l_lo = lacc[0], l_hi = lacc[2];
         const int64_t tb = t / p.m, tm = t - tb * p.m;
         if (seg_kb0 == 0 && kb == upt - 1) {
           const float f_lo = sink_factor(m_lo, l_lo, __ldg(p.sink + g8) * kLog2e);
