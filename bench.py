@@ -162,19 +162,30 @@ def device_inputs(cfg, seed, device):
     return q, kv, sink, idx
 
 
-def count_our_launches(fn):
-    """Kernels of libsparse_attn launched by one call of ``fn`` (profiled once,
-    outside every timed region)."""
+def profile_our_kernels(fn, flush, reps=5):
+    """Our kernels launched per call of ``fn`` and their mean device duration,
+    from a CUPTI trace of ``reps`` L2-flushed calls made outside every timed
+    region.  Returns (launches per call, {kernel: mean us}) or (None, {error})."""
     try:
         from torch.profiler import ProfilerActivity, profile
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            fn()
+            for _ in range(reps):
+                flush.zero_()
+                fn()
             torch.cuda.synchronize()
-        names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
-        ours = [n for n in names if "sa_" in n and ("fwd_kernel" in n or "combine" in n)]
-        return len(ours), sorted(set(ours))
+        per, n = {}, 0
+        for e in prof.events():
+            if e.device_type.name != "CUDA":
+                continue
+            name = e.name
+            if "sa_" in name and ("fwd_kernel" in name or "combine" in name):
+                short = name.split("(")[0].split("::")[-1]
+                per.setdefault(short, []).append(e.device_time_total if hasattr(
+                    e, "device_time_total") else e.cuda_time_total)
+                n += 1
+        return n // reps, {k: statistics.mean(v) for k, v in per.items()}
     except Exception as e:  # profiler unavailable: report unknown
-        return None, [f"profiler failed: {e}"]
+        return None, {"profiler failed": str(e)}
 
 
 # ----------------------------------------------------------------------------
@@ -275,7 +286,7 @@ def main():
         flush.zero_()
         step()
     torch.cuda.synchronize()
-    per_call, kernel_names = (None, []) if args.no_launch_count else count_our_launches(step)
+    per_call, kernel_us = (None, {}) if args.no_launch_count else profile_our_kernels(step, flush)
 
     def barrier():
         if world > 1:
@@ -384,7 +395,7 @@ def main():
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": None if per_call is None else per_call * K,
-        "kernels": kernel_names,
+        "kernel_us": kernel_us,
         "step_ms": {"mean": mean_ms, "min": min(step_ms), "median": statistics.median(step_ms)},
         "clocks": clocks,
     }

@@ -282,18 +282,19 @@ __global__ void __launch_bounds__(NT, 1) sa_mma_fwd_kernel(const Params p) {
 
 // ----------------------------------------------------------------------------
 // LSE combine of split rows (shared by every variant).
-// Block (g, hg): if CTA g ends a row that started in an earlier CTA ("owns"
-// it), merge the fp32 partials of CTAs f..g of that row for heads
-// 4hg..4hg+3, with the sink as the extra logit (reference.py:34-38); partial
-// slots follow the rule in sa_common.cuh.  Thread: one head, 8 columns.  All
-// partial loads of a thread are issued together (two memory round trips for
-// up to kCombineBatch partials).  Launched as a programmatic dependent of the
-// forward kernel: griddepcontrol.wait returns once that grid has completed
-// and its stores are visible.
+// Block (g, h): if CTA g ends a row that started in an earlier CTA ("owns"
+// it), merge the fp32 partials of CTAs f..g of that row for head h, with the
+// sink as the extra logit (reference.py:34-38); partial slots follow the rule
+// in sa_common.cuh.  64 threads x 8 columns.  All partial loads of a thread
+// are issued together (two memory round trips for up to kCombineBatch
+// partials).  Launched as a programmatic dependent of the forward kernel:
+// blocks are small (64 threads, no shared memory, <= 112 registers) so they
+// can become resident beside a running forward CTA, and griddepcontrol.wait
+// returns once the forward grid has completed and its stores are visible.
 // ----------------------------------------------------------------------------
 constexpr int kCombineBatch = 8;
 
-__global__ void __launch_bounds__(256) sa_combine_kernel(const Params p) {
+__global__ void __launch_bounds__(64) sa_combine_kernel(const Params p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int64_t G = p.grid, g = blockIdx.x, U = p.units, upt = p.upt;
   const int64_t u0 = unit_begin(g, U, G), u1 = unit_begin(g + 1, U, G);
@@ -305,8 +306,8 @@ __global__ void __launch_bounds__(256) sa_combine_kernel(const Params p) {
   const int np = static_cast<int>(g - f + 1);
   auto slot_of = [&](int k) -> int64_t { return (k == 0 && f_mid) ? 2 * f + 1 : 2 * (f + k); };
 
-  const int h = 4 * blockIdx.y + (threadIdx.x >> 6);
-  const int d0 = (threadIdx.x & 63) * 8;
+  const int h = blockIdx.y;
+  const int d0 = threadIdx.x * 8;
   const float sink_l2 = __ldg(p.sink + h) * kLog2e;
   float acc[8];
 #pragma unroll
@@ -371,10 +372,13 @@ bool any_split(const Params& p) {
 }
 
 cudaError_t launch_combine(const Params& p, cudaStream_t st) {
+#ifdef SA_NO_COMBINE  // development builds only: time the forward kernel alone
+  return cudaSuccess;
+#endif
   if (!any_split(p)) return cudaSuccess;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(p.grid), kHeads / 4, 1);
-  cfg.blockDim = dim3(256, 1, 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(p.grid), kHeads, 1);
+  cfg.blockDim = dim3(64, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

@@ -6,10 +6,13 @@ shared object is missing or cannot be loaded, :func:`lib` raises.
 from __future__ import annotations
 
 import ctypes
+import os
 import pathlib
 import threading
 
-LIB_PATH = pathlib.Path(__file__).resolve().parent / "libsparse_attn.so"
+# SPARSE_ATTN_LIB overrides the library path (e.g. an instrumented build)
+LIB_PATH = pathlib.Path(os.environ.get("SPARSE_ATTN_LIB") or
+                        pathlib.Path(__file__).resolve().parent / "libsparse_attn.so")
 
 SA_OK = 0
 SA_ERR_INVALID_ARG = -1
