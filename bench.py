@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="decode")
-    ap.add_argument("--variant", choices=["auto", "mma", "tcgen05"], default="auto")
+    ap.add_argument("--variant", choices=["auto", "mma", "tcgen05", "ws"], default="auto")
     ap.add_argument("--grid", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the CPU baseline leg (profiling runs)")
@@ -266,7 +266,7 @@ def main():
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
-    variant = {"auto": 0, "mma": 1, "tcgen05": 2}[args.variant]
+    variant = {"auto": 0, "mma": 1, "tcgen05": 2, "ws": 3}[args.variant]
     cfg = CONFIGS[args.config]
     q, kv, sink, idx = device_inputs(cfg, seed=1000 + rank, device=dev)
     o = torch.empty_like(q)

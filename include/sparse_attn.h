@@ -45,10 +45,12 @@ extern "C" {
 #define SA_ERR_CUDA (-3)        /* CUDA runtime error (see last_cuda_error) */
 #define SA_ERR_UNSUPPORTED (-4) /* h != 16, d != 512, or no sm_100 device   */
 
-/* Kernel variants for sa_fwd_ex (SA_VARIANT_AUTO picks the fastest). */
+/* Kernel variants for sa_fwd_ex (SA_VARIANT_AUTO picks the fastest, WS). */
 #define SA_VARIANT_AUTO 0
-#define SA_VARIANT_MMA 1     /* warp mma.sync + cp.async gather            */
-#define SA_VARIANT_TCGEN05 2 /* tcgen05 MMA (TMEM accumulators) + TMA gather */
+#define SA_VARIANT_MMA 1     /* all-warp mma.sync, cp.async ring, __syncthreads     */
+#define SA_VARIANT_TCGEN05 2 /* S^T by tcgen05 (TMEM), P.V warp MMAs, mbarrier pipe */
+#define SA_VARIANT_WS 3      /* warp-specialized: cp.async + TMA(Q) producers,      */
+                             /* mma.sync consumers with Q in registers (default)    */
 
 /* Library ABI version (major * 10000 + minor * 100 + patch). */
 int sa_version(void);
@@ -62,7 +64,8 @@ const char* sa_strerror(int code);
 int sa_variant_available(int variant);
 
 /* Debug/health query, synchronous: copies into *flags the error word that the
- * tensor-core kernel sets on the current device when one of its bounded
+ * pipelined kernels (SA_VARIANT_TCGEN05, SA_VARIANT_WS; the latter reported
+ * as 100 + code) set on the current device when one of their bounded
  * pipeline waits gave up (0 = never).  Intended for tests and health checks,
  * not the hot path.  No counterpart in the reference. */
 int sa_device_status(int* flags);

@@ -20,6 +20,9 @@ int tc_ctas_per_sm();
 bool tc_available();
 bool tc_supports(const Params& p);
 int read_tc_error(int* flags);
+cudaError_t launch_ws(const Params& p, cudaStream_t st);
+int ws_unit_keys();
+int read_ws_error(int* flags);
 }  // namespace sa
 
 namespace {
@@ -88,8 +91,11 @@ int sa_last_cuda_error(void) { return t_last_cuda_error; }
 
 int sa_device_status(int* flags) {
   if (flags == nullptr) return SA_ERR_INVALID_ARG;
-  const int e = sa::read_tc_error(flags);
+  int a = 0, b = 0;
+  int e = sa::read_tc_error(&a);
+  if (e == 0) e = sa::read_ws_error(&b);
   if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
+  *flags = a != 0 ? a : (b != 0 ? 100 + b : 0);
   return SA_OK;
 }
 
@@ -99,6 +105,7 @@ int sa_variant_available(int variant) {
     case SA_VARIANT_MMA:
       return 1;
     case SA_VARIANT_TCGEN05:
+    case SA_VARIANT_WS:
       return sa::tc_available() ? 1 : 0;
     default:
       return 0;
@@ -176,7 +183,7 @@ int sa_fwd_ex(const void* q, const void* kv, const float* sink, const int32_t* i
   // variant: the tensor-core path whenever its TMA maps can describe the
   // inputs, the warp-MMA path otherwise
   if (variant == SA_VARIANT_AUTO)
-    variant = (sa::tc_available() && sa::tc_supports(p)) ? SA_VARIANT_TCGEN05 : SA_VARIANT_MMA;
+    variant = (sa::tc_available() && sa::tc_supports(p)) ? SA_VARIANT_WS : SA_VARIANT_MMA;
   int unit_keys, ctas_per_sm;
   if (variant == SA_VARIANT_MMA) {
     unit_keys = sa::mma_unit_keys();
@@ -185,6 +192,10 @@ int sa_fwd_ex(const void* q, const void* kv, const float* sink, const int32_t* i
     if (!sa::tc_available() || !sa::tc_supports(p)) return SA_ERR_UNSUPPORTED;
     unit_keys = sa::tc_unit_keys();
     ctas_per_sm = sa::tc_ctas_per_sm();
+  } else if (variant == SA_VARIANT_WS) {
+    if (!sa::tc_supports(p)) return SA_ERR_UNSUPPORTED;
+    unit_keys = sa::ws_unit_keys();
+    ctas_per_sm = 1;
   } else {
     return SA_ERR_INVALID_ARG;
   }
@@ -204,7 +215,9 @@ int sa_fwd_ex(const void* q, const void* kv, const float* sink, const int32_t* i
   p.part_ml = reinterpret_cast<float*>(ws + sa::ws_acc_bytes(p.grid));
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  e = (variant == SA_VARIANT_MMA) ? sa::launch_mma(p, st) : sa::launch_tc(p, st);
+  e = (variant == SA_VARIANT_MMA)       ? sa::launch_mma(p, st)
+      : (variant == SA_VARIANT_TCGEN05) ? sa::launch_tc(p, st)
+                                        : sa::launch_ws(p, st);
   if (e != cudaSuccess) return fail_cuda(e);
   return SA_OK;
 }

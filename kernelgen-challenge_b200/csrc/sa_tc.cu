@@ -539,21 +539,28 @@ bool tc_supports(const Params& p) {
   return (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0;
 }
 
-cudaError_t launch_tc(const Params& p, cudaStream_t st) {
-  using namespace tc_path;
+// 4-D tensor map of q [b, m, 16, 512] (any row strides) with 64 x 16 boxes
+// in the 128-byte swizzle; shared by the kernels that load Q with TMA.
+cudaError_t encode_q_map(const Params& p, CUtensorMap* q_map) {
   auto enc = encoder();
   if (enc == nullptr) return cudaErrorNotSupported;
+  cuuint64_t dims[4] = {(cuuint64_t)kDim, (cuuint64_t)kHeads, (cuuint64_t)p.m, (cuuint64_t)p.b};
+  cuuint64_t strides[3] = {(cuuint64_t)p.q_sh * 2, (cuuint64_t)p.q_sm * 2, (cuuint64_t)p.q_sb * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)kHeads, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  if (enc(q_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<__nv_bfloat16*>(p.q), dims,
+          strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  return cudaSuccess;
+}
+
+cudaError_t launch_tc(const Params& p, cudaStream_t st) {
+  using namespace tc_path;
   CUtensorMap q_map;
   {
-    cuuint64_t dims[4] = {(cuuint64_t)kDim, (cuuint64_t)kHeads, (cuuint64_t)p.m, (cuuint64_t)p.b};
-    cuuint64_t strides[3] = {(cuuint64_t)p.q_sh * 2, (cuuint64_t)p.q_sm * 2,
-                             (cuuint64_t)p.q_sb * 2};
-    cuuint32_t box[4] = {64, (cuuint32_t)kHeads, 1, 1};
-    cuuint32_t es[4] = {1, 1, 1, 1};
-    if (enc(&q_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<__nv_bfloat16*>(p.q), dims,
-            strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return cudaErrorInvalidValue;
+    const cudaError_t eq = encode_q_map(p, &q_map);
+    if (eq != cudaSuccess) return eq;
   }
   cudaError_t e = cudaFuncSetAttribute(sa_tc_fwd_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,

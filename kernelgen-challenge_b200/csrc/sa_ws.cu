@@ -1,0 +1,430 @@
+// sa_ws.cu — warp-specialized persistent gather-attend kernel for sm_100a:
+// TMA + cp.async + mbarrier pipeline feeding four consumer warps that run
+// both products on the warp-level tensor-core instructions (mma.sync
+// m16n8k16).  This is the default variant.
+//
+// Algorithm: track-01/submission.py:276-347 (math of reference.py:24-40);
+// masking of submission.py:313-322; sink in the denominator only
+// (submission.py:340-345).  Work schedule and split/combine: sa_common.cuh.
+//
+// Why warp MMAs here: with 16 heads, one m16n8k16 exactly covers the heads,
+// while a tcgen05.mma needs M >= 64, so the heads must sit on N=16, where it
+// costs ~60 cycles per instruction (measured for any M in {64,128}, N <= 128).
+// Per 64-key unit that is ~2400 tensor cycles (S^T on tcgen05 + P.V) against
+// ~1000 for 512 m16n8k16 (S and P.V), and the single tcgen05 issuing thread
+// kept each ring slot busy ~3.9 us instead of ~1 us.  The gather, not the
+// math, bounds this op; a short slot hold keeps two or more units in flight.
+//
+// Per 64-key unit (64 KiB of gathered rows, 8 slabs of [64 keys x 64 cols]
+// in the 128-byte swizzle):
+//   S[16 x 64] = Q[16 x 512] . K^T   consumer warp c: keys 16c..16c+15
+//                                    (64 MMAs, Q fragments held in registers
+//                                    for the whole row)
+//   online softmax on the MMA fragments (running max raised only when a
+//   score exceeds it by more than 2^8: one barrier vote per unit)
+//   P -> shared memory (bf16, swizzled rows)
+//   O[16 x 128c..128c+127] += P . V  consumer warp c: slabs 2c, 2c+1 (64 MMAs)
+//   row sums l = P . 1               (4 MMAs, every warp, no reduction)
+//
+// Warp roles (224 threads, one CTA per SM):
+//   warps 0..1   KV producer (cp.async into a 3-deep ring of 64 KiB slots)
+//   warp 2       Q producer (one tiled TMA per 64 columns when a row starts;
+//                the consumers release the Q tile as soon as they hold its
+//                fragments, so the next row's Q load overlaps this row)
+//   warps 3..6   consumers c = 0..3
+//
+// Every mbarrier wait is bounded; on a timeout the CTA records an error code
+// in sa_ws_error (readable through sa_device_status) and stops issuing work.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "sa_tc.cuh"
+
+namespace sa {
+
+__device__ int sa_ws_error;  // nonzero after a bounded wait gave up
+
+namespace ws_path {
+using namespace tc;
+
+constexpr int UK = 64;                      // keys per unit
+constexpr int NSLOT = 3;                    // ring depth (units)
+constexpr int SLOT_BYTES = UK * kDim * 2;   // 64 KiB
+constexpr int SLAB_BYTES = UK * 128;        // [64 keys x 64 cols] = 8 KiB
+constexpr int Q_BYTES = kHeads * kDim * 2;  // 16 KiB
+constexpr int P_BYTES = kHeads * UK * 2;    // 2 KiB, P [head][key] bf16
+constexpr int NCW = 4;                      // consumer warps
+constexpr int NCT = NCW * 32;
+constexpr int NT = 3 * 32 + NCT;            // 224
+constexpr float kRescaleThreshold = 8.0f;   // log2 domain
+
+struct __align__(1024) Smem {
+  uint8_t ring[NSLOT][SLOT_BYTES];
+  uint8_t q[Q_BYTES];
+  uint8_t p[P_BYTES];
+  uint32_t mask[NSLOT][2];  // validity: [0] keys 2l, [1] keys 2l+1 (bit l)
+  float red_max[NCW][kHeads];
+  // full: rows landed (64 cp.async arrivals + mask writer); empty: the four
+  // consumer warps finished the unit; q_full / q_empty: the Q tile
+  uint64_t full[NSLOT], empty[NSLOT], q_full, q_empty;
+  int err;
+};
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + manual 1 KiB alignment
+
+__device__ __forceinline__ void set_err(Smem& S, int code) {
+  if (atomicCAS(&S.err, 0, code) == 0) atomicCAS(&sa_ws_error, 0, code);
+}
+
+// Bounded wait that also gives up at once when another warp recorded an error.
+// After an error every role keeps walking its loop (so all threads reach the
+// same named barriers) but issues no more copies.
+__device__ __forceinline__ bool wait_or_err(Smem& S, uint64_t& bar, uint32_t parity, int code) {
+  const uint32_t b = smem_u32(&bar);
+  if (*reinterpret_cast<volatile int*>(&S.err) != 0) return false;
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(b, parity)) return true;
+    if ((i & 1023u) == 1023u && *reinterpret_cast<volatile int*>(&S.err) != 0) return false;
+  }
+  set_err(S, code);
+  return false;
+}
+
+// Byte offset of the 16-byte chunk `ch` (keys 8ch..8ch+7) of P row `h`:
+// rows of 128 B with chunks XOR-swizzled by the row, so ldmatrix reads of 8
+// rows hit 8 different bank groups.
+__device__ __forceinline__ uint32_t p_chunk(int h, int ch) {
+  return h * 128 + ((ch ^ (h & 7)) << 4);
+}
+
+__global__ void __launch_bounds__(NT, 1)
+    sa_ws_fwd_kernel(const Params p, const __grid_constant__ CUtensorMap q_map) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& S = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                     ~static_cast<uintptr_t>(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t G = p.grid, g = blockIdx.x;
+  const int64_t u0 = unit_begin(g, p.units, G), u1 = unit_begin(g + 1, p.units, G);
+  const int n = static_cast<int>(u1 - u0);
+  if (n <= 0) return;
+  const int64_t upt = p.upt;
+  const int64_t t_first = u0 / upt;
+  const int64_t t_last = (u1 - 1) / upt;
+  const int64_t kb_first = u0 - t_first * upt;
+  // the combine kernel of split rows may launch now; it waits for this grid
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (tid == 0) {
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(smem_u32(&S.full[s]), 64 + 1);
+      mbar_init(smem_u32(&S.empty[s]), NCW);
+    }
+    mbar_init(smem_u32(&S.q_full), 1);
+    mbar_init(smem_u32(&S.q_empty), NCW);
+    S.err = 0;
+    fence_mbar_init();
+  }
+  if (warp == 2 && lane == 0) tma_prefetch_desc(&q_map);
+  __syncthreads();
+
+#define SA_TRACE_EV(u, e) ((void)0)
+  if (warp < 2) {
+    // ------------------------------------------------------------ KV producer
+    // 64 threads; thread c copies 16-byte chunk c of all 64 rows, so every
+    // warp-wide cp.async reads 512 contiguous bytes of one row.  The rows land
+    // in the 128-byte-swizzled slab layout.
+    const uint64_t pol = l2_policy_evict_first();
+    const int c = tid, j = c >> 3, cc = c & 7;
+    int64_t t = t_first, kb = kb_first;
+    int64_t tb = t / p.m, tm = t - tb * p.m;
+    auto load_ids = [&](int64_t kb_, int64_t tb_, int64_t tm_, int32_t& a, int32_t& b) {
+      const int64_t k0 = kb_ * UK + 2 * lane;
+      const int32_t* base = p.idx + tb_ * p.i_sb + tm_ * p.i_sm;
+      a = k0 < p.topk ? __ldg(base + k0 * p.i_sk) : -1;
+      b = k0 + 1 < p.topk ? __ldg(base + (k0 + 1) * p.i_sk) : -1;
+    };
+    int32_t na, nb;
+    load_ids(kb, tb, tm, na, nb);
+    for (int i = 0; i < n; ++i) {
+      const int32_t ia = na, ib = nb;
+      const int64_t cur_tb = tb;
+      // advance the cursor and prefetch the next unit's indices
+      if (++kb == upt) {
+        kb = 0;
+        ++t;
+        if (++tm == p.m) {
+          tm = 0;
+          ++tb;
+        }
+      }
+      if (i + 1 < n) load_ids(kb, tb, tm, na, nb);
+
+      const int slot = i % NSLOT;
+      const bool ok = i < NSLOT || wait_or_err(S, S.empty[slot], ((i / NSLOT) - 1) & 1, 1);
+      if (!__all_sync(0xffffffffu, ok)) continue;
+      if (tid == 0) SA_TRACE_EV(i, 0);
+      if (warp == 0) {
+        const uint32_t ma = __ballot_sync(0xffffffffu, ia >= 0 && (int64_t)ia < p.kv_len);
+        const uint32_t mb = __ballot_sync(0xffffffffu, ib >= 0 && (int64_t)ib < p.kv_len);
+        if (lane == 0) {
+          S.mask[slot][0] = ma;
+          S.mask[slot][1] = mb;
+        }
+      }
+      const __nv_bfloat16* kvb = p.kv + cur_tb * p.kv_sb + c * 8;
+      const uint32_t dst0 = smem_u32(S.ring[slot]) + j * SLAB_BYTES;
+#pragma unroll 8
+      for (int k = 0; k < UK / 2; ++k) {
+        const int32_t ida = __shfl_sync(0xffffffffu, ia, k);  // row 2k
+        const int32_t idb = __shfl_sync(0xffffffffu, ib, k);  // row 2k+1
+        const bool va = ida >= 0 && (int64_t)ida < p.kv_len;
+        const bool vb = idb >= 0 && (int64_t)idb < p.kv_len;
+        const int r = 2 * k;
+        cp_async16_hint(dst0 + r * 128 + ((cc ^ (r & 7)) << 4),
+                        kvb + (va ? (int64_t)ida : 0) * p.kv_sn, va ? 16 : 0, pol);
+        cp_async16_hint(dst0 + (r + 1) * 128 + ((cc ^ ((r + 1) & 7)) << 4),
+                        kvb + (vb ? (int64_t)idb : 0) * p.kv_sn, vb ? 16 : 0, pol);
+      }
+      // the slot's full barrier counts 64 hardware arrivals (one per thread,
+      // when its copies land) plus the mask writer's release arrival
+      cp_async_mbar_arrive_noinc(smem_u32(&S.full[slot]));
+      if (warp == 0 && lane == 0) mbar_arrive(smem_u32(&S.full[slot]));
+    }
+    cp_async_wait<0>();
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ Q producer
+    if (lane == 0) {
+      for (int64_t t = t_first; t <= t_last; ++t) {
+        const int s = static_cast<int>(t - t_first);
+        if (s > 0 && !wait_or_err(S, S.q_empty, (s - 1) & 1, 6)) continue;
+        const int64_t tb = t / p.m, tm = t - tb * p.m;
+        mbar_arrive_expect_tx(smem_u32(&S.q_full), Q_BYTES);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          tma_load_4d(smem_u32(S.q) + j * 2048, &q_map, 64 * j, 0, (int32_t)tm, (int32_t)tb,
+                      smem_u32(&S.q_full));
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int c = warp - 3;                   // 0..3
+    const int g8 = lane >> 2, q4 = lane & 3;  // mma fragment coordinates
+    const uint32_t qbase = smem_u32(S.q), pbase = smem_u32(S.p);
+    const uint32_t kOnes = 0x3F803F80u;  // bf16 pair (1, 1)
+    uint32_t qf[32][4];                  // Q A-fragments, 32 k-steps of 16 columns
+    float m_lo = -INFINITY, m_hi = -INFINITY;  // running max, heads g8 / g8+8 (log2)
+    float o[16][4];  // O[heads g8, g8+8][128c + 8nt + 2q4 + {0,1}]
+    float lacc[4];   // running row sums: [0] head g8, [2] head g8+8
+    int64_t t = t_first, kb = kb_first, seg_kb0 = kb_first;
+    int seg = 0;
+    bool seg_first = true;
+    for (int i = 0; i < n; ++i) {
+      const bool seg_end = (i == n - 1) || kb == upt - 1;
+      if (seg_first) {
+        m_lo = m_hi = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+        lacc[0] = lacc[1] = lacc[2] = lacc[3] = 0.f;
+        seg_kb0 = kb;
+        // this row's Q into registers, then hand the tile back to the Q producer
+        wait_or_err(S, S.q_full, seg & 1, 7);
+        {
+          const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+          for (int ks = 0; ks < 32; ++ks) {
+            const int ch = (ks & 3) * 2 + (lane >> 4);
+            ldmatrix_x4(qf[ks], qbase + (ks >> 2) * 2048 + row * 128 + ((ch ^ (row & 7)) << 4));
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&S.q_empty));
+      }
+      const int slot = i % NSLOT;
+      wait_or_err(S, S.full[slot], (i / NSLOT) & 1, 8);
+      const uint32_t sb = smem_u32(S.ring[slot]);
+
+      // ---- S for keys 16c + 8nt + {0..7}: 2 n-tiles x 32 k-steps, 2-way split
+      float sa[2][2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int z = 0; z < 2; ++z) sa[nt][z][0] = sa[nt][z][1] = sa[nt][z][2] = sa[nt][z][3] = 0.f;
+#pragma unroll
+      for (int kp = 0; kp < 16; ++kp) {  // k-steps 2kp, 2kp+1: columns 32kp..32kp+31
+        const int slab = kp >> 1, c0 = (kp & 1) * 4;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int key = 16 * c + 8 * nt + (lane & 7);
+          uint32_t kf[4];
+          ldmatrix_x4(kf, sb + slab * SLAB_BYTES + key * 128 + (((c0 + (lane >> 3)) ^ (key & 7)) << 4));
+          mma_16816(sa[nt][0], qf[2 * kp], kf[0], kf[1]);
+          mma_16816(sa[nt][1], qf[2 * kp + 1], kf[2], kf[3]);
+        }
+      }
+      // ---- softmax on the fragments: x[nt][0,1] head g8, x[nt][2,3] head g8+8,
+      //      keys 16c + 8nt + 2q4 + {0,1}
+      const uint32_t mw0 = S.mask[slot][0], mw1 = S.mask[slot][1];
+      float x[2][4];
+      bool over = false;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int l = 8 * c + 4 * nt + q4;  // producer lane that loaded these keys
+        const bool v0 = (mw0 >> l) & 1u, v1 = (mw1 >> l) & 1u;
+        x[nt][0] = v0 ? (sa[nt][0][0] + sa[nt][1][0]) * p.scale_log2 : -INFINITY;
+        x[nt][1] = v1 ? (sa[nt][0][1] + sa[nt][1][1]) * p.scale_log2 : -INFINITY;
+        x[nt][2] = v0 ? (sa[nt][0][2] + sa[nt][1][2]) * p.scale_log2 : -INFINITY;
+        x[nt][3] = v1 ? (sa[nt][0][3] + sa[nt][1][3]) * p.scale_log2 : -INFINITY;
+        over |= fmaxf(x[nt][0], x[nt][1]) > m_lo + kRescaleThreshold;
+        over |= fmaxf(x[nt][2], x[nt][3]) > m_hi + kRescaleThreshold;
+      }
+      // The vote barrier also orders this unit's P writes after every warp's
+      // P.V of the previous unit (single P tile).
+      if (named_bar_or(1, NCT, over)) {
+        // raise the running max to the block max (rare after a row's first unit)
+        float b_lo = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
+        float b_hi = fmaxf(fmaxf(x[0][2], x[0][3]), fmaxf(x[1][2], x[1][3]));
+#pragma unroll
+        for (int off = 1; off <= 2; off <<= 1) {
+          b_lo = fmaxf(b_lo, __shfl_xor_sync(0xffffffffu, b_lo, off));
+          b_hi = fmaxf(b_hi, __shfl_xor_sync(0xffffffffu, b_hi, off));
+        }
+        if (q4 == 0) {
+          S.red_max[c][g8] = b_lo;
+          S.red_max[c][g8 + 8] = b_hi;
+        }
+        named_bar(2, NCT);
+        float n_lo = m_lo, n_hi = m_hi;
+#pragma unroll
+        for (int w = 0; w < NCW; ++w) {
+          n_lo = fmaxf(n_lo, S.red_max[w][g8]);
+          n_hi = fmaxf(n_hi, S.red_max[w][g8 + 8]);
+        }
+        const float c_lo = (n_lo == m_lo) ? 1.f : exp2f(m_lo - n_lo);
+        const float c_hi = (n_hi == m_hi) ? 1.f : exp2f(m_hi - n_hi);
+        m_lo = n_lo;
+        m_hi = n_hi;
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) {
+          o[nt][0] *= c_lo;
+          o[nt][1] *= c_lo;
+          o[nt][2] *= c_hi;
+          o[nt][3] *= c_hi;
+        }
+        lacc[0] *= c_lo;
+        lacc[1] *= c_lo;
+        lacc[2] *= c_hi;
+        lacc[3] *= c_hi;
+      }
+      {
+        const float base_lo = (m_lo == -INFINITY) ? 0.f : m_lo;
+        const float base_hi = (m_hi == -INFINITY) ? 0.f : m_hi;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int ch = 2 * c + nt;  // keys 8ch..8ch+7
+          *reinterpret_cast<uint32_t*>(S.p + p_chunk(g8, ch) + 4 * q4) =
+              pack_bf16x2(exp2f(x[nt][0] - base_lo), exp2f(x[nt][1] - base_lo));
+          *reinterpret_cast<uint32_t*>(S.p + p_chunk(g8 + 8, ch) + 4 * q4) =
+              pack_bf16x2(exp2f(x[nt][2] - base_hi), exp2f(x[nt][3] - base_hi));
+        }
+      }
+      named_bar(3, NCT);  // P of all 64 keys written
+
+      // ---- O[16 x 128 cols of this warp] += P[16 x 64] . V[64 x 128]
+#pragma unroll
+      for (int kst = 0; kst < 4; ++kst) {
+        uint32_t pa[4];
+        {
+          const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+          ldmatrix_x4(pa, pbase + p_chunk(row, 2 * kst + (lane >> 4)));
+        }
+        mma_16816(lacc, pa, kOnes, kOnes);  // row sums of the bf16 P actually used
+        const int kr = kst * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {
+          const int slab = 2 * c + (np >> 2);
+          const int ch = ((np & 3) << 1) + (lane >> 4);
+          uint32_t vb[4];
+          ldmatrix_x4_trans(vb, sb + slab * SLAB_BYTES + kr * 128 + ((ch ^ (kr & 7)) << 4));
+          mma_16816(o[2 * np], pa, vb[0], vb[1]);
+          mma_16816(o[2 * np + 1], pa, vb[2], vb[3]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&S.empty[slot]));  // slot free for the producer
+
+      if (seg_end) {
+        // ---------------- epilogue of the segment ending at unit i ----------
+        const int64_t tb = t / p.m, tm = t - tb * p.m;
+        const float l_lo = lacc[0], l_hi = lacc[2];
+        if (seg_kb0 == 0 && kb == upt - 1) {
+          const float f_lo = sink_factor(m_lo, l_lo, __ldg(p.sink + g8) * kLog2e);
+          const float f_hi = sink_factor(m_hi, l_hi, __ldg(p.sink + g8 + 8) * kLog2e);
+          __nv_bfloat16* ob = p.o + tb * p.o_sb + tm * p.o_sm;
+#pragma unroll
+          for (int nt = 0; nt < 16; ++nt) {
+            const int d = 128 * c + 8 * nt + 2 * q4;
+            *reinterpret_cast<uint32_t*>(ob + g8 * p.o_sh + d) =
+                pack_bf16x2(o[nt][0] * f_lo, o[nt][1] * f_lo);
+            *reinterpret_cast<uint32_t*>(ob + (g8 + 8) * p.o_sh + d) =
+                pack_bf16x2(o[nt][2] * f_hi, o[nt][3] * f_hi);
+          }
+        } else {
+          const int64_t pslot = 2 * g + (t == t_first ? 0 : 1);
+          float* pacc = p.part_acc + pslot * kPartAccFloats;
+#pragma unroll
+          for (int nt = 0; nt < 16; ++nt) {
+            const int d = 128 * c + 8 * nt + 2 * q4;
+            *reinterpret_cast<float2*>(pacc + g8 * kDim + d) = make_float2(o[nt][0], o[nt][1]);
+            *reinterpret_cast<float2*>(pacc + (g8 + 8) * kDim + d) =
+                make_float2(o[nt][2], o[nt][3]);
+          }
+          if (c == 0 && q4 == 0) {
+            p.part_ml[pslot * kPartMlFloats + g8] = m_lo;
+            p.part_ml[pslot * kPartMlFloats + g8 + 8] = m_hi;
+            p.part_ml[pslot * kPartMlFloats + kHeads + g8] = l_lo;
+            p.part_ml[pslot * kPartMlFloats + kHeads + g8 + 8] = l_hi;
+          }
+        }
+      }
+      if (seg_end) ++seg;
+      seg_first = seg_end;
+      if (++kb == upt) {
+        kb = 0;
+        ++t;
+      }
+    }
+  }
+}
+
+}  // namespace ws_path
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+int ws_unit_keys() { return ws_path::UK; }
+
+int read_ws_error(int* flags) {
+  int v = 0;
+  const cudaError_t e = cudaMemcpyFromSymbol(&v, sa_ws_error, sizeof(int));
+  if (e != cudaSuccess) return (int)e;
+  *flags = v;
+  return 0;
+}
+
+cudaError_t encode_q_map(const Params& p, CUtensorMap* q_map);  // sa_tc.cu
+
+cudaError_t launch_ws(const Params& p, cudaStream_t st) {
+  using namespace ws_path;
+  CUtensorMap q_map;
+  cudaError_t e = encode_q_map(p, &q_map);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(sa_ws_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kSmemBytes);
+  if (e != cudaSuccess) return e;
+  sa_ws_fwd_kernel<<<p.grid, NT, kSmemBytes, st>>>(p, q_map);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return launch_combine(p, st);
+}
+
+}  // namespace sa

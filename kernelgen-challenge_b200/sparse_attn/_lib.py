@@ -23,6 +23,7 @@ SA_ERR_UNSUPPORTED = -4
 SA_VARIANT_AUTO = 0
 SA_VARIANT_MMA = 1
 SA_VARIANT_TCGEN05 = 2
+SA_VARIANT_WS = 3
 
 # every function the header declares, with its ctypes signature
 _I64 = ctypes.c_int64
