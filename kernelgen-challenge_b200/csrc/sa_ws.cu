@@ -124,6 +124,9 @@ __global__ void __launch_bounds__(NT, 1)
     fence_mbar_init();
   }
   if (warp == 2 && lane == 0) tma_prefetch_desc(&q_map);
+  // launched as a programmatic dependent of the previous kernel in the stream:
+  // the set-up above overlaps its tail; inputs are read only after it is done
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   __syncthreads();
 
 #define SA_TRACE_EV(u, e) ((void)0)
@@ -421,8 +424,17 @@ cudaError_t launch_ws(const Params& p, cudaStream_t st) {
   e = cudaFuncSetAttribute(sa_ws_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)kSmemBytes);
   if (e != cudaSuccess) return e;
-  sa_ws_fwd_kernel<<<p.grid, NT, kSmemBytes, st>>>(p, q_map);
-  e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
+  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, sa_ws_fwd_kernel, p, q_map);
   if (e != cudaSuccess) return e;
   return launch_combine(p, st);
 }
