@@ -282,25 +282,38 @@ __global__ void __launch_bounds__(NT, 1) sa_mma_fwd_kernel(const Params p) {
 
 // ----------------------------------------------------------------------------
 // LSE combine of split rows (shared by every variant).
-// Block (g, h): if CTA g ends a row that started in an earlier CTA ("owns"
-// it), merge the fp32 partials of CTAs f..g of that row for head h, with the
-// sink as the extra logit (reference.py:34-38); partial slots follow the rule
-// in sa_common.cuh.  64 threads x 8 columns.  All partial loads of a thread
-// are issued together (two memory round trips for up to kCombineBatch
-// partials).  Launched as a programmatic dependent of the forward kernel:
-// blocks are small (64 threads, no shared memory, <= 112 registers) so they
-// can become resident beside a running forward CTA, and griddepcontrol.wait
-// returns once the forward grid has completed and its stores are visible.
+// A row is split when the CTA that ends it ("owner") starts inside it.  Block
+// (j, h) merges head h of the j-th split row: the fp32 partials of CTAs
+// f..owner with the sink as the extra logit (reference.py:34-38); partial
+// slots follow the rule in sa_common.cuh.  64 threads x 8 columns, all loads
+// of a thread (maxima, sums and data of up to kCombineBatch partials) issued
+// together: one memory round trip.  The blocks are small (64 threads, <= 128
+// registers, no shared memory) so that, launched as programmatic dependents
+// of the forward kernel, they become resident beside its CTAs and start the
+// moment griddepcontrol.wait releases them (forward grid complete, stores
+// visible).
 // ----------------------------------------------------------------------------
-constexpr int kCombineBatch = 8;
+constexpr int kCombineBatch = 4;
+constexpr int kMaxOwners = 512;  // >= the largest persistent grid (2 x SM count)
 
-__global__ void __launch_bounds__(64) sa_combine_kernel(const Params p) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int64_t G = p.grid, g = blockIdx.x, U = p.units, upt = p.upt;
+struct OwnerList {
+  uint16_t cta[kMaxOwners];  // owner CTA of each split row, in CTA order
+};
+
+__host__ __device__ inline bool owns_split_row(int64_t g, int64_t U, int64_t G, int64_t upt) {
   const int64_t u0 = unit_begin(g, U, G), u1 = unit_begin(g + 1, U, G);
-  if (u0 >= u1) return;
-  const int64_t t = u0 / upt, ts = t * upt, te = ts + upt;
-  if (u0 == ts || u1 < te) return;
+  if (u0 >= u1) return false;
+  const int64_t ts = (u0 / upt) * upt;
+  return u0 != ts && u1 >= ts + upt;
+}
+
+__global__ void __launch_bounds__(64, 8) sa_combine_kernel(const Params p,
+                                                          const __grid_constant__ OwnerList owners) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int64_t G = p.grid, U = p.units, upt = p.upt;
+  const int64_t g = owners.cta[blockIdx.x];
+  const int64_t u0 = unit_begin(g, U, G);
+  const int64_t t = u0 / upt, ts = t * upt;
   const int64_t f = cta_of_unit(ts, U, G);
   const bool f_mid = unit_begin(f, U, G) < ts;
   const int np = static_cast<int>(g - f + 1);
@@ -312,13 +325,15 @@ __global__ void __launch_bounds__(64) sa_combine_kernel(const Params p) {
   float acc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-  // running merge over batches of partials (one batch in practice)
-  float M = sink_l2, den = 1.f;  // den is relative to M: exp2(sink - M) with M = sink
+  float M = sink_l2, den = 1.f;  // den relative to M (= exp2(sink - M) for M = sink)
   for (int k0 = 0; k0 < np; k0 += kCombineBatch) {
     float mk[kCombineBatch], lk[kCombineBatch];
     float4 va[kCombineBatch], vb[kCombineBatch];
 #pragma unroll
     for (int k = 0; k < kCombineBatch; ++k) {
+      mk[k] = -INFINITY;
+      lk[k] = 0.f;
+      va[k] = vb[k] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (k0 + k < np) {
         const int64_t sl = slot_of(k0 + k);
         mk[k] = __ldcg(p.part_ml + sl * kPartMlFloats + h);
@@ -331,26 +346,23 @@ __global__ void __launch_bounds__(64) sa_combine_kernel(const Params p) {
     }
     float Mb = M;
 #pragma unroll
-    for (int k = 0; k < kCombineBatch; ++k)
-      if (k0 + k < np) Mb = fmaxf(Mb, mk[k]);
+    for (int k = 0; k < kCombineBatch; ++k) Mb = fmaxf(Mb, mk[k]);
     const float r = exp2f(M - Mb);  // rescale what was merged so far
     den *= r;
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] *= r;
 #pragma unroll
     for (int k = 0; k < kCombineBatch; ++k) {
-      if (k0 + k < np) {
-        const float w = exp2f(mk[k] - Mb);
-        den += lk[k] * w;
-        acc[0] += w * va[k].x;
-        acc[1] += w * va[k].y;
-        acc[2] += w * va[k].z;
-        acc[3] += w * va[k].w;
-        acc[4] += w * vb[k].x;
-        acc[5] += w * vb[k].y;
-        acc[6] += w * vb[k].z;
-        acc[7] += w * vb[k].w;
-      }
+      const float w = exp2f(mk[k] - Mb);  // 0 for absent partials
+      den += lk[k] * w;
+      acc[0] += w * va[k].x;
+      acc[1] += w * va[k].y;
+      acc[2] += w * va[k].z;
+      acc[3] += w * va[k].w;
+      acc[4] += w * vb[k].x;
+      acc[5] += w * vb[k].y;
+      acc[6] += w * vb[k].z;
+      acc[7] += w * vb[k].w;
     }
     M = Mb;
   }
@@ -364,20 +376,23 @@ __global__ void __launch_bounds__(64) sa_combine_kernel(const Params p) {
   *reinterpret_cast<uint4*>(p.o + tb * p.o_sb + tm * p.o_sm + h * p.o_sh + d0) = w;
 }
 
-// True when some token is split across CTAs (the combine kernel has work).
-bool any_split(const Params& p) {
-  for (int64_t g = 1; g < p.grid; ++g)
-    if (unit_begin(g, p.units, p.grid) % p.upt != 0) return true;
-  return false;
+// Owner CTAs of the split rows (the combine kernel's blocks).
+int split_rows(const Params& p, OwnerList* list) {
+  int n = 0;
+  for (int64_t g = 1; g < p.grid && n < kMaxOwners; ++g)
+    if (owns_split_row(g, p.units, p.grid, p.upt)) list->cta[n++] = static_cast<uint16_t>(g);
+  return n;
 }
 
 cudaError_t launch_combine(const Params& p, cudaStream_t st) {
 #ifdef SA_NO_COMBINE  // development builds only: time the forward kernel alone
   return cudaSuccess;
 #endif
-  if (!any_split(p)) return cudaSuccess;
+  OwnerList owners;
+  const int rows = split_rows(p, &owners);
+  if (rows == 0) return cudaSuccess;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(p.grid), kHeads, 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(rows), kHeads, 1);
   cfg.blockDim = dim3(64, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
@@ -386,7 +401,7 @@ cudaError_t launch_combine(const Params& p, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, sa_combine_kernel, p);
+  return cudaLaunchKernelEx(&cfg, sa_combine_kernel, p, owners);
 }
 
 int mma_unit_keys() { return mma_path::BN; }
