@@ -1,0 +1,55 @@
+"""Row-sharded run over NCCL on 2 GPUs equals the single-GPU result (GPU).
+
+Skipped unless at least two GPUs are visible.  Each rank computes its row
+range of a reduced long-context problem with the B200 op and the ranks
+all-gather the output; the single-GPU op on the same inputs is the check
+(bitwise: both run the same kernel on the same rows).
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs():
+    import dataclasses
+    from sparse_attn.workloads import CONFIGS, make_inputs
+    cfg = dataclasses.replace(CONFIGS["long"], b=2, m=96)
+    return make_inputs(cfg, seed=5)
+
+
+def _worker(rank, world, port, path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    from sparse_attn.shard import sparse_attn_sharded
+    q, kv, sink, idx, scale = _inputs()
+    o = sparse_attn_sharded(q.to(dev), kv.to(dev), sink.to(dev), idx.to(dev), scale)
+    torch.cuda.synchronize()
+    if rank == 0:
+        torch.save(o.cpu(), path)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sharded_nccl_two_gpus_equals_single_gpu(tmp_path):
+    from sparse_attn import sparse_attn
+    path = str(tmp_path / "o.pt")
+    mp.spawn(_worker, args=(2, _free_port(), path), nprocs=2, join=True)
+    q, kv, sink, idx, scale = _inputs()
+    ref = sparse_attn(q.cuda(), kv.cuda(), sink.cuda(), idx.cuda(), scale).cpu()
+    assert torch.equal(torch.load(path), ref)
