@@ -2,8 +2,9 @@
 
 Skipped unless at least two GPUs are visible.  Each rank computes its row
 range of a reduced long-context problem with the B200 op and the ranks
-all-gather the output; the single-GPU op on the same inputs is the check
-(bitwise: both run the same kernel on the same rows).
+all-gather the output; the single-GPU op on the same inputs is the check,
+within the parity tolerance (a rank's smaller problem splits rows across
+CTAs differently, so partial sums merge in a different order).
 """
 import os
 import socket
@@ -52,4 +53,5 @@ def test_sharded_nccl_two_gpus_equals_single_gpu(tmp_path):
     mp.spawn(_worker, args=(2, _free_port(), path), nprocs=2, join=True)
     q, kv, sink, idx, scale = _inputs()
     ref = sparse_attn(q.cuda(), kv.cuda(), sink.cuda(), idx.cuda(), scale).cpu()
-    assert torch.equal(torch.load(path), ref)
+    from helpers import assert_close
+    assert_close(torch.load(path), ref, what="2-GPU sharded vs 1 GPU")
