@@ -1,0 +1,41 @@
+"""Profiling driver: three L2-flushed calls of one configuration.
+
+    python -m sparse_attn.profile_case <config> [variant]
+
+Counterpart of the reference's ``track-01/profile.py`` (torch.profiler
+timeline, :19-33); here it is the target program for ``ncu`` captures
+(``-s 1 -c 1`` selects the second call).  Inputs are seeded and made on the
+GPU; ``variant`` is an SA_VARIANT_* number (0 = automatic).
+"""
+from __future__ import annotations
+
+import sys
+
+import torch
+
+from . import sparse_attn_out, workspace_bytes
+from .workloads import CONFIGS, D, H, SCALE, make_indices
+
+
+def main(argv=None):
+    argv = sys.argv[1:] if argv is None else argv
+    cfg = CONFIGS[argv[0] if argv else "decode"]
+    variant = int(argv[1]) if len(argv) > 1 else 0
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(cfg.b, cfg.m, H, D, generator=g, device=dev, dtype=torch.bfloat16)
+    kv = torch.randn(cfg.b, cfg.kv_len, D, generator=g, device=dev, dtype=torch.bfloat16)
+    sink = torch.randn(H, generator=g, device=dev)
+    idx = make_indices(cfg, torch.Generator().manual_seed(0)).to(dev)
+    o = torch.empty_like(q)
+    ws = torch.empty(workspace_bytes(cfg.b, cfg.m, cfg.topk, 0), dtype=torch.uint8, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        flush.zero_()
+        sparse_attn_out(o, q, kv, sink, idx, SCALE, ws, variant=variant)
+    torch.cuda.synchronize()
+    print(f"{cfg.name}: mean |o| = {o.float().abs().mean().item():.5f}")
+
+
+if __name__ == "__main__":
+    main()
