@@ -163,9 +163,11 @@ def device_inputs(cfg, seed, device):
 
 
 def profile_our_kernels(fn, flush, reps=5):
-    """Our kernels launched per call of ``fn`` and their mean device duration,
-    from a CUPTI trace of ``reps`` L2-flushed calls made outside every timed
-    region.  Returns (launches per call, {kernel: mean us}) or (None, {error})."""
+    """Our kernels launched per call of ``fn``, their mean device duration, and
+    the mean device timeline of a call (gap after the preceding kernel, span
+    from our first kernel's start to our last kernel's end), from a CUPTI trace
+    of ``reps`` L2-flushed calls made outside every timed region.
+    Returns (launches per call, {name: mean us}) or (None, {error})."""
     try:
         from torch.profiler import ProfilerActivity, profile
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
@@ -173,17 +175,34 @@ def profile_our_kernels(fn, flush, reps=5):
                 flush.zero_()
                 fn()
             torch.cuda.synchronize()
-        per, n = {}, 0
-        for e in prof.events():
-            if e.device_type.name != "CUDA":
-                continue
-            name = e.name
-            if "sa_" in name and ("fwd_kernel" in name or "combine" in name):
-                short = name.split("(")[0].split("::")[-1]
-                per.setdefault(short, []).append(e.device_time_total if hasattr(
-                    e, "device_time_total") else e.cuda_time_total)
+        kern = sorted((e for e in prof.events() if e.device_type.name == "CUDA"),
+                      key=lambda e: e.time_range.start)
+        per, gaps, spans, n = {}, [], [], 0
+        prev_end, first_start, last_end = None, None, None
+        for e in kern:
+            ours = "sa_" in e.name and ("fwd_kernel" in e.name or "combine" in e.name)
+            if ours:
+                short = e.name.split("(")[0].split("::")[-1]
+                per.setdefault(short, []).append(e.time_range.end - e.time_range.start)
                 n += 1
-        return n // reps, {k: statistics.mean(v) for k, v in per.items()}
+                if first_start is None:
+                    first_start = e.time_range.start
+                    if prev_end is not None:
+                        gaps.append(first_start - prev_end)
+                last_end = e.time_range.end
+            else:
+                if first_start is not None:
+                    spans.append(last_end - first_start)
+                    first_start = None
+                prev_end = e.time_range.end
+        if first_start is not None:
+            spans.append(last_end - first_start)
+        out = {k: statistics.mean(v) for k, v in per.items()}
+        if gaps:
+            out["gap_after_previous_kernel"] = statistics.mean(gaps)
+        if spans:
+            out["span_first_start_to_last_end"] = statistics.mean(spans)
+        return n // reps, out
     except Exception as e:  # profiler unavailable: report unknown
         return None, {"profiler failed": str(e)}
 

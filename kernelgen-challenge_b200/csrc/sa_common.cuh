@@ -27,6 +27,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 namespace sa {
 
 constexpr int kHeads = 16;
@@ -73,6 +75,23 @@ __host__ __device__ inline int64_t unit_begin(int64_t g, int64_t units, int64_t 
 // Largest CTA index k with unit_begin(k) <= u (requires grid <= units).
 __host__ __device__ inline int64_t cta_of_unit(int64_t u, int64_t units, int64_t grid) {
   return ((u + 1) * grid - 1) / units;
+}
+
+// Runs `fn` (returning cudaError_t) once per CUDA device, the first time it is
+// called with that device current; later calls return the first result.
+struct PerDeviceOnce {
+  static constexpr int kMax = 64;
+  std::once_flag flag[kMax];
+  cudaError_t err[kMax] = {};
+};
+template <class Fn>
+cudaError_t once_per_device(PerDeviceOnce& o, Fn&& fn) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= PerDeviceOnce::kMax) return cudaErrorInvalidDevice;
+  std::call_once(o.flag[dev], [&] { o.err[dev] = fn(); });
+  return o.err[dev];
 }
 
 // Launches the LSE-combine kernel when some row is split across CTAs

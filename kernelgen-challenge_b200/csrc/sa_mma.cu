@@ -410,8 +410,11 @@ size_t mma_smem_bytes() { return sizeof(mma_path::Smem); }
 
 cudaError_t launch_mma(const Params& p, cudaStream_t st) {
   const size_t smem = sizeof(mma_path::Smem);
-  cudaError_t e = cudaFuncSetAttribute(mma_path::sa_mma_fwd_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static PerDeviceOnce attr_once;
+  cudaError_t e = once_per_device(attr_once, [&] {
+    return cudaFuncSetAttribute(mma_path::sa_mma_fwd_kernel,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  });
   if (e != cudaSuccess) return e;
   mma_path::sa_mma_fwd_kernel<<<p.grid, mma_path::NT, smem, st>>>(p);
   e = cudaGetLastError();

@@ -421,8 +421,11 @@ cudaError_t launch_ws(const Params& p, cudaStream_t st) {
   CUtensorMap q_map;
   cudaError_t e = encode_q_map(p, &q_map);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(sa_ws_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)kSmemBytes);
+  static PerDeviceOnce attr_once;
+  e = once_per_device(attr_once, [] {
+    return cudaFuncSetAttribute(sa_ws_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kSmemBytes);
+  });
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);

@@ -1,4 +1,4 @@
-"""``sparse_attn`` as a torch custom op over the C ABI.
+"""``sparse_attn`` over the C ABI, plus its torch custom-op registration.
 
 Drop-in for ``track-01/submission.py:975`` — same name, arguments, dtypes,
 shapes and return value:
@@ -11,8 +11,17 @@ makes the inputs contiguous (:995-998) and allocates the output (:1000); the
 launch goes to ``libsparse_attn.so`` on the current CUDA stream.  Anything the
 C library rejects raises ``RuntimeError`` with the library's status text.
 There is no CPU path: CPU tensors raise.
+
+The call path is kept short (the kernels of a decode step take ~40 us, so
+host overhead matters): the workspace is cached per (device, stream) and
+reused by every call on that stream (stream order makes that safe; ~19 MB per
+stream on a B200), and the C library is called directly.  The same function
+is registered as the torch custom op ``torch.ops.sparse_attn_b200.fwd`` (with
+a fake implementation) for graph capture and ``torch.compile`` users.
 """
 from __future__ import annotations
+
+import functools
 
 import torch
 
@@ -21,14 +30,37 @@ from . import _lib
 __all__ = ["sparse_attn", "sparse_attn_out", "workspace_bytes"]
 
 
-def workspace_bytes(b: int, m: int, topk: int, device: torch.device | int | None = None) -> int:
-    dev = torch.cuda.current_device() if device is None else torch.device("cuda", device).index \
-        if isinstance(device, int) else (device.index if device.index is not None
-                                          else torch.cuda.current_device())
+def _device_index(device) -> int:
+    if device is None:
+        return torch.cuda.current_device()
+    if isinstance(device, int):
+        return device
+    return device.index if device.index is not None else torch.cuda.current_device()
+
+
+@functools.lru_cache(maxsize=256)
+def _workspace_bytes(b: int, m: int, topk: int, dev: int) -> int:
     n = _lib.lib().sa_workspace_bytes(b, m, topk, dev)
     if n == 0:
         raise RuntimeError(f"sparse_attn: cannot size workspace on cuda:{dev}")
     return int(n)
+
+
+def workspace_bytes(b: int, m: int, topk: int, device: torch.device | int | None = None) -> int:
+    """Device workspace (bytes) ``sparse_attn_out`` needs for this problem."""
+    return _workspace_bytes(int(b), int(m), int(topk), _device_index(device))
+
+
+_ws_cache: dict = {}
+
+
+def _cached_workspace(dev: torch.device, stream, nbytes: int) -> torch.Tensor:
+    key = (dev.index, stream.cuda_stream)
+    ws = _ws_cache.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        _ws_cache[key] = ws
+    return ws
 
 
 def _validate(q, kv, attn_sink, topk_idxs):
@@ -64,15 +96,14 @@ def sparse_attn_out(o, q, kv, attn_sink, topk_idxs, scale, workspace=None, *,
 
     No copies: q/kv/o need a unit last-dim stride and 16-byte aligned rows.
     ``workspace`` (uint8 CUDA tensor of at least :func:`workspace_bytes`) is
-    allocated here when omitted.  ``variant``/``grid`` select the kernel
+    taken from a per-(device, stream) cache when omitted.  ``variant``/``grid`` select the kernel
     variant and persistent grid size (0 = automatic).
     """
     b, m, h, d = q.shape
     kv_len, topk = kv.shape[1], topk_idxs.shape[-1]
-    if workspace is None:
-        workspace = torch.empty(workspace_bytes(b, m, topk, q.device), dtype=torch.uint8,
-                                device=q.device)
     st = torch.cuda.current_stream(q.device) if stream is None else stream
+    if workspace is None:
+        workspace = _cached_workspace(q.device, st, workspace_bytes(b, m, topk, q.device))
     L = _lib.lib()
     rc = L.sa_fwd_ex(
         q.data_ptr(), kv.data_ptr(), attn_sink.data_ptr(), topk_idxs.data_ptr(), o.data_ptr(),
@@ -85,9 +116,7 @@ def sparse_attn_out(o, q, kv, attn_sink, topk_idxs, scale, workspace=None, *,
     return o
 
 
-@torch.library.custom_op("sparse_attn_b200::fwd", mutates_args=())
-def _fwd(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor,
-         topk_idxs: torch.Tensor, scale: float) -> torch.Tensor:
+def _forward(q, kv, attn_sink, topk_idxs, scale):
     _validate(q, kv, attn_sink, topk_idxs)
     q_c = q if _row_ok(q) else q.contiguous()
     kv_c = kv if _row_ok(kv) else kv.contiguous()
@@ -96,9 +125,16 @@ def _fwd(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor,
     o = torch.empty(b, m, h, d, dtype=q.dtype, device=q.device)
     if o.numel() == 0:
         return o
-    with torch.cuda.device(q.device):
-        sparse_attn_out(o, q_c, kv_c, sink_c, topk_idxs, scale)
-    return o
+    if q.device.index != torch.cuda.current_device():
+        with torch.cuda.device(q.device):
+            return sparse_attn_out(o, q_c, kv_c, sink_c, topk_idxs, scale)
+    return sparse_attn_out(o, q_c, kv_c, sink_c, topk_idxs, scale)
+
+
+@torch.library.custom_op("sparse_attn_b200::fwd", mutates_args=())
+def _fwd(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor,
+         topk_idxs: torch.Tensor, scale: float) -> torch.Tensor:
+    return _forward(q, kv, attn_sink, topk_idxs, scale)
 
 
 @_fwd.register_fake
@@ -120,4 +156,4 @@ def sparse_attn(q, kv, attn_sink, topk_idxs, scale):
     Returns:
         o:          [b, m, h, d]   bf16
     """
-    return _fwd(q, kv, attn_sink, topk_idxs, float(scale))
+    return _forward(q, kv, attn_sink, topk_idxs, float(scale))

@@ -157,3 +157,14 @@ def test_no_pipeline_timeouts():
     args = make_inputs("plumbing", seed=3)
     run_gpu(*args)
     assert device_status() == 0
+
+
+def test_custom_op_registration_matches():
+    """torch.ops.sparse_attn_b200.fwd (for graph capture / compile users) is the
+    same computation as the drop-in function."""
+    args, o_gold = load_golden("ragged")
+    a = _cuda(*args)
+    o1 = torch.ops.sparse_attn_b200.fwd(a[0], a[1], a[2], a[3], float(a[4]))
+    o2 = sparse_attn(*a)
+    assert torch.equal(o1, o2)
+    assert_close(o1, o_gold, what="custom op")
