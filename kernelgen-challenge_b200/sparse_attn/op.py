@@ -3,8 +3,10 @@
 Drop-in for ``track-01/submission.py:975`` — same name, arguments, dtypes,
 shapes and return value:
 
-    sparse_attn(q[b,m,16,512] bf16, kv[b,kv_len,512] bf16, attn_sink[16] fp32,
-                topk_idxs[b,m,topk] int32, scale: float) -> o[b,m,16,512] bf16
+    sparse_attn(q[b,m,h,512] bf16, kv[b,kv_len,512] bf16, attn_sink[h] fp32,
+                topk_idxs[b,m,topk] int32, scale: float) -> o[b,m,h,512] bf16
+
+with h <= 16 (the kernels run 16 heads; fewer are zero-padded).
 
 Like the reference wrapper it asserts ``q.dim() == 4`` (submission.py:989),
 makes the inputs contiguous (:995-998) and allocates the output (:1000); the
@@ -116,8 +118,23 @@ def sparse_attn_out(o, q, kv, attn_sink, topk_idxs, scale, workspace=None, *,
     return o
 
 
+_KERNEL_HEADS = 16
+
+
 def _forward(q, kv, attn_sink, topk_idxs, scale):
     _validate(q, kv, attn_sink, topk_idxs)
+    h = q.shape[2]
+    if h < _KERNEL_HEADS:
+        # fewer heads: pad to the kernel's 16 (the reference pads to
+        # max(16, next_pow2(h)) and masks, submission.py:1004); heads are
+        # independent, so the padded heads only cost their own work
+        if h == 0:
+            return q.new_empty(q.shape)
+        qp = q.new_zeros(*q.shape[:2], _KERNEL_HEADS, q.shape[3])
+        qp[:, :, :h] = q
+        sp = attn_sink.new_zeros(_KERNEL_HEADS)
+        sp[:h] = attn_sink
+        return _forward(qp, kv, sp, topk_idxs, scale)[:, :, :h].contiguous()
     q_c = q if _row_ok(q) else q.contiguous()
     kv_c = kv if _row_ok(kv) else kv.contiguous()
     sink_c = attn_sink.contiguous()
@@ -147,7 +164,7 @@ def sparse_attn(q, kv, attn_sink, topk_idxs, scale):
     """Top-k sparse attention with attention sink (track-01 signature).
 
     Args:
-        q:          [b, m, h, d]   bf16 (h = 16, d = 512)
+        q:          [b, m, h, d]   bf16 (h <= 16, d = 512)
         kv:         [b, kv_len, d] bf16 (K and V shared)
         attn_sink:  [h]            fp32
         topk_idxs:  [b, m, topk]   int32; -1 (or any index outside [0, kv_len))

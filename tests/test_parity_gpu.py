@@ -168,3 +168,40 @@ def test_custom_op_registration_matches():
     o2 = sparse_attn(*a)
     assert torch.equal(o1, o2)
     assert_close(o1, o_gold, what="custom op")
+
+
+@pytest.mark.parametrize("h", [1, 5, 8, 16])
+def test_fewer_heads_padded(h):
+    """h < 16 is served by padding to 16 heads (reference: submission.py:1004)."""
+    q, kv, sink, idx, scale = make_golden.make_case("ragged")
+    q, sink = q[:, :, :h].contiguous(), sink[:h].contiguous()
+    o = sparse_attn(*_cuda(q, kv, sink, idx, scale))
+    assert o.shape == q.shape
+    assert_close(o, sparse_attn_oracle(q, kv, sink, idx, scale), what=f"h={h}")
+
+
+def _ragged_case(seed=11):
+    """1200 rows (ragged schedule), rows padded with -1 to random lengths,
+    interior -1 slots, and a few fully masked rows."""
+    g = torch.Generator().manual_seed(seed)
+    b, m, kv_len, topk = 2, 600, 300, 200
+    q = torch.randn(b, m, 16, 512, generator=g).to(torch.bfloat16)
+    kv = torch.randn(b, kv_len, 512, generator=g).to(torch.bfloat16)
+    sink = torch.randn(16, generator=g)
+    idx = torch.randint(0, kv_len, (b, m, topk), generator=g, dtype=torch.int32)
+    length = torch.randint(0, topk + 1, (b, m, 1), generator=g)
+    idx = torch.where(torch.arange(topk)[None, None, :] < length, idx, torch.full_like(idx, -1))
+    idx = torch.where(torch.rand(b, m, topk, generator=g) < 0.1, torch.full_like(idx, -1), idx)
+    idx[0, 7] = -1
+    idx[1, 599] = -1
+    return q, kv, sink, idx, 512 ** -0.5
+
+
+@pytest.mark.parametrize("grid", [0, 5, 1000])
+def test_ragged_schedule_rows_of_varying_length(grid):
+    args = _ragged_case()
+    ref = sparse_attn_oracle(*args)
+    for v in VARIANTS:
+        o = run_gpu(*args, variant=v, grid=grid)
+        assert_close(o, ref, what=f"ragged variant={v} grid={grid}")
+        assert torch.count_nonzero(o[0, 7]) == 0 and torch.count_nonzero(o[1, 599]) == 0
