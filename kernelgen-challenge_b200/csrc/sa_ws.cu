@@ -26,12 +26,12 @@
 //   O[16 x 128c..128c+127] += P . V  consumer warp c: slabs 2c, 2c+1 (64 MMAs)
 //   row sums l = P . 1               (4 MMAs, every warp, no reduction)
 //
-// Warp roles (224 threads, one CTA per SM):
-//   warps 0..1   KV producer (cp.async into a 3-deep ring of 64 KiB slots)
-//   warp 2       Q producer (one tiled TMA per 64 columns when a row starts;
-//                the consumers release the Q tile as soon as they hold its
-//                fragments, so the next row's Q load overlaps this row)
-//   warps 3..6   consumers c = 0..3
+// Warp roles (256 threads, one CTA per SM):
+//   warps 0..3   KV producer (cp.async from 128 threads into a 3-deep ring of
+//                64 KiB slots)
+//   warps 4..7   consumers c = 0..3; once all four hold a row's Q fragments,
+//                one of them refills the Q tile with the next row's Q by TMA
+//                (one box per 64 columns), so that load overlaps this row
 //
 // Every mbarrier wait is bounded; on a timeout the CTA records an error code
 // in sa_ws_error (readable through sa_device_status) and stops issuing work.
@@ -44,6 +44,23 @@ namespace sa {
 
 __device__ int sa_ws_error;  // nonzero after a bounded wait gave up
 
+#ifdef SA_TRACE
+// Pipeline timeline for development builds only (-DSA_TRACE): per CTA, per
+// unit (first kTraceUnits), per event, %globaltimer in ns.
+constexpr int kTraceCtas = 160, kTraceUnits = 16, kTraceEvents = 8;
+__device__ unsigned long long sa_ws_trace[kTraceCtas][kTraceUnits][kTraceEvents];
+__device__ __forceinline__ void ws_trace_ev(int unit, int ev) {
+  if (blockIdx.x < kTraceCtas && unit < kTraceUnits) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    sa_ws_trace[blockIdx.x][unit][ev] = t;
+  }
+}
+#define SA_TRACE_EV(u, e) ws_trace_ev((u), (e))
+#else
+#define SA_TRACE_EV(u, e) ((void)0)
+#endif
+
 namespace ws_path {
 using namespace tc;
 
@@ -55,7 +72,7 @@ constexpr int Q_BYTES = kHeads * kDim * 2;  // 16 KiB
 constexpr int P_BYTES = kHeads * UK * 2;    // 2 KiB, P [head][key] bf16
 constexpr int NCW = 4;                      // consumer warps
 constexpr int NCT = NCW * 32;
-constexpr int NT = 3 * 32 + NCT;            // 224
+constexpr int NT = 4 * 32 + NCT;            // 256: every warp may use 255 registers
 constexpr float kRescaleThreshold = 8.0f;   // log2 domain
 
 struct __align__(1024) Smem {
@@ -64,9 +81,9 @@ struct __align__(1024) Smem {
   uint8_t p[P_BYTES];
   uint32_t mask[NSLOT][2];  // validity: [0] keys 2l, [1] keys 2l+1 (bit l)
   float red_max[NCW][kHeads];
-  // full: rows landed (64 cp.async arrivals + mask writer); empty: the four
-  // consumer warps finished the unit; q_full / q_empty: the Q tile
-  uint64_t full[NSLOT], empty[NSLOT], q_full, q_empty;
+  // full: rows landed (128 cp.async arrivals + mask writer); empty: the four
+  // consumer warps finished the unit; q_full: the Q tile of the next row
+  uint64_t full[NSLOT], empty[NSLOT], q_full;
   int err;
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + manual 1 KiB alignment
@@ -115,28 +132,28 @@ __global__ void __launch_bounds__(NT, 1)
 
   if (tid == 0) {
     for (int s = 0; s < NSLOT; ++s) {
-      mbar_init(smem_u32(&S.full[s]), 64 + 1);
+      mbar_init(smem_u32(&S.full[s]), 128 + 1);
       mbar_init(smem_u32(&S.empty[s]), NCW);
     }
     mbar_init(smem_u32(&S.q_full), 1);
-    mbar_init(smem_u32(&S.q_empty), NCW);
     S.err = 0;
     fence_mbar_init();
   }
-  if (warp == 2 && lane == 0) tma_prefetch_desc(&q_map);
+  if (warp == 4 && lane == 0) tma_prefetch_desc(&q_map);
   // launched as a programmatic dependent of the previous kernel in the stream:
   // the set-up above overlaps its tail; inputs are read only after it is done
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __syncthreads();
 
-#define SA_TRACE_EV(u, e) ((void)0)
-  if (warp < 2) {
+  if (warp < 4) {
     // ------------------------------------------------------------ KV producer
-    // 64 threads; thread c copies 16-byte chunk c of all 64 rows, so every
-    // warp-wide cp.async reads 512 contiguous bytes of one row.  The rows land
-    // in the 128-byte-swizzled slab layout.
+    // 128 threads; thread pt copies 16-byte chunk c = pt & 63 of the 32 rows
+    // of parity pt >> 6, so every warp-wide cp.async reads 512 contiguous bytes
+    // of one row.  The rows land in the 128-byte-swizzled slab layout.  (With
+    // half as many issuing threads the gather rate drops by a quarter: issue,
+    // not memory, would then bound it.)
     const uint64_t pol = l2_policy_evict_first();
-    const int c = tid, j = c >> 3, cc = c & 7;
+    const int c = tid & 63, par = tid >> 6, j = c >> 3, cc = c & 7;
     int64_t t = t_first, kb = kb_first;
     int64_t tb = t / p.m, tm = t - tb * p.m;
     auto load_ids = [&](int64_t kb_, int64_t tb_, int64_t tm_, int32_t& a, int32_t& b) {
@@ -175,42 +192,25 @@ __global__ void __launch_bounds__(NT, 1)
       }
       const __nv_bfloat16* kvb = p.kv + cur_tb * p.kv_sb + c * 8;
       const uint32_t dst0 = smem_u32(S.ring[slot]) + j * SLAB_BYTES;
+      const int32_t mine = par ? ib : ia;  // warp-uniform parity
 #pragma unroll 8
       for (int k = 0; k < UK / 2; ++k) {
-        const int32_t ida = __shfl_sync(0xffffffffu, ia, k);  // row 2k
-        const int32_t idb = __shfl_sync(0xffffffffu, ib, k);  // row 2k+1
-        const bool va = ida >= 0 && (int64_t)ida < p.kv_len;
-        const bool vb = idb >= 0 && (int64_t)idb < p.kv_len;
-        const int r = 2 * k;
+        const int32_t id = __shfl_sync(0xffffffffu, mine, k);  // row 2k + par
+        const bool v = id >= 0 && (int64_t)id < p.kv_len;
+        const int r = 2 * k + par;
         cp_async16_hint(dst0 + r * 128 + ((cc ^ (r & 7)) << 4),
-                        kvb + (va ? (int64_t)ida : 0) * p.kv_sn, va ? 16 : 0, pol);
-        cp_async16_hint(dst0 + (r + 1) * 128 + ((cc ^ ((r + 1) & 7)) << 4),
-                        kvb + (vb ? (int64_t)idb : 0) * p.kv_sn, vb ? 16 : 0, pol);
+                        kvb + (v ? (int64_t)id : 0) * p.kv_sn, v ? 16 : 0, pol);
       }
-      // the slot's full barrier counts 64 hardware arrivals (one per thread,
+      // the slot's full barrier counts 128 hardware arrivals (one per thread,
       // when its copies land) plus the mask writer's release arrival
       cp_async_mbar_arrive_noinc(smem_u32(&S.full[slot]));
       if (warp == 0 && lane == 0) mbar_arrive(smem_u32(&S.full[slot]));
     }
     cp_async_wait<0>();
-  } else if (warp == 2) {
-    // ------------------------------------------------------------ Q producer
-    if (lane == 0) {
-      for (int64_t t = t_first; t <= t_last; ++t) {
-        const int s = static_cast<int>(t - t_first);
-        if (s > 0 && !wait_or_err(S, S.q_empty, (s - 1) & 1, 6)) continue;
-        const int64_t tb = t / p.m, tm = t - tb * p.m;
-        mbar_arrive_expect_tx(smem_u32(&S.q_full), Q_BYTES);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          tma_load_4d(smem_u32(S.q) + j * 2048, &q_map, 64 * j, 0, (int32_t)tm, (int32_t)tb,
-                      smem_u32(&S.q_full));
-      }
-    }
-    __syncwarp();
   } else {
     // ------------------------------------------------------------ consumers
-    const int c = warp - 3;                   // 0..3
+    const int c = warp - 4;                   // 0..3
+    const int tt = tid - 128;                 // consumer thread 0..127
     const int g8 = lane >> 2, q4 = lane & 3;  // mma fragment coordinates
     const uint32_t qbase = smem_u32(S.q), pbase = smem_u32(S.p);
     const uint32_t kOnes = 0x3F803F80u;  // bf16 pair (1, 1)
@@ -218,6 +218,16 @@ __global__ void __launch_bounds__(NT, 1)
     float m_lo = -INFINITY, m_hi = -INFINITY;  // running max, heads g8 / g8+8 (log2)
     float o[16][4];  // O[heads g8, g8+8][128c + 8nt + 2q4 + {0,1}]
     float lacc[4];   // running row sums: [0] head g8, [2] head g8+8
+    auto issue_q = [&](int64_t row) {
+      const int64_t qb = row / p.m, qm = row - qb * p.m;
+      fence_proxy_async_smem();  // the Q fragment reads above precede the TMA refill
+      mbar_arrive_expect_tx(smem_u32(&S.q_full), Q_BYTES);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        tma_load_4d(qbase + j * 2048, &q_map, 64 * j, 0, (int32_t)qm, (int32_t)qb,
+                    smem_u32(&S.q_full));
+    };
+    if (tt == 0) issue_q(t_first);
     int64_t t = t_first, kb = kb_first, seg_kb0 = kb_first;
     int seg = 0;
     bool seg_first = true;
@@ -229,8 +239,10 @@ __global__ void __launch_bounds__(NT, 1)
         for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
         lacc[0] = lacc[1] = lacc[2] = lacc[3] = 0.f;
         seg_kb0 = kb;
-        // this row's Q into registers, then hand the tile back to the Q producer
+        // this row's Q into registers; once every consumer holds it, the tile
+        // is refilled with the next row's Q (one TMA box per 64 columns)
         wait_or_err(S, S.q_full, seg & 1, 7);
+        if (c == 0 && lane == 0) SA_TRACE_EV(i, 6);
         {
           const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
@@ -239,11 +251,12 @@ __global__ void __launch_bounds__(NT, 1)
             ldmatrix_x4(qf[ks], qbase + (ks >> 2) * 2048 + row * 128 + ((ch ^ (row & 7)) << 4));
           }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&S.q_empty));
+        named_bar(4, NCT);
+        if (tt == 0 && t < t_last) issue_q(t + 1);
       }
       const int slot = i % NSLOT;
       wait_or_err(S, S.full[slot], (i / NSLOT) & 1, 8);
+      if (c == 0 && lane == 0) SA_TRACE_EV(i, 1);
       const uint32_t sb = smem_u32(S.ring[slot]);
 
       // ---- S for keys 16c + 8nt + {0..7}: 2 n-tiles x 32 k-steps, 2-way split
@@ -266,6 +279,13 @@ __global__ void __launch_bounds__(NT, 1)
       }
       // ---- softmax on the fragments: x[nt][0,1] head g8, x[nt][2,3] head g8+8,
       //      keys 16c + 8nt + 2q4 + {0,1}
+#ifdef SA_TRACE
+      {  // development builds: wait for S before stamping
+        const float dep = sa[0][0][0] + sa[1][1][3];
+        if (dep == 1.2345e-30f) sa_ws_trace[0][0][0] = 1;
+        if (c == 0 && lane == 0) SA_TRACE_EV(i, 2);
+      }
+#endif
       const uint32_t mw0 = S.mask[slot][0], mw1 = S.mask[slot][1];
       float x[2][4];
       bool over = false;
@@ -331,6 +351,7 @@ __global__ void __launch_bounds__(NT, 1)
         }
       }
       named_bar(3, NCT);  // P of all 64 keys written
+      if (c == 0 && lane == 0) SA_TRACE_EV(i, 3);
 
       // ---- O[16 x 128 cols of this warp] += P[16 x 64] . V[64 x 128]
 #pragma unroll
@@ -354,6 +375,15 @@ __global__ void __launch_bounds__(NT, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&S.empty[slot]));  // slot free for the producer
+#ifdef SA_TRACE
+      {  // development builds: wait for P.V before stamping
+        float dep = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) dep += o[nt][0];
+        if (dep == 1.2345e-30f) sa_ws_trace[0][0][0] = 1;
+        if (c == 0 && lane == 0) SA_TRACE_EV(i, 4);
+      }
+#endif
 
       if (seg_end) {
         // ---------------- epilogue of the segment ending at unit i ----------
@@ -389,6 +419,7 @@ __global__ void __launch_bounds__(NT, 1)
           }
         }
       }
+      if (seg_end && c == 0 && lane == 0) SA_TRACE_EV(i, 5);
       if (seg_end) ++seg;
       seg_first = seg_end;
       if (++kb == upt) {
@@ -405,6 +436,17 @@ __global__ void __launch_bounds__(NT, 1)
 // host side
 // ---------------------------------------------------------------------------
 int ws_unit_keys() { return ws_path::UK; }
+
+#ifdef SA_TRACE
+extern "C" int sa_ws_trace_read(unsigned long long* out, size_t bytes) {
+  if (bytes < sizeof(sa_ws_trace)) return -1;
+  return (int)cudaMemcpyFromSymbol(out, sa_ws_trace, sizeof(sa_ws_trace));
+}
+extern "C" int sa_ws_trace_clear() {
+  static unsigned long long zero[kTraceCtas * kTraceUnits * kTraceEvents] = {};
+  return (int)cudaMemcpyToSymbol(sa_ws_trace, zero, sizeof(zero));
+}
+#endif
 
 int read_ws_error(int* flags) {
   int v = 0;
