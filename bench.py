@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the CPU baseline leg (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--graph", action="store_true",
+                    help="capture one op call in a CUDA graph and time its replays")
     ap.add_argument("--no-launch-count", action="store_true",
                     help="skip the one profiled call that counts our kernel launches")
     return ap.parse_args()
@@ -220,40 +222,50 @@ def cpu_sample_inputs(cfg, rows, seed=0):
     return q, kv, sink, idx, scale, b * cfg.m
 
 
-def cpu_throughput(cfg, rows, min_seconds, max_reps):
+CPU_IMPL = "fp32 torch CPU restatement of reference.py (oracle/sparse_attn_oracle.py)"
+
+
+def cpu_impl():
+    """The reference's algorithm on the host cores, written with the same torch
+    ops as reference.py (the faster CPU form on the GPU hosts: torch's
+    vectorised einsum beats the scalar C restatement in oracle/sa_host.c)."""
     from oracle.sparse_attn_oracle import sparse_attn_oracle
-    torch.set_num_threads(os.cpu_count() or 1)
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    return sparse_attn_oracle, cores
+
+
+def cpu_throughput(cfg, rows, min_seconds, max_reps):
+    fn, cores = cpu_impl()
     q, kv, sink, idx, scale, n = cpu_sample_inputs(cfg, rows)
-    sparse_attn_oracle(q, kv, sink, idx, scale)  # warm-up
+    fn(q, kv, sink, idx, scale)  # warm-up
     reps, t0 = 0, time.perf_counter()
     while True:
-        sparse_attn_oracle(q, kv, sink, idx, scale)
+        fn(q, kv, sink, idx, scale)
         reps += 1
         el = time.perf_counter() - t0
         if el >= min_seconds or reps >= max_reps:
             break
-    return n * reps / el, n, reps, el
+    return n * reps / el, n, reps, el, cores
 
 
 def run_reference(args):
     rank, _, _ = dist_env()
     if rank != 0:
         return
-    from oracle.sparse_attn_oracle import sparse_attn_oracle
     cfg = CONFIGS[args.config]
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    rows = 4
+    fn, cores = cpu_impl()
+    rows = 16
     q, kv, sink, idx, scale, n = cpu_sample_inputs(cfg, rows)
     for _ in range(max(args.warmup, 0)):
-        sparse_attn_oracle(q, kv, sink, idx, scale)
+        fn(q, kv, sink, idx, scale)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        sparse_attn_oracle(q, kv, sink, idx, scale)
+        fn(q, kv, sink, idx, scale)
     el = time.perf_counter() - t0
     val = n * args.steps / el
     sample = (f"{n} query rows of config '{cfg.name}' per step (b=1 slice, kv_len={cfg.kv_len}, "
-              f"topk={cfg.topk}), fp32 torch CPU restatement of reference.py")
+              f"topk={cfg.topk}), {CPU_IMPL}")
     line = {
         "metric": METRIC, "value": val, "unit": UNIT, "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -297,9 +309,20 @@ def main():
     valid = int(((idx >= 0) & (idx < cfg.kv_len)).sum().item())
     gathered = valid * D * 2
 
-    def step():
+    def op_call():
         sparse_attn_out(o, q, kv, sink, idx, SCALE, ws, variant=variant, grid=args.grid,
-                        stream=stream)
+                        stream=torch.cuda.current_stream(dev))
+
+    step = op_call
+    if args.graph:
+        # one op call (forward + combine launches, programmatic dependency kept)
+        # captured once; every step replays it on the timed stream
+        op_call()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            op_call()
+        step = graph.replay
 
     for _ in range(max(args.warmup, 3)):
         flush.zero_()
@@ -388,10 +411,10 @@ def main():
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        val, n, reps, el = cpu_throughput(cfg, rows=16, min_seconds=10.0, max_reps=50)
-        cpu = {"value": val, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-               "sample": f"{n} query rows of '{cfg.name}' x {reps} reps ({el:.1f} s), fp32 "
-                         "torch CPU restatement of reference.py"}
+        val, n, reps, el, cores = cpu_throughput(cfg, rows=16, min_seconds=10.0, max_reps=200)
+        cpu = {"value": val, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"{n} query rows of '{cfg.name}' x {reps} reps ({el:.1f} s), "
+                         f"{CPU_IMPL}"}
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
@@ -402,7 +425,8 @@ def main():
                    "kv_len": cfg.kv_len, "topk": cfg.topk, "global_batch": cfg.b * world,
                    "parallelism": f"rows sharded by batch over {world} GPU(s), no collective",
                    "l2": "flushed (256 MiB write) before every timed step, flush untimed",
-                   "variant": args.variant, "grid": args.grid},
+                   "variant": args.variant, "grid": args.grid,
+                   "launch": "CUDA graph replay" if args.graph else "stream launch"},
         "gathered_kv_gbs": gathered * world * K / (max_total_ms / 1e3) / 1e9,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,

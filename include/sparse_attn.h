@@ -70,6 +70,15 @@ int sa_variant_available(int variant);
  * not the hot path.  No counterpart in the reference. */
 int sa_device_status(int* flags);
 
+/* Debug/health query, synchronous: *count = the number of gathered slots, on
+ * the current device and since the last reset, whose index was neither -1 nor
+ * inside [0, kv_len).  Such slots are masked like -1 (the output never reads
+ * out of bounds); this counter lets a caller detect a faulty index producer.
+ * reset != 0 zeroes the counter after reading it.  Counts only kernels that
+ * have completed.  The reference masks only -1 (track-01/submission.py:313-322)
+ * and leaves other indices undefined. */
+int sa_index_faults(uint64_t* count, int reset);
+
 /* Last cudaError_t observed by this thread inside the library (0 if none). */
 int sa_last_cuda_error(void);
 

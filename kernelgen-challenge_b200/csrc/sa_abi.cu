@@ -23,6 +23,9 @@ int read_tc_error(int* flags);
 cudaError_t launch_ws(const Params& p, cudaStream_t st);
 int ws_unit_keys();
 int read_ws_error(int* flags);
+int read_ws_index_faults(unsigned long long* out, bool reset);
+int read_tc_index_faults(unsigned long long* out, bool reset);
+int read_mma_index_faults(unsigned long long* out, bool reset);
 }  // namespace sa
 
 namespace {
@@ -96,6 +99,17 @@ int sa_device_status(int* flags) {
   if (e == 0) e = sa::read_ws_error(&b);
   if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
   *flags = a != 0 ? a : (b != 0 ? 100 + b : 0);
+  return SA_OK;
+}
+
+int sa_index_faults(uint64_t* count, int reset) {
+  if (count == nullptr) return SA_ERR_INVALID_ARG;
+  unsigned long long total = 0;
+  int e = sa::read_ws_index_faults(&total, reset != 0);
+  if (e == 0) e = sa::read_tc_index_faults(&total, reset != 0);
+  if (e == 0) e = sa::read_mma_index_faults(&total, reset != 0);
+  if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
+  *count = total;
   return SA_OK;
 }
 

@@ -173,6 +173,31 @@ __device__ __forceinline__ bool slot_valid(int64_t key, int64_t topk, int32_t id
   return key < topk && id >= 0 && (int64_t)id < kv_len;
 }
 
+// An index that is neither the -1 sentinel nor inside [0, kv_len) is masked
+// like -1 but also counted: each kernel's translation unit keeps a device
+// counter of such slots (read and reset by sa_index_faults), so a caller can
+// tell its index producer wrote garbage.  Warp-aggregated: one atomic per
+// unit that holds any.
+__device__ __forceinline__ bool index_fault(int32_t id, int64_t kv_len) {
+  return id < -1 || (int64_t)id >= kv_len;
+}
+__device__ __forceinline__ void count_index_faults(unsigned long long* counter, uint32_t n) {
+  if (n != 0u) atomicAdd(counter, (unsigned long long)n);
+}
+// Host side: read (and optionally zero) one translation unit's counter.
+template <typename Sym>
+inline int index_fault_io(const Sym& sym, unsigned long long* out, bool reset) {
+  unsigned long long v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, sym, sizeof(v));
+  if (e == cudaSuccess && reset) {
+    const unsigned long long zero = 0;
+    e = cudaMemcpyToSymbol(sym, &zero, sizeof(zero));
+  }
+  if (e != cudaSuccess) return (int)e;
+  *out += v;
+  return 0;
+}
+
 // Final normalisation with the sink as the (topk+1)-th logit
 // (track-01/reference/reference.py:34-38, submission.py:340-345): the sink adds
 // exp(sink - max) to the denominator and nothing to the numerator.

@@ -28,6 +28,9 @@
 #include "sa_common.cuh"
 
 namespace sa {
+
+__device__ unsigned long long sa_mma_index_faults;  // out-of-range indices seen
+
 namespace mma_path {
 
 constexpr int BN = 32;      // keys per unit
@@ -156,6 +159,11 @@ __global__ void __launch_bounds__(NT, 1) sa_mma_fwd_kernel(const Params p) {
     const int32_t my_id = S.idx[i % IDXR][lane];
     const uint32_t vmask =
         __ballot_sync(0xffffffffu, slot_valid(kb * BN + lane, p.topk, my_id, p.kv_len));
+    if (warp == 0) {
+      const uint32_t f =
+          __ballot_sync(0xffffffffu, kb * BN + lane < p.topk && index_fault(my_id, p.kv_len));
+      if (lane == 0) count_index_faults(&sa_mma_index_faults, __popc(f));
+    }
 
     if (vmask != 0u) {
       const uint32_t kvs = smem_u32(&S.kv[i % STAGES][0][0]);
@@ -405,6 +413,10 @@ cudaError_t launch_combine(const Params& p, cudaStream_t st) {
 }
 
 int mma_unit_keys() { return mma_path::BN; }
+
+int read_mma_index_faults(unsigned long long* out, bool reset) {
+  return index_fault_io(sa_mma_index_faults, out, reset);
+}
 
 size_t mma_smem_bytes() { return sizeof(mma_path::Smem); }
 

@@ -43,6 +43,7 @@
 namespace sa {
 
 __device__ int sa_ws_error;  // nonzero after a bounded wait gave up
+__device__ unsigned long long sa_ws_index_faults;  // out-of-range indices seen
 
 #ifdef SA_TRACE
 // Pipeline timeline for development builds only (-DSA_TRACE): per CTA, per
@@ -185,9 +186,12 @@ __global__ void __launch_bounds__(NT, 1)
       if (warp == 0) {
         const uint32_t ma = __ballot_sync(0xffffffffu, ia >= 0 && (int64_t)ia < p.kv_len);
         const uint32_t mb = __ballot_sync(0xffffffffu, ib >= 0 && (int64_t)ib < p.kv_len);
+        const uint32_t fa = __ballot_sync(0xffffffffu, index_fault(ia, p.kv_len));
+        const uint32_t fb = __ballot_sync(0xffffffffu, index_fault(ib, p.kv_len));
         if (lane == 0) {
           S.mask[slot][0] = ma;
           S.mask[slot][1] = mb;
+          count_index_faults(&sa_ws_index_faults, __popc(fa) + __popc(fb));
         }
       }
       const __nv_bfloat16* kvb = p.kv + cur_tb * p.kv_sb + c * 8;
@@ -447,6 +451,10 @@ extern "C" int sa_ws_trace_clear() {
   return (int)cudaMemcpyToSymbol(sa_ws_trace, zero, sizeof(zero));
 }
 #endif
+
+int read_ws_index_faults(unsigned long long* out, bool reset) {
+  return index_fault_io(sa_ws_index_faults, out, reset);
+}
 
 int read_ws_error(int* flags) {
   int v = 0;

@@ -37,6 +37,7 @@ SIGNATURES = {
     "sa_last_cuda_error": (ctypes.c_int, []),
     "sa_variant_available": (ctypes.c_int, [ctypes.c_int]),
     "sa_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "sa_index_faults": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]),
     "sa_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, ctypes.c_int]),
     "sa_fwd": (ctypes.c_int, _FWD_ARGS),
     "sa_fwd_ex": (ctypes.c_int, _FWD_ARGS + [ctypes.c_int, ctypes.c_int]),
@@ -83,6 +84,14 @@ def device_status() -> int:
     """Error word of the tensor-core kernel on the current device (0 = healthy)."""
     v = ctypes.c_int(0)
     check(lib().sa_device_status(ctypes.byref(v)))
+    return v.value
+
+
+def index_faults(reset: bool = False) -> int:
+    """Slots whose index was neither -1 nor in [0, kv_len), on the current
+    device since the last reset (they were masked like -1)."""
+    v = ctypes.c_uint64(0)
+    check(lib().sa_index_faults(ctypes.byref(v), int(bool(reset))))
     return v.value
 
 

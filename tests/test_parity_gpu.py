@@ -205,3 +205,25 @@ def test_ragged_schedule_rows_of_varying_length(grid):
         o = run_gpu(*args, variant=v, grid=grid)
         assert_close(o, ref, what=f"ragged variant={v} grid={grid}")
         assert torch.count_nonzero(o[0, 7]) == 0 and torch.count_nonzero(o[1, 599]) == 0
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_index_faults_counted(variant):
+    """Indices that are neither -1 nor in [0, kv_len) are masked and counted
+    exactly once per slot; -1 is not counted."""
+    from sparse_attn._lib import index_faults
+    q, kv, sink, idx, scale = make_inputs("plumbing", seed=11)
+    kv_len = kv.shape[1]
+    idx[0, 0, :7] = -1                    # sentinel: masked, not counted
+    idx[0, 1, 3] = -2
+    idx[0, 2, 10:15] = kv_len
+    idx[0, 5, 63] = kv_len + 1000
+    idx[0, 9, 0] = -(2 ** 31)
+    expected = 1 + 5 + 1 + 1
+    torch.cuda.synchronize()
+    index_faults(reset=True)
+    o = run_gpu(q, kv, sink, idx, scale, variant=variant)
+    torch.cuda.synchronize()
+    assert index_faults(reset=True) == expected
+    assert index_faults() == 0
+    assert_close(o, sparse_attn_oracle(q, kv, sink, idx, scale), what="faulty indices")
