@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the CPU baseline leg (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--kv", choices=["bf16", "fp8"], default="bf16",
+                    help="KV cache format: bf16 (the reference's) or e4m3 + fp32 per-token "
+                         "scale (sparse_attn_fp8)")
     ap.add_argument("--graph", action="store_true",
                     help="capture one op call in a CUDA graph and time its replays")
     ap.add_argument("--no-launch-count", action="store_true",
@@ -309,9 +312,21 @@ def main():
     valid = int(((idx >= 0) & (idx < cfg.kv_len)).sum().item())
     gathered = valid * D * 2
 
+    fp8 = args.kv == "fp8"
+    if fp8:
+        # quantised once, outside every timed region, by the library's own kernel
+        kv8, kscale = sparse_attn.quantize_kv_fp8(kv)
+        del kv
+        torch.cuda.synchronize()
+        gathered = valid * (D + 4)  # e4m3 row + its fp32 scale
+
     def op_call():
-        sparse_attn_out(o, q, kv, sink, idx, SCALE, ws, variant=variant, grid=args.grid,
-                        stream=torch.cuda.current_stream(dev))
+        if fp8:
+            sparse_attn.sparse_attn_fp8_out(o, q, kv8, kscale, sink, idx, SCALE, ws,
+                                            grid=args.grid, stream=torch.cuda.current_stream(dev))
+        else:
+            sparse_attn_out(o, q, kv, sink, idx, SCALE, ws, variant=variant, grid=args.grid,
+                            stream=torch.cuda.current_stream(dev))
 
     step = op_call
     if args.graph:
@@ -367,7 +382,8 @@ def main():
         def e2e_step():
             qd = q_h.to(dev, non_blocking=True)
             idd = idx_h.to(dev, non_blocking=True)
-            out = sparse_attn.sparse_attn(qd, kv, sink, idd, SCALE)
+            out = (sparse_attn.sparse_attn_fp8(qd, kv8, kscale, sink, idd, SCALE) if fp8
+                   else sparse_attn.sparse_attn(qd, kv, sink, idd, SCALE))
             o_h.copy_(out, non_blocking=True)
 
         for _ in range(3):
@@ -390,7 +406,8 @@ def main():
                "h2d_bytes_per_step": q_h.numel() * q_h.element_size()
                + idx_h.numel() * idx_h.element_size(),
                "d2h_bytes_per_step": o_h.numel() * o_h.element_size(),
-               "steps": ke, "kv_cache_resident": True, "api": "sparse_attn.sparse_attn"}
+               "steps": ke, "kv_cache_resident": True,
+               "api": "sparse_attn.sparse_attn_fp8" if fp8 else "sparse_attn.sparse_attn"}
 
     if rank != 0:
         if world > 1:
@@ -405,7 +422,8 @@ def main():
     if tpath.exists():
         try:
             tj = json.loads(tpath.read_text())
-            traffic = tj.get(f"{args.config}:{args.variant}", tj.get(args.config))
+            key = f"{args.config}:fp8" if fp8 else f"{args.config}:{args.variant}"
+            traffic = tj.get(key, None if fp8 else tj.get(args.config))
         except Exception:
             traffic = None
 
@@ -419,13 +437,15 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": max_total_ms / K, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 KV (fp32 per-token scale), bf16 q/o" if fp8 else "bf16",
         "data": "synthetic (seeded; q/kv/sink randn on device, distinct indices per row)",
         "config": {"workload": cfg.name, "b": cfg.b, "m": cfg.m, "h": H, "d": D,
                    "kv_len": cfg.kv_len, "topk": cfg.topk, "global_batch": cfg.b * world,
                    "parallelism": f"rows sharded by batch over {world} GPU(s), no collective",
                    "l2": "flushed (256 MiB write) before every timed step, flush untimed",
-                   "variant": args.variant, "grid": args.grid,
+                   "variant": "fp8" if fp8 else args.variant, "grid": args.grid,
+                   "kv_cache": "e4m3 + fp32 per-token scale" if fp8 else "bf16",
                    "launch": "CUDA graph replay" if args.graph else "stream launch"},
         "gathered_kv_gbs": gathered * world * K / (max_total_ms / 1e3) / 1e9,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -433,8 +453,9 @@ def main():
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)"
                      if peak_kind == "measured" else "fallback 6650 GB/s",
                      "algorithmic_bytes_per_step": gathered,
-                     "note": "achieved = valid gathered KV bytes / mean event time of one op "
-                             "call (main + combine kernels)"},
+                     "note": "achieved = valid gathered KV bytes (" + ("516" if fp8 else "1024")
+                             + " per slot) / mean event time of one op call (main + combine "
+                             "kernels)"},
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": None if per_call is None else per_call * K,

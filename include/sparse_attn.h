@@ -63,9 +63,35 @@ const char* sa_strerror(int code);
  * the reference (its backend probe is track-01/submission.py:927-969). */
 int sa_variant_available(int variant);
 
+/* fp8 KV cache.  kv8 is [b, kv_len, 512] e4m3 (torch.float8_e4m3fn) bytes,
+ * kv_scale is [b, kv_len] fp32, and row t of batch b stands for the bf16 row
+ * kv8[b,t,:] * kv_scale[b,t].  The result is sa_fwd on that dequantised cache,
+ * computed with e4m3 tensor-core MMAs.  Q and P are split into two e4m3 terms,
+ * so accuracy stays close to the bf16 path.  kv_strides are in bytes (rows
+ * 16-byte aligned); kv_scale_strides are in elements.  The workspace is sized
+ * by sa_workspace_bytes.  grid_ctas = 0 picks one CTA per SM.  q must be
+ * 16-byte aligned (it is loaded by TMA).  The gathered bytes per slot are 516
+ * instead of 1024.  The reference has no fp8 cache; this replaces
+ * track-01/submission.py:975-1021 for callers that keep one. */
+int sa_fwd_fp8(const void* q, const void* kv8, const float* kv_scale, const float* sink,
+               const int32_t* idx, void* o, int64_t b, int64_t m, int64_t h, int64_t d,
+               int64_t kv_len, int64_t topk, const int64_t q_strides[4],
+               const int64_t kv_strides[3], const int64_t kv_scale_strides[2],
+               const int64_t idx_strides[3], const int64_t o_strides[4], float scale,
+               void* workspace, size_t workspace_bytes, void* stream, int grid_ctas);
+
+/* Quantises a bf16 cache [b, kv_len, 512] to the layout sa_fwd_fp8 reads.  Per
+ * row: amax = max |x|, kv8 = e4m3_rn_satfinite(x * (448 / amax)),
+ * kv_scale = amax / 448; an all-zero row gives zeros and scale 0.  Strides are
+ * in elements of each tensor.  Stream-ordered and allocation-free.  No
+ * counterpart in the reference. */
+int sa_quantize_kv_fp8(const void* kv, void* kv8, float* kv_scale, int64_t b, int64_t kv_len,
+                       int64_t d, const int64_t kv_strides[3], const int64_t kv8_strides[3],
+                       const int64_t kv_scale_strides[2], void* stream);
+
 /* Debug/health query, synchronous: copies into *flags the error word that the
  * pipelined kernels (SA_VARIANT_TCGEN05, SA_VARIANT_WS; the latter reported
- * as 100 + code) set on the current device when one of their bounded
+ * as 100 + code, sa_fwd_fp8 as 200 + code) set on the current device when one of their bounded
  * pipeline waits gave up (0 = never).  Intended for tests and health checks,
  * not the hot path.  No counterpart in the reference. */
 int sa_device_status(int* flags);

@@ -26,6 +26,18 @@ int read_ws_error(int* flags);
 int read_ws_index_faults(unsigned long long* out, bool reset);
 int read_tc_index_faults(unsigned long long* out, bool reset);
 int read_mma_index_faults(unsigned long long* out, bool reset);
+cudaError_t launch_fp8(const Params& p, cudaStream_t st);
+int fp8_unit_keys();
+int read_fp8_error(int* flags);
+int read_fp8_index_faults(unsigned long long* out, bool reset);
+struct QuantParams {
+  const __nv_bfloat16* kv;
+  uint8_t* kv8;
+  float* kscale;
+  int64_t b, kv_len;
+  int64_t kv_sb, kv_sn, o_sb, o_sn, s_sb, s_sn;
+};
+cudaError_t launch_quantize_fp8(const QuantParams& qp, int sms, cudaStream_t st);
 }  // namespace sa
 
 namespace {
@@ -94,11 +106,12 @@ int sa_last_cuda_error(void) { return t_last_cuda_error; }
 
 int sa_device_status(int* flags) {
   if (flags == nullptr) return SA_ERR_INVALID_ARG;
-  int a = 0, b = 0;
+  int a = 0, b = 0, f = 0;
   int e = sa::read_tc_error(&a);
   if (e == 0) e = sa::read_ws_error(&b);
+  if (e == 0) e = sa::read_fp8_error(&f);
   if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
-  *flags = a != 0 ? a : (b != 0 ? 100 + b : 0);
+  *flags = a != 0 ? a : (b != 0 ? 100 + b : (f != 0 ? 200 + f : 0));
   return SA_OK;
 }
 
@@ -108,6 +121,7 @@ int sa_index_faults(uint64_t* count, int reset) {
   int e = sa::read_ws_index_faults(&total, reset != 0);
   if (e == 0) e = sa::read_tc_index_faults(&total, reset != 0);
   if (e == 0) e = sa::read_mma_index_faults(&total, reset != 0);
+  if (e == 0) e = sa::read_fp8_index_faults(&total, reset != 0);
   if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
   *count = total;
   return SA_OK;
@@ -232,6 +246,121 @@ int sa_fwd_ex(const void* q, const void* kv, const float* sink, const int32_t* i
   e = (variant == SA_VARIANT_MMA)       ? sa::launch_mma(p, st)
       : (variant == SA_VARIANT_TCGEN05) ? sa::launch_tc(p, st)
                                         : sa::launch_ws(p, st);
+  if (e != cudaSuccess) return fail_cuda(e);
+  return SA_OK;
+}
+
+int sa_fwd_fp8(const void* q, const void* kv8, const float* kv_scale, const float* sink,
+               const int32_t* idx, void* o, int64_t b, int64_t m, int64_t h, int64_t d,
+               int64_t kv_len, int64_t topk, const int64_t q_strides[4],
+               const int64_t kv_strides[3], const int64_t kv_scale_strides[2],
+               const int64_t idx_strides[3], const int64_t o_strides[4], float scale,
+               void* workspace, size_t workspace_bytes, void* stream, int grid_ctas) {
+  t_last_cuda_error = 0;
+  if (b < 0 || m < 0 || kv_len < 0 || topk < 0) return SA_ERR_INVALID_ARG;
+  if (h != sa::kHeads || d != sa::kDim) return SA_ERR_UNSUPPORTED;
+  if (b == 0 || m == 0) return SA_OK;
+  if (!q || !kv8 || !kv_scale || !sink || !idx || !o || !q_strides || !kv_strides ||
+      !kv_scale_strides || !idx_strides || !o_strides)
+    return SA_ERR_INVALID_ARG;
+  if (q_strides[3] != 1 || kv_strides[2] != 1 || o_strides[3] != 1) return SA_ERR_INVALID_ARG;
+  if (!aligned16(q) || !aligned16(kv8) || !aligned16(o)) return SA_ERR_INVALID_ARG;
+  for (int i = 0; i < 3; ++i)
+    if ((q_strides[i] % 8) != 0 || (o_strides[i] % 8) != 0) return SA_ERR_INVALID_ARG;
+  for (int i = 0; i < 2; ++i)  // e4m3 rows: byte strides, 16-byte aligned
+    if ((kv_strides[i] % 16) != 0) return SA_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(idx) & 3u) != 0 ||
+      (reinterpret_cast<uintptr_t>(kv_scale) & 3u) != 0)
+    return SA_ERR_INVALID_ARG;
+  if (kv_len > INT32_MAX) return SA_ERR_INVALID_ARG;
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e);
+  const DeviceInfo* di = device_info(dev);
+  if (di == nullptr) return SA_ERR_UNSUPPORTED;
+  if (di->err != cudaSuccess) return fail_cuda(di->err);
+  if (di->major != 10 || !sa::tc_available()) return SA_ERR_UNSUPPORTED;
+
+  sa::Params p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.kv = static_cast<const __nv_bfloat16*>(kv8);  // e4m3 bytes
+  p.kscale = kv_scale;
+  p.sink = sink;
+  p.idx = idx;
+  p.o = static_cast<__nv_bfloat16*>(o);
+  p.b = b;
+  p.m = m;
+  p.kv_len = kv_len;
+  p.topk = topk;
+  p.q_sb = q_strides[0];
+  p.q_sm = q_strides[1];
+  p.q_sh = q_strides[2];
+  p.kv_sb = kv_strides[0];
+  p.kv_sn = kv_strides[1];
+  p.ks_sb = kv_scale_strides[0];
+  p.ks_sn = kv_scale_strides[1];
+  p.i_sb = idx_strides[0];
+  p.i_sm = idx_strides[1];
+  p.i_sk = idx_strides[2];
+  p.o_sb = o_strides[0];
+  p.o_sm = o_strides[1];
+  p.o_sh = o_strides[2];
+  p.scale_log2 = scale * sa::kLog2e;
+  if (!sa::tc_supports(p)) return SA_ERR_UNSUPPORTED;
+  p.upt = ceil_div(topk > 0 ? topk : 1, sa::fp8_unit_keys());
+  p.units = b * m * p.upt;
+  int64_t grid = grid_ctas > 0 ? grid_ctas : (int64_t)di->sms;
+  if (grid > max_grid(di->sms)) grid = max_grid(di->sms);
+  if (grid > p.units) grid = p.units;
+  p.grid = static_cast<int>(grid);
+
+  const size_t need = sa::workspace_bytes_for_grid(p.grid);
+  if (workspace == nullptr || workspace_bytes < need) return SA_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return SA_ERR_INVALID_ARG;
+  char* ws = static_cast<char*>(workspace);
+  p.part_acc = reinterpret_cast<float*>(ws);
+  p.part_ml = reinterpret_cast<float*>(ws + sa::ws_acc_bytes(p.grid));
+  e = sa::launch_fp8(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail_cuda(e);
+  return SA_OK;
+}
+
+int sa_quantize_kv_fp8(const void* kv, void* kv8, float* kv_scale, int64_t b, int64_t kv_len,
+                       int64_t d, const int64_t kv_strides[3], const int64_t kv8_strides[3],
+                       const int64_t kv_scale_strides[2], void* stream) {
+  t_last_cuda_error = 0;
+  if (b < 0 || kv_len < 0) return SA_ERR_INVALID_ARG;
+  if (d != sa::kDim) return SA_ERR_UNSUPPORTED;
+  if (b == 0 || kv_len == 0) return SA_OK;
+  if (!kv || !kv8 || !kv_scale || !kv_strides || !kv8_strides || !kv_scale_strides)
+    return SA_ERR_INVALID_ARG;
+  if (kv_strides[2] != 1 || kv8_strides[2] != 1) return SA_ERR_INVALID_ARG;
+  if (!aligned16(kv) || (reinterpret_cast<uintptr_t>(kv8) & 7u) != 0 ||
+      (reinterpret_cast<uintptr_t>(kv_scale) & 3u) != 0)
+    return SA_ERR_INVALID_ARG;
+  for (int i = 0; i < 2; ++i)
+    if ((kv_strides[i] % 8) != 0 || (kv8_strides[i] % 8) != 0) return SA_ERR_INVALID_ARG;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e);
+  const DeviceInfo* di = device_info(dev);
+  if (di == nullptr) return SA_ERR_UNSUPPORTED;
+  if (di->err != cudaSuccess) return fail_cuda(di->err);
+  if (di->major != 10) return SA_ERR_UNSUPPORTED;
+  sa::QuantParams qp{};
+  qp.kv = static_cast<const __nv_bfloat16*>(kv);
+  qp.kv8 = static_cast<uint8_t*>(kv8);
+  qp.kscale = kv_scale;
+  qp.b = b;
+  qp.kv_len = kv_len;
+  qp.kv_sb = kv_strides[0];
+  qp.kv_sn = kv_strides[1];
+  qp.o_sb = kv8_strides[0];
+  qp.o_sn = kv8_strides[1];
+  qp.s_sb = kv_scale_strides[0];
+  qp.s_sn = kv_scale_strides[1];
+  e = sa::launch_quantize_fp8(qp, di->sms, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail_cuda(e);
   return SA_OK;
 }

@@ -52,6 +52,10 @@ struct Params {
   int64_t upt;       // units per token
   int64_t units;     // tokens * upt
   int grid;
+  // fp8 KV cache only (sa_fwd_fp8): kv holds e4m3 bytes (kv_sb, kv_sn in
+  // bytes) and row t of batch b dequantises as kv8[b,t,:] * kscale[b,t]
+  const float* kscale;
+  int64_t ks_sb, ks_sn;
 };
 
 // Workspace layout shared by the host (sizing) and the kernels.

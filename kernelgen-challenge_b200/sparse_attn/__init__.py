@@ -8,6 +8,8 @@ in hand-written sm_100a kernels in ``libsparse_attn.so`` (C ABI:
 from ._lib import (SA_VARIANT_AUTO, SA_VARIANT_MMA, SA_VARIANT_TCGEN05,  # noqa: F401
                    SA_VARIANT_WS, LIB_PATH, lib)
 from .op import sparse_attn, sparse_attn_out, workspace_bytes  # noqa: F401
+from .fp8 import quantize_kv_fp8, sparse_attn_fp8, sparse_attn_fp8_out  # noqa: F401
 
 __all__ = ["sparse_attn", "sparse_attn_out", "workspace_bytes", "lib", "LIB_PATH",
+           "quantize_kv_fp8", "sparse_attn_fp8", "sparse_attn_fp8_out",
            "SA_VARIANT_AUTO", "SA_VARIANT_MMA", "SA_VARIANT_TCGEN05", "SA_VARIANT_WS"]

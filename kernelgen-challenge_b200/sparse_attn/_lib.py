@@ -42,6 +42,11 @@ SIGNATURES = {
     "sa_fwd": (ctypes.c_int, _FWD_ARGS),
     "sa_fwd_ex": (ctypes.c_int, _FWD_ARGS + [ctypes.c_int, ctypes.c_int]),
     "sa_fwd_noalloc": (ctypes.c_int, _FWD_ARGS[:16] + [_P, ctypes.c_int]),
+    "sa_fwd_fp8": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
+                                  _I64P, _I64P, _I64P, _I64P, _I64P, ctypes.c_float, _P,
+                                  ctypes.c_size_t, _P, ctypes.c_int]),
+    "sa_quantize_kv_fp8": (ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _I64P, _I64P, _I64P,
+                                          _P]),
 }
 
 _lock = threading.Lock()

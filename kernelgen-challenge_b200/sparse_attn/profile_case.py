@@ -1,11 +1,12 @@
 """Profiling driver: three L2-flushed calls of one configuration.
 
-    python -m sparse_attn.profile_case <config> [variant]
+    python -m sparse_attn.profile_case <config> [variant | fp8]
 
 Counterpart of the reference's ``track-01/profile.py`` (torch.profiler
 timeline, :19-33); here it is the target program for ``ncu`` captures
 (``-s 1 -c 1`` selects the second call).  Inputs are seeded and made on the
-GPU; ``variant`` is an SA_VARIANT_* number (0 = automatic).
+GPU; ``variant`` is an SA_VARIANT_* number (0 = automatic), or ``fp8`` for
+the e4m3 KV-cache kernel (the cache quantised on the GPU before the calls).
 """
 from __future__ import annotations
 
@@ -13,14 +14,15 @@ import sys
 
 import torch
 
-from . import sparse_attn_out, workspace_bytes
+from . import quantize_kv_fp8, sparse_attn_fp8_out, sparse_attn_out, workspace_bytes
 from .workloads import CONFIGS, D, H, SCALE, make_indices
 
 
 def main(argv=None):
     argv = sys.argv[1:] if argv is None else argv
     cfg = CONFIGS[argv[0] if argv else "decode"]
-    variant = int(argv[1]) if len(argv) > 1 else 0
+    fp8 = len(argv) > 1 and argv[1] == "fp8"
+    variant = int(argv[1]) if len(argv) > 1 and not fp8 else 0
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
     q = torch.randn(cfg.b, cfg.m, H, D, generator=g, device=dev, dtype=torch.bfloat16)
@@ -30,9 +32,15 @@ def main(argv=None):
     o = torch.empty_like(q)
     ws = torch.empty(workspace_bytes(cfg.b, cfg.m, cfg.topk, 0), dtype=torch.uint8, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    if fp8:
+        kv8, ks = quantize_kv_fp8(kv)
+        del kv
     for _ in range(3):
         flush.zero_()
-        sparse_attn_out(o, q, kv, sink, idx, SCALE, ws, variant=variant)
+        if fp8:
+            sparse_attn_fp8_out(o, q, kv8, ks, sink, idx, SCALE, ws)
+        else:
+            sparse_attn_out(o, q, kv, sink, idx, SCALE, ws, variant=variant)
     torch.cuda.synchronize()
     print(f"{cfg.name}: mean |o| = {o.float().abs().mean().item():.5f}")
 

@@ -40,7 +40,8 @@ from __future__ import annotations
 
 import torch
 
-__all__ = ["sparse_attn_oracle", "valid_slot_count"]
+__all__ = ["sparse_attn_oracle", "valid_slot_count", "quantize_kv_fp8_ref", "dequantize_kv_fp8",
+           "sparse_attn_fp8_oracle"]
 
 
 def _chunk_rows(m: int, topk: int, d: int, budget_bytes: int = 1 << 30) -> int:
@@ -102,3 +103,36 @@ def valid_slot_count(topk_idxs, kv_len: int) -> int:
     """Number of slots whose row is actually gathered (index in [0, kv_len))."""
     idx = topk_idxs
     return int(((idx >= 0) & (idx < kv_len)).sum().item())
+
+
+# ---------------------------------------------------------------------------
+# fp8 (e4m3) KV cache with one fp32 scale per token.  The reference has no fp8
+# cache; its semantics here are the reference op on the dequantised cache.
+# ---------------------------------------------------------------------------
+E4M3_MAX = 448.0
+
+
+@torch.no_grad()
+def quantize_kv_fp8_ref(kv):
+    """CPU statement of the quantiser: per row amax = max|x|,
+    kv8 = e4m3_rn(x * (448 / amax)), scale = amax / 448 (zero rows: 0, 0)."""
+    x = kv.cpu().float()
+    amax = x.abs().amax(dim=-1)
+    # a correctly rounded fp32 division (torch evaluates `float / tensor` as a
+    # reciprocal followed by a product: two roundings)
+    inv = torch.where(amax > 0, torch.full_like(amax, E4M3_MAX) / amax, torch.zeros_like(amax))
+    kv8 = (x * inv.unsqueeze(-1)).to(torch.float8_e4m3fn)
+    return kv8, amax / E4M3_MAX
+
+
+def dequantize_kv_fp8(kv8, kv_scale):
+    """fp32 cache rows: kv8[b, t, :] * kv_scale[b, t]."""
+    return kv8.cpu().float() * kv_scale.cpu().float().unsqueeze(-1)
+
+
+def sparse_attn_fp8_oracle(q, kv8, kv_scale, attn_sink, topk_idxs, scale, **kw):
+    """The reference's algorithm (``sparse_attn_oracle``) on the dequantised
+    fp32 cache; reference.py:32 widens kv to fp32 first, so an fp32 cache
+    enters its arithmetic unchanged."""
+    return sparse_attn_oracle(q, dequantize_kv_fp8(kv8, kv_scale), attn_sink, topk_idxs,
+                              scale, **kw)

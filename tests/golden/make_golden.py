@@ -32,6 +32,7 @@ import torch
 
 HERE = pathlib.Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent.parent / "kernelgen-challenge_b200"))
+sys.path.insert(0, str(HERE.parent.parent))
 
 from sparse_attn.workloads import SCALE, make_inputs  # noqa: E402
 
@@ -85,6 +86,27 @@ def make_case(name):
 
 CASES = ["plumbing", "ragged", "replacement", "masked", "out_of_range", "short", "causal_head"]
 
+# fp8 cache cases: the bf16 case's cache quantised by the quantiser's CPU
+# statement (oracle/sparse_attn_oracle.py:quantize_kv_fp8_ref); the expected
+# output is the reference run on the dequantised fp32 cache.
+FP8_CASES = ["fp8_plumbing", "fp8_masked", "fp8_causal_head"]
+
+
+def make_fp8_case(name):
+    """(q, kv8, kv_scale, sink, idx, scale) of fp8 golden case ``name``."""
+    from oracle.sparse_attn_oracle import quantize_kv_fp8_ref
+    q, kv, sink, idx, scale = make_case(name[len("fp8_"):])
+    kv8, ks = quantize_kv_fp8_ref(kv)
+    return q, kv8, ks, sink, idx, scale
+
+
+def input_digest_fp8(q, kv8, ks, sink, idx, scale) -> str:
+    h = hashlib.sha256()
+    for t in (q.view(torch.int16), kv8.view(torch.uint8), ks, sink, idx):
+        h.update(t.contiguous().numpy().tobytes())
+    h.update(repr(float(scale)).encode())
+    return h.hexdigest()
+
 
 def input_digest(q, kv, sink, idx, scale) -> str:
     h = hashlib.sha256()
@@ -126,6 +148,13 @@ def main():
         o = reference_output(ref, q, kv, sink, idx, scale)
         np.savez_compressed(HERE / f"{name}.npz", o=o.view(torch.int16).numpy(),
                             digest=np.array(input_digest(q, kv, sink, idx, scale)))
+        print(name, tuple(o.shape), "finite:", bool(torch.isfinite(o.float()).all()))
+    from oracle.sparse_attn_oracle import dequantize_kv_fp8
+    for name in FP8_CASES:
+        q, kv8, ks, sink, idx, scale = make_fp8_case(name)
+        o = reference_output(ref, q, dequantize_kv_fp8(kv8, ks), sink, idx, scale)
+        np.savez_compressed(HERE / f"{name}.npz", o=o.view(torch.int16).numpy(),
+                            digest=np.array(input_digest_fp8(q, kv8, ks, sink, idx, scale)))
         print(name, tuple(o.shape), "finite:", bool(torch.isfinite(o.float()).all()))
 
 

@@ -36,3 +36,12 @@ def assert_close(actual, expected, atol=ATOL, rtol=RTOL, what=""):
         raise AssertionError(f"{what}: {bad} of {ok.numel()} elements outside "
                              f"atol={atol} rtol={rtol}; max|d|={diff.max().item():.3e}")
     return diff.max().item()
+
+
+def load_golden_fp8(name):
+    import make_golden
+    args = make_golden.make_fp8_case(name)
+    z = np.load(GOLDEN / f"{name}.npz")
+    assert str(z["digest"]) == make_golden.input_digest_fp8(*args), \
+        f"golden inputs of {name!r} no longer reproduce (generator drift)"
+    return args, torch.from_numpy(z["o"]).view(torch.bfloat16)

@@ -76,3 +76,35 @@ def test_sink_only_scales_output():
     s = torch.einsum("bmhd,bmtd->bmht", q.float(), g) * scale
     plain = torch.einsum("bmht,bmtd->bmhd", torch.softmax(s, -1), g)
     assert torch.allclose(lo, plain, atol=1e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("name", make_golden.FP8_CASES)
+def test_fp8_oracle_matches_golden(name):
+    """The fp8-cache oracle is the reference's algorithm on the dequantised
+    cache: equal to the live reference's output on that cache."""
+    from helpers import load_golden_fp8
+    from oracle.sparse_attn_oracle import sparse_attn_fp8_oracle
+    args, o_gold = load_golden_fp8(name)
+    o = sparse_attn_fp8_oracle(*args)
+    if name == "fp8_plumbing":
+        assert torch.equal(o.view(torch.int16), o_gold.view(torch.int16))
+    else:
+        assert_within_one_ulp(o, o_gold)
+
+
+def test_fp8_quantiser_statement():
+    """Dequantised rows are within half an e4m3 step (2^-4 relative to the
+    row's amax at most) of the bf16 rows; zero rows give scale 0."""
+    from oracle.sparse_attn_oracle import dequantize_kv_fp8, quantize_kv_fp8_ref
+    g = torch.Generator().manual_seed(5)
+    kv = (torch.randn(2, 40, 512, generator=g) *
+          torch.logspace(-3, 3, 40).view(1, 40, 1)).to(torch.bfloat16)
+    kv[1, 7] = 0
+    kv8, sc = quantize_kv_fp8_ref(kv)
+    assert kv8.dtype == torch.float8_e4m3fn and sc.shape == (2, 40)
+    x = kv.float()
+    amax = x.abs().amax(-1, keepdim=True)
+    err = (dequantize_kv_fp8(kv8, sc) - x).abs()
+    assert bool((err <= amax * 2.0 ** -4 + 1e-30).all())
+    assert float(kv8[0].float().abs().max()) == 448.0
+    assert float(sc[1, 7]) == 0.0 and bool((kv8[1, 7].float() == 0).all())
