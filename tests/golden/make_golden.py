@@ -100,6 +100,38 @@ def make_fp8_case(name):
     return q, kv8, ks, sink, idx, scale
 
 
+# hc_split_sinkhorn (track-02) cases: shapes of track-02/workloads.py:21-26
+# (one decode and one prefill shape) plus a ragged one
+HC_CASES = {"hc_decode": (64, 1), "hc_prefill": (4, 1024), "hc_ragged": (3, 37)}
+
+
+def make_hc_case(name, seed=0):
+    """(mixes, hc_scale, hc_base) of hc case ``name``: N(0,1) fp32 like
+    track-02/workloads.py:32-37, from a seeded CPU generator."""
+    b, s = HC_CASES[name]
+    g = torch.Generator().manual_seed(100 + seed + len(name))
+    mixes = torch.randn(b, s, 24, generator=g)
+    hc_scale = torch.randn(3, generator=g)
+    hc_base = torch.randn(24, generator=g)
+    return mixes, hc_scale, hc_base
+
+
+def input_digest_hc(mixes, hc_scale, hc_base) -> str:
+    h = hashlib.sha256()
+    for t in (mixes, hc_scale, hc_base):
+        h.update(t.contiguous().numpy().tobytes())
+    return h.hexdigest()
+
+
+def _load_hc_reference():
+    root = pathlib.Path(os.environ.get("SPARSE_ATTN_REFERENCE", "/root/reference"))
+    path = root / "track-02" / "reference" / "reference.py"
+    spec = importlib.util.spec_from_file_location("kernelgen_track02_reference", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.hc_split_sinkhorn
+
+
 def input_digest_fp8(q, kv8, ks, sink, idx, scale) -> str:
     h = hashlib.sha256()
     for t in (q.view(torch.int16), kv8.view(torch.uint8), ks, sink, idx):
@@ -156,6 +188,13 @@ def main():
         np.savez_compressed(HERE / f"{name}.npz", o=o.view(torch.int16).numpy(),
                             digest=np.array(input_digest_fp8(q, kv8, ks, sink, idx, scale)))
         print(name, tuple(o.shape), "finite:", bool(torch.isfinite(o.float()).all()))
+    hc_ref = _load_hc_reference()
+    for name in HC_CASES:
+        mixes, sc, base = make_hc_case(name)
+        pre, post, comb = hc_ref(mixes, sc, base, 4, 20, 1e-6)
+        np.savez_compressed(HERE / f"{name}.npz", pre=pre.numpy(), post=post.numpy(),
+                            comb=comb.numpy(), digest=np.array(input_digest_hc(mixes, sc, base)))
+        print(name, tuple(comb.shape))
 
 
 if __name__ == "__main__":

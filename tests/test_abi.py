@@ -13,12 +13,17 @@ import torch
 import sparse_attn
 from sparse_attn import _lib
 
-HEADER = pathlib.Path(__file__).resolve().parent.parent / "include" / "sparse_attn.h"
+INCLUDE = pathlib.Path(__file__).resolve().parent.parent / "include"
+# headers of libsparse_attn.so (sparse_attn_host.h belongs to the oracle's library)
+HEADERS = [INCLUDE / "sparse_attn.h", INCLUDE / "hc_sinkhorn.h"]
 
 
 def declared_functions():
-    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
-    return sorted(set(re.findall(r"\b(sa_[a-z_]+)\s*\(", text)))
+    names = set()
+    for hdr in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", hdr.read_text(), flags=re.S)
+        names |= set(re.findall(r"\b((?:sa|hcs)_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
 
 
 def test_library_builds_and_loads():
