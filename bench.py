@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--kv", choices=["bf16", "fp8"], default="bf16",
                     help="KV cache format: bf16 (the reference's) or e4m3 + fp32 per-token "
                          "scale (sparse_attn_fp8)")
+    ap.add_argument("--op", choices=["sparse_attn", "hc_sinkhorn"], default="sparse_attn",
+                    help="hc_sinkhorn: the track-02 op on its 1k-1-64 prefill shape")
     ap.add_argument("--graph", action="store_true",
                     help="capture one op call in a CUDA graph and time its replays")
     ap.add_argument("--no-launch-count", action="store_true",
@@ -286,8 +288,72 @@ def run_reference(args):
 # ----------------------------------------------------------------------------
 # GPU leg
 # ----------------------------------------------------------------------------
+def run_hc_sinkhorn(args):
+    """hc_split_sinkhorn (track-02) on the 1k-1-64 prefill shape [64, 1024, 24]
+    (track-02/workloads.py:25), tokens/s; 192 algorithmic bytes per token
+    (24 fp32 in, 24 out).  The CPU leg times the torch restatement of
+    track-02/reference/reference.py."""
+    b, s_ = 64, 1024
+    if args.impl == "reference":
+        from oracle.hc_sinkhorn_oracle import hc_split_sinkhorn_oracle
+        torch.set_num_threads(os.cpu_count() or 1)
+        g = torch.Generator().manual_seed(0)
+        mixes, sc, base = torch.randn(b, s_, 24, generator=g), torch.randn(3, generator=g), \
+            torch.randn(24, generator=g)
+        for _ in range(max(args.warmup, 0)):
+            hc_split_sinkhorn_oracle(mixes, sc, base)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            hc_split_sinkhorn_oracle(mixes, sc, base)
+        el = time.perf_counter() - t0
+        val = b * s_ * args.steps / el
+        print(json.dumps({"metric": "hc_split_sinkhorn tokens/s", "value": val, "unit": "tokens/s",
+                          "impl": "reference", "n_gpus": args.gpus, "steps": args.steps,
+                          "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+                          "cpu_baseline": {"value": val, "unit": "tokens/s",
+                                           "cores": os.cpu_count(), "kind": "port",
+                                           "sample": "full [64,1024,24] per step"},
+                          "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    import sparse_attn
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    mixes = torch.randn(b, s_, 24, generator=g, device=dev)
+    sc, base = torch.randn(3, generator=g, device=dev), torch.randn(24, generator=g, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        sparse_attn.hc_split_sinkhorn(mixes, sc, base)
+    K = args.steps
+    st = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    en = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    torch.cuda.synchronize()
+    for k in range(K):
+        flush.zero_()
+        st[k].record(stream)
+        sparse_attn.hc_split_sinkhorn(mixes, sc, base)
+        en[k].record(stream)
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(e) for a, e in zip(st, en)) / K
+    tokens = b * s_
+    peak, kind = measured_peaks()
+    achieved = tokens * 192 / (ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "hc_split_sinkhorn tokens/s", "value": tokens / (ms / 1e3), "unit": "tokens/s",
+        "n_gpus": 1, "steps": K, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "dtype": "f32", "data": "synthetic (seeded randn)",
+        "config": {"workload": "track-02 1k-1-64 prefill", "shape": [b, s_, 24],
+                   "l2": "flushed before every timed step, flush untimed"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "note": "192 algorithmic bytes per token"}}),
+        flush=True)
+
+
 def main():
     args = parse()
+    if args.op == "hc_sinkhorn":
+        return run_hc_sinkhorn(args)
     if args.impl == "reference":
         return run_reference(args)
 
