@@ -38,6 +38,9 @@ struct QuantParams {
   int64_t kv_sb, kv_sn, o_sb, o_sn, s_sb, s_sn;
 };
 cudaError_t launch_quantize_fp8(const QuantParams& qp, int sms, cudaStream_t st);
+cudaError_t launch_bwd(const Params& f, const __nv_bfloat16* dout, __nv_bfloat16* dq, float* dkv,
+                       float* dsink, int64_t dkv_sb, int64_t dkv_sn, float scale,
+                       cudaStream_t st);
 }  // namespace sa
 
 namespace {
@@ -322,6 +325,64 @@ int sa_fwd_fp8(const void* q, const void* kv8, const float* kv_scale, const floa
   p.part_acc = reinterpret_cast<float*>(ws);
   p.part_ml = reinterpret_cast<float*>(ws + sa::ws_acc_bytes(p.grid));
   e = sa::launch_fp8(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail_cuda(e);
+  return SA_OK;
+}
+
+int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx, const void* o,
+           const void* dout, void* dq, float* dkv, float* dsink, int64_t b, int64_t m, int64_t h,
+           int64_t d, int64_t kv_len, int64_t topk, const int64_t q_strides[4],
+           const int64_t kv_strides[3], const int64_t idx_strides[3], const int64_t o_strides[4],
+           const int64_t dkv_strides[3], float scale, void* stream) {
+  t_last_cuda_error = 0;
+  if (b < 0 || m < 0 || kv_len < 0 || topk < 0) return SA_ERR_INVALID_ARG;
+  if (h != sa::kHeads || d != sa::kDim) return SA_ERR_UNSUPPORTED;
+  if (b == 0 || m == 0) return SA_OK;
+  if (!q || !kv || !sink || !idx || !o || !dout || !dq || !dkv || !dsink || !q_strides ||
+      !kv_strides || !idx_strides || !o_strides || !dkv_strides)
+    return SA_ERR_INVALID_ARG;
+  if (q_strides[3] != 1 || kv_strides[2] != 1 || o_strides[3] != 1 || dkv_strides[2] != 1)
+    return SA_ERR_INVALID_ARG;
+  if (!aligned16(q) || !aligned16(kv) || !aligned16(o) || !aligned16(dout) || !aligned16(dq) ||
+      (reinterpret_cast<uintptr_t>(dkv) & 7u) != 0 || (reinterpret_cast<uintptr_t>(idx) & 3u) != 0)
+    return SA_ERR_INVALID_ARG;
+  for (int i = 0; i < 3; ++i)
+    if ((q_strides[i] % 8) != 0 || (o_strides[i] % 8) != 0) return SA_ERR_INVALID_ARG;
+  for (int i = 0; i < 2; ++i)
+    if ((kv_strides[i] % 8) != 0 || (dkv_strides[i] % 2) != 0) return SA_ERR_INVALID_ARG;
+  if (kv_len > INT32_MAX || b * m > INT32_MAX) return SA_ERR_INVALID_ARG;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e);
+  const DeviceInfo* di = device_info(dev);
+  if (di == nullptr) return SA_ERR_UNSUPPORTED;
+  if (di->err != cudaSuccess) return fail_cuda(di->err);
+  if (di->major != 10) return SA_ERR_UNSUPPORTED;
+  sa::Params p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.kv = static_cast<const __nv_bfloat16*>(kv);
+  p.sink = sink;
+  p.idx = idx;
+  p.o = static_cast<__nv_bfloat16*>(const_cast<void*>(o));
+  p.b = b;
+  p.m = m;
+  p.kv_len = kv_len;
+  p.topk = topk;
+  p.q_sb = q_strides[0];
+  p.q_sm = q_strides[1];
+  p.q_sh = q_strides[2];
+  p.kv_sb = kv_strides[0];
+  p.kv_sn = kv_strides[1];
+  p.i_sb = idx_strides[0];
+  p.i_sm = idx_strides[1];
+  p.i_sk = idx_strides[2];
+  p.o_sb = o_strides[0];
+  p.o_sm = o_strides[1];
+  p.o_sh = o_strides[2];
+  p.scale_log2 = scale * sa::kLog2e;
+  e = sa::launch_bwd(p, static_cast<const __nv_bfloat16*>(dout), static_cast<__nv_bfloat16*>(dq),
+                     dkv, dsink, dkv_strides[0], dkv_strides[1], scale,
+                     static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail_cuda(e);
   return SA_OK;
 }

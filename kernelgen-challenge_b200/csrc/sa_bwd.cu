@@ -1,0 +1,353 @@
+// sa_bwd.cu — backward pass of sparse_attn for sm_100a: gradients of q, the
+// KV cache and the sink, given o and dO from the forward.
+//
+// The reference has no backward.  This restates the gradient of its forward
+// (track-01/reference/reference.py:24-40, masking of
+// track-01/submission.py:313-322).  Per query row and head h, with p_t the
+// softmax weights over the valid slots and the sink, and v_t = k_t = kv[idx_t]:
+//   D      = sum_d dO . o                    (o from the forward)
+//   dp_t   = dO . v_t
+//   ds_t   = p_t (dp_t - D)
+//   dq     = scale * sum_t ds_t k_t
+//   dkv[idx_t] += scale * ds_t q + p_t dO    (summed over heads; duplicates add)
+//   dsink  = -p_sink * D                     (summed over rows)
+//
+// One CTA (4 warps) per query row.  Its units of 64 gathered rows (the forward's
+// 128-byte-swizzled slab layout) stream through a 2-deep cp.async ring twice:
+//   pass A  S = Q.K^T (warp w: keys 16w..16w+15), online max / sum per head:
+//           the row's log-sum-exp including the sink
+//   pass B  S and dP = dO.V^T again (warp w: keys 16w..16w+15), P and
+//           dS = P (dP - D) * scale into shared memory (bf16), then
+//           dq[16 x 128w..] += dS . K       (registers, whole row)
+//           dkv chunk [16 keys x 64 cols] = dS^T . Q + P^T . dO per warp, added
+//           into an fp32 gradient buffer with 8-byte atomics (masked slots skip)
+// All products are bf16 warp MMAs with fp32 accumulation.
+#include "sa_common.cuh"
+
+namespace sa {
+namespace bwd_path {
+
+constexpr int UK = 64;                      // keys per unit
+constexpr int NW = 4;                       // warps
+constexpr int NT = NW * 32;
+constexpr int SLOT_BYTES = UK * kDim * 2;   // 64 KiB
+constexpr int SLAB_BYTES = UK * 128;        // [64 keys x 64 cols]
+constexpr int T_BYTES = kHeads * kDim * 2;  // 16 KiB: Q or dO tile
+constexpr int P_BYTES = kHeads * UK * 2;    // 2 KiB: P or dS tile [head][key]
+
+struct BwdParams {
+  Params f;                  // forward arguments (q, kv, sink, idx, o, shapes, strides)
+  const __nv_bfloat16* dout; // dO, strides as o
+  __nv_bfloat16* dq;         // [b, m, 16, 512] contiguous
+  float* dkv;                // [b, kv_len, 512] fp32, row stride dkv_sn
+  float* dsink;              // [16] fp32
+  int64_t dkv_sb, dkv_sn;
+  float scale;
+};
+
+struct __align__(1024) Smem {
+  uint8_t ring[2][SLOT_BYTES];
+  uint8_t q[T_BYTES];   // 8 slabs [16 heads][64 cols], chunks swizzled by head
+  uint8_t dout[T_BYTES];
+  uint8_t p[P_BYTES];   // P   [head][key] bf16, chunks swizzled
+  uint8_t ds[P_BYTES];  // dS * scale
+  int32_t ids[2][UK];   // slot ids of the unit in each ring slot (-1: masked)
+  float red[NW][2][kHeads];
+  float D[kHeads];
+  float M[kHeads];      // log2-domain max including the sink
+  float invZ[kHeads];
+};
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+
+__device__ __forceinline__ uint32_t p_chunk(int h, int ch) {
+  return h * 128 + ((ch ^ (h & 7)) << 4);
+}
+// byte offset of the 16-byte chunk holding columns 8c..8c+7 of head h in a Q / dO tile
+__device__ __forceinline__ uint32_t t_chunk(int h, int c) {
+  return (c >> 3) * 2048 + h * 128 + (((c & 7) ^ (h & 7)) << 4);
+}
+
+__device__ __forceinline__ void red_add_f2(float* addr, float a, float b) {
+  atomicAdd(reinterpret_cast<float2*>(addr), make_float2(a, b));
+}
+
+__global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& S = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                     ~static_cast<uintptr_t>(1023));
+  const Params& p = bp.f;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g8 = lane >> 2, q4 = lane & 3;
+  const int64_t row = blockIdx.x;
+  const int64_t tb = row / p.m, tm = row - tb * p.m;
+  const int64_t U = (p.topk + UK - 1) / UK;
+  const int32_t* irow = p.idx + tb * p.i_sb + tm * p.i_sm;
+  const __nv_bfloat16* kvb = p.kv + tb * p.kv_sb;
+  const uint32_t qbase = smem_u32(S.q), dobase = smem_u32(S.dout);
+  const uint32_t pbase = smem_u32(S.p), dsbase = smem_u32(S.ds);
+
+  // ---- Q and dO of this row into their tiles; D = dO . o per head
+  {
+    const __nv_bfloat16* qr = p.q + tb * p.q_sb + tm * p.q_sm;
+    const __nv_bfloat16* dr = bp.dout + tb * p.o_sb + tm * p.o_sm;
+    for (int k = tid; k < kHeads * (kDim / 8); k += NT) {  // 16-byte chunks
+      const int h = k / (kDim / 8), c = k % (kDim / 8);
+      cp_async16(qbase + t_chunk(h, c), qr + h * p.q_sh + 8 * c, 16);
+      cp_async16(dobase + t_chunk(h, c), dr + h * p.o_sh + 8 * c, 16);
+    }
+    cp_async_commit();
+    const __nv_bfloat16* orow = p.o + tb * p.o_sb + tm * p.o_sm;
+    for (int h = warp; h < kHeads; h += NW) {
+      float acc = 0.f;
+      for (int c = lane; c < kDim / 8; c += 32) {
+        const uint4 a = *reinterpret_cast<const uint4*>(orow + h * p.o_sh + 8 * c);
+        const uint4 d = *reinterpret_cast<const uint4*>(dr + h * p.o_sh + 8 * c);
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, dw[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&aw[e]));
+          const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dw[e]));
+          acc += x.x * y.x + x.y * y.y;
+        }
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+      if (lane == 0) S.D[h] = acc;
+    }
+  }
+
+  // ---- gather of unit u into ring slot s: thread copies chunk tid & 63 of the
+  // rows of parity tid >> 6
+  auto issue = [&](int64_t u, int s) {
+    const int c = tid & 63, par = tid >> 6, j = c >> 3, cc = c & 7;
+    const uint32_t dst0 = smem_u32(S.ring[s]) + j * SLAB_BYTES;
+    for (int k = 0; k < UK / 2; ++k) {
+      const int r = par + 2 * k;
+      const int64_t key = u * UK + r;
+      const int32_t id = key < p.topk ? __ldg(irow + key * p.i_sk) : -1;
+      const bool v = id >= 0 && (int64_t)id < p.kv_len;
+      cp_async16(dst0 + r * 128 + ((cc ^ (r & 7)) << 4), kvb + (v ? (int64_t)id : 0) * p.kv_sn + c * 8,
+                 v ? 16 : 0);
+      if (c == 0) S.ids[s][r] = v ? id : -1;
+    }
+    cp_async_commit();
+  };
+
+  // S (or dP with the dO tile) for keys 16w + 8nt + ..: sa[nt][z] split accumulators
+  auto scores = [&](uint32_t sb, uint32_t abase, float (&sa)[2][2][4]) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int z = 0; z < 2; ++z) sa[nt][z][0] = sa[nt][z][1] = sa[nt][z][2] = sa[nt][z][3] = 0.f;
+    const int arow = (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll 4
+    for (int kp = 0; kp < 16; ++kp) {  // columns 32kp..32kp+31
+      uint32_t a0[4], a1[4];
+      ldmatrix_x4(a0, abase + t_chunk(arow, 4 * kp + (lane >> 4)));
+      ldmatrix_x4(a1, abase + t_chunk(arow, 4 * kp + 2 + (lane >> 4)));
+      const int slab = kp >> 1, c0 = (kp & 1) * 4;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int key = 16 * warp + 8 * nt + (lane & 7);
+        uint32_t kf[4];
+        ldmatrix_x4(kf, sb + slab * SLAB_BYTES + key * 128 + (((c0 + (lane >> 3)) ^ (key & 7)) << 4));
+        mma_16816(sa[nt][0], a0, kf[0], kf[1]);
+        mma_16816(sa[nt][1], a1, kf[2], kf[3]);
+      }
+    }
+  };
+
+  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;  // pass A, this lane's keys
+  float dq[16][4];  // dq[heads g8, g8+8][128w + 8nt + 2q4 + {0,1}]
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) dq[nt][0] = dq[nt][1] = dq[nt][2] = dq[nt][3] = 0.f;
+
+  if (U > 0) issue(0, 0);
+  for (int64_t i = 0; i < 2 * U; ++i) {
+    const int s = static_cast<int>(i & 1);
+    if (i + 1 < 2 * U) {
+      issue((i + 1) % U, s ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // unit i landed (and, at i = 0, the Q / dO tiles and D)
+    const uint32_t sb = smem_u32(S.ring[s]);
+    const bool passB = i >= U;
+    if (i == U) {
+      // ---- end of pass A: M and 1/Z per head, including the sink
+#pragma unroll
+      for (int off = 1; off <= 2; off <<= 1) {
+        const float mo_lo = __shfl_xor_sync(0xffffffffu, m_lo, off);
+        const float lo_lo = __shfl_xor_sync(0xffffffffu, l_lo, off);
+        const float mo_hi = __shfl_xor_sync(0xffffffffu, m_hi, off);
+        const float lo_hi = __shfl_xor_sync(0xffffffffu, l_hi, off);
+        const float n_lo = fmaxf(m_lo, mo_lo), n_hi = fmaxf(m_hi, mo_hi);
+        l_lo = (n_lo == -INFINITY) ? 0.f : l_lo * exp2f(m_lo - n_lo) + lo_lo * exp2f(mo_lo - n_lo);
+        l_hi = (n_hi == -INFINITY) ? 0.f : l_hi * exp2f(m_hi - n_hi) + lo_hi * exp2f(mo_hi - n_hi);
+        m_lo = n_lo;
+        m_hi = n_hi;
+      }
+      if (q4 == 0) {
+        S.red[warp][0][g8] = m_lo;
+        S.red[warp][1][g8] = l_lo;
+        S.red[warp][0][g8 + 8] = m_hi;
+        S.red[warp][1][g8 + 8] = l_hi;
+      }
+      __syncthreads();
+      if (tid < kHeads) {
+        const float sl2 = __ldg(p.sink + tid) * kLog2e;
+        float M = sl2;
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, S.red[w][0][tid]);
+        float Z = exp2f(sl2 - M);
+        for (int w = 0; w < NW; ++w)
+          if (S.red[w][0][tid] != -INFINITY) Z += S.red[w][1][tid] * exp2f(S.red[w][0][tid] - M);
+        S.M[tid] = M;
+        S.invZ[tid] = 1.f / Z;
+        // dsink = -p_sink * D
+        atomicAdd(bp.dsink + tid, -exp2f(sl2 - M) / Z * S.D[tid]);
+      }
+      __syncthreads();
+    }
+    float sa[2][2][4];
+    scores(sb, qbase, sa);
+    float x[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int key = 16 * warp + 8 * nt + 2 * q4;
+      const bool v0 = S.ids[s][key] >= 0, v1 = S.ids[s][key + 1] >= 0;
+      x[nt][0] = v0 ? (sa[nt][0][0] + sa[nt][1][0]) * p.scale_log2 : -INFINITY;
+      x[nt][1] = v1 ? (sa[nt][0][1] + sa[nt][1][1]) * p.scale_log2 : -INFINITY;
+      x[nt][2] = v0 ? (sa[nt][0][2] + sa[nt][1][2]) * p.scale_log2 : -INFINITY;
+      x[nt][3] = v1 ? (sa[nt][0][3] + sa[nt][1][3]) * p.scale_log2 : -INFINITY;
+    }
+    if (!passB) {
+      // online max / sum of this lane's keys
+      const float b_lo = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
+      const float b_hi = fmaxf(fmaxf(x[0][2], x[0][3]), fmaxf(x[1][2], x[1][3]));
+      const float n_lo = fmaxf(m_lo, b_lo), n_hi = fmaxf(m_hi, b_hi);
+      if (n_lo != -INFINITY) {
+        l_lo = l_lo * exp2f(m_lo - n_lo) + exp2f(x[0][0] - n_lo) + exp2f(x[0][1] - n_lo) +
+               exp2f(x[1][0] - n_lo) + exp2f(x[1][1] - n_lo);
+        m_lo = n_lo;
+      }
+      if (n_hi != -INFINITY) {
+        l_hi = l_hi * exp2f(m_hi - n_hi) + exp2f(x[0][2] - n_hi) + exp2f(x[0][3] - n_hi) +
+               exp2f(x[1][2] - n_hi) + exp2f(x[1][3] - n_hi);
+        m_hi = n_hi;
+      }
+      __syncthreads();  // slot s free for the next issue
+      continue;
+    }
+    // ---- pass B: P, dP, dS
+    float dpa[2][2][4];
+    scores(sb, dobase, dpa);
+    {
+      const float M_lo = S.M[g8], M_hi = S.M[g8 + 8];
+      const float iz_lo = S.invZ[g8], iz_hi = S.invZ[g8 + 8];
+      const float D_lo = S.D[g8], D_hi = S.D[g8 + 8];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const float p0 = exp2f(x[nt][0] - M_lo) * iz_lo, p1 = exp2f(x[nt][1] - M_lo) * iz_lo;
+        const float p2 = exp2f(x[nt][2] - M_hi) * iz_hi, p3 = exp2f(x[nt][3] - M_hi) * iz_hi;
+        const float d0 = p0 * (dpa[nt][0][0] + dpa[nt][1][0] - D_lo) * bp.scale;
+        const float d1 = p1 * (dpa[nt][0][1] + dpa[nt][1][1] - D_lo) * bp.scale;
+        const float d2 = p2 * (dpa[nt][0][2] + dpa[nt][1][2] - D_hi) * bp.scale;
+        const float d3 = p3 * (dpa[nt][0][3] + dpa[nt][1][3] - D_hi) * bp.scale;
+        const int ch = 2 * warp + nt;
+        *reinterpret_cast<uint32_t*>(S.p + p_chunk(g8, ch) + 4 * q4) = pack_bf16x2(p0, p1);
+        *reinterpret_cast<uint32_t*>(S.p + p_chunk(g8 + 8, ch) + 4 * q4) = pack_bf16x2(p2, p3);
+        *reinterpret_cast<uint32_t*>(S.ds + p_chunk(g8, ch) + 4 * q4) = pack_bf16x2(d0, d1);
+        *reinterpret_cast<uint32_t*>(S.ds + p_chunk(g8 + 8, ch) + 4 * q4) = pack_bf16x2(d2, d3);
+      }
+    }
+    __syncthreads();  // P and dS of all 64 keys written
+    // ---- dq[16 x 128w..128w+127] += dS[16 x 64] . K[64 x 128]
+#pragma unroll
+    for (int kst = 0; kst < 4; ++kst) {
+      uint32_t da[4];
+      {
+        const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
+        ldmatrix_x4(da, dsbase + p_chunk(r, 2 * kst + (lane >> 4)));
+      }
+      const int kr = kst * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int np = 0; np < 8; ++np) {
+        const int slab = 2 * warp + (np >> 2);
+        const int ch = ((np & 3) << 1) + (lane >> 4);
+        uint32_t vb[4];
+        ldmatrix_x4_trans(vb, sb + slab * SLAB_BYTES + kr * 128 + ((ch ^ (kr & 7)) << 4));
+        mma_16816(dq[2 * np], da, vb[0], vb[1]);
+        mma_16816(dq[2 * np + 1], da, vb[2], vb[3]);
+      }
+    }
+    // ---- dkv[keys 16w..16w+15][cols] = dS^T . Q + P^T . dO, 64 columns at a time
+    {
+      // A-fragments (rows = keys, k = heads) by transposed loads of the
+      // [head][key] tiles: matrices (heads 0-7 | 8-15) x (keys 16w..+7 | 16w+8..+15)
+      const int mt = lane >> 3, hr = (lane & 7) + 8 * (mt >> 1), kc = 2 * warp + (mt & 1);
+      uint32_t ad[4], ap[4];
+      ldmatrix_x4_trans(ad, dsbase + p_chunk(hr, kc));
+      ldmatrix_x4_trans(ap, pbase + p_chunk(hr, kc));
+      const int key_lo = 16 * warp + g8, key_hi = key_lo + 8;
+      const int32_t id_lo = S.ids[s][key_lo], id_hi = S.ids[s][key_hi];
+      float* dlo = bp.dkv + tb * bp.dkv_sb + (int64_t)(id_lo < 0 ? 0 : id_lo) * bp.dkv_sn;
+      float* dhi = bp.dkv + tb * bp.dkv_sb + (int64_t)(id_hi < 0 ? 0 : id_hi) * bp.dkv_sn;
+      // B-fragments (k = heads, n = columns) by transposed loads of the Q / dO
+      // tiles: matrices (heads 0-7 | 8-15) x (columns n0..n0+7 | n0+8..n0+15)
+      const int br = (lane & 7) + 8 * (mt & 1), bcol = (mt >> 1);
+#pragma unroll 1
+      for (int cb = 0; cb < kDim / 64; ++cb) {
+        float acc[8][4];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {  // n-tiles 2np, 2np+1: columns 64cb + 16np ..
+          uint32_t bq[4], bd[4];
+          const int c8 = 8 * cb + 2 * np + bcol;
+          ldmatrix_x4_trans(bq, qbase + t_chunk(br, c8));
+          ldmatrix_x4_trans(bd, dobase + t_chunk(br, c8));
+          mma_16816(acc[2 * np], ad, bq[0], bq[1]);
+          mma_16816(acc[2 * np + 1], ad, bq[2], bq[3]);
+          mma_16816(acc[2 * np], ap, bd[0], bd[1]);
+          mma_16816(acc[2 * np + 1], ap, bd[2], bd[3]);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          const int col = 64 * cb + 8 * nt + 2 * q4;
+          if (id_lo >= 0) red_add_f2(dlo + col, acc[nt][0], acc[nt][1]);
+          if (id_hi >= 0) red_add_f2(dhi + col, acc[nt][2], acc[nt][3]);
+        }
+      }
+    }
+    __syncthreads();  // slot s and the P / dS tiles free
+  }
+  cp_async_wait<0>();  // (no units: the Q / dO copies)
+  // ---- dq of this row (the scale is already in dS)
+  __nv_bfloat16* dqr = bp.dq + row * (kHeads * kDim);
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    const int d = 128 * warp + 8 * nt + 2 * q4;
+    *reinterpret_cast<uint32_t*>(dqr + g8 * kDim + d) = pack_bf16x2(dq[nt][0], dq[nt][1]);
+    *reinterpret_cast<uint32_t*>(dqr + (g8 + 8) * kDim + d) = pack_bf16x2(dq[nt][2], dq[nt][3]);
+  }
+}
+
+}  // namespace bwd_path
+
+cudaError_t launch_bwd(const Params& f, const __nv_bfloat16* dout, __nv_bfloat16* dq, float* dkv,
+                       float* dsink, int64_t dkv_sb, int64_t dkv_sn, float scale,
+                       cudaStream_t st) {
+  using namespace bwd_path;
+  static PerDeviceOnce attr_once;
+  cudaError_t e = once_per_device(attr_once, [] {
+    return cudaFuncSetAttribute(sa_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kSmemBytes);
+  });
+  if (e != cudaSuccess) return e;
+  BwdParams bp{f, dout, dq, dkv, dsink, dkv_sb, dkv_sn, scale};
+  sa_bwd_kernel<<<static_cast<unsigned>(f.b * f.m), NT, kSmemBytes, st>>>(bp);
+  return cudaGetLastError();
+}
+
+}  // namespace sa

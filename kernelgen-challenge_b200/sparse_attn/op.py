@@ -29,7 +29,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["sparse_attn", "sparse_attn_out", "workspace_bytes"]
+__all__ = ["sparse_attn", "sparse_attn_out", "sparse_attn_backward", "workspace_bytes"]
 
 
 def _device_index(device) -> int:
@@ -160,6 +160,62 @@ def _(q, kv, attn_sink, topk_idxs, scale):
     return q.new_empty(q.shape)
 
 
+def sparse_attn_backward(q, kv, attn_sink, topk_idxs, scale, o, do):
+    """Gradients of ``sparse_attn`` (``sa_bwd`` in ``libsparse_attn.so``).
+
+    Given the forward's inputs, its output ``o`` and the upstream gradient
+    ``do``, returns ``(dq, dkv, dsink)`` with the dtypes of q, kv and
+    attn_sink.  Masked slots contribute nothing; duplicated indices add.  The
+    reference has no backward: this is the gradient of its forward
+    (track-01/reference/reference.py:24-40).
+    """
+    _validate(q, kv, attn_sink, topk_idxs)
+    h = q.shape[2]
+    if h < _KERNEL_HEADS:  # zero heads: zero gradients of their own, none into kv
+        pad = _KERNEL_HEADS - h
+        zq = q.new_zeros(*q.shape[:2], pad, q.shape[3])
+        dq, dkv, dsink = sparse_attn_backward(
+            torch.cat([q, zq], 2), kv, torch.cat([attn_sink, attn_sink.new_zeros(pad)]),
+            topk_idxs, scale, torch.cat([o, torch.zeros_like(zq)], 2),
+            torch.cat([do, torch.zeros_like(zq)], 2))
+        return dq[:, :, :h].contiguous(), dkv, dsink[:h].contiguous()
+    b, m, _, d = q.shape
+    q_c = q if _row_ok(q) else q.contiguous()
+    kv_c = kv if _row_ok(kv) else kv.contiguous()
+    o_c, do_c = o.contiguous(), do.to(q.dtype).contiguous()
+    dq = torch.empty(b, m, h, d, dtype=q.dtype, device=q.device)
+    dkv = torch.zeros(kv.shape, dtype=torch.float32, device=q.device)
+    dsink = torch.zeros(h, dtype=torch.float32, device=q.device)
+    if dq.numel() == 0:
+        return dq, dkv.to(kv.dtype), dsink.to(attn_sink.dtype)
+    with torch.cuda.device(q.device):
+        st = torch.cuda.current_stream(q.device)
+        _lib.check(_lib.lib().sa_bwd(
+            q_c.data_ptr(), kv_c.data_ptr(), attn_sink.contiguous().data_ptr(),
+            topk_idxs.data_ptr(), o_c.data_ptr(), do_c.data_ptr(), dq.data_ptr(),
+            dkv.data_ptr(), dsink.data_ptr(), b, m, h, d, kv.shape[1], topk_idxs.shape[-1],
+            _lib.i64_array(q_c.stride()), _lib.i64_array(kv_c.stride()),
+            _lib.i64_array(topk_idxs.stride()), _lib.i64_array(o_c.stride()),
+            _lib.i64_array(dkv.stride()), float(scale), st.cuda_stream))
+    return dq, dkv.to(kv.dtype), dsink.to(attn_sink.dtype)
+
+
+def _setup_context(ctx, inputs, output):
+    q, kv, attn_sink, topk_idxs, scale = inputs
+    ctx.save_for_backward(q, kv, attn_sink, topk_idxs, output)
+    ctx.scale = scale
+
+
+def _fwd_backward(ctx, grad_o):
+    q, kv, attn_sink, topk_idxs, o = ctx.saved_tensors
+    dq, dkv, dsink = sparse_attn_backward(q, kv, attn_sink, topk_idxs, ctx.scale, o, grad_o)
+    return dq, dkv, dsink, None, None
+
+
+torch.library.register_autograd("sparse_attn_b200::fwd", _fwd_backward,
+                                setup_context=_setup_context)
+
+
 def sparse_attn(q, kv, attn_sink, topk_idxs, scale):
     """Top-k sparse attention with attention sink (track-01 signature).
 
@@ -172,5 +228,11 @@ def sparse_attn(q, kv, attn_sink, topk_idxs, scale):
         scale:      float
     Returns:
         o:          [b, m, h, d]   bf16
+
+    Differentiable: when autograd records (an input requires grad) the call
+    goes through the registered op, whose backward is ``sa_bwd``.
     """
+    if torch.is_grad_enabled() and (q.requires_grad or kv.requires_grad or
+                                    attn_sink.requires_grad):
+        return torch.ops.sparse_attn_b200.fwd(q, kv, attn_sink, topk_idxs, float(scale))
     return _forward(q, kv, attn_sink, topk_idxs, float(scale))

@@ -41,7 +41,7 @@ from __future__ import annotations
 import torch
 
 __all__ = ["sparse_attn_oracle", "valid_slot_count", "quantize_kv_fp8_ref", "dequantize_kv_fp8",
-           "sparse_attn_fp8_oracle"]
+           "sparse_attn_fp8_oracle", "sparse_attn_oracle_grads"]
 
 
 def _chunk_rows(m: int, topk: int, d: int, budget_bytes: int = 1 << 30) -> int:
@@ -136,3 +136,29 @@ def sparse_attn_fp8_oracle(q, kv8, kv_scale, attn_sink, topk_idxs, scale, **kw):
     enters its arithmetic unchanged."""
     return sparse_attn_oracle(q, dequantize_kv_fp8(kv8, kv_scale), attn_sink, topk_idxs,
                               scale, **kw)
+
+
+# ---------------------------------------------------------------------------
+# Gradients (the reference has no backward): torch autograd through the same
+# fp32 restatement, on the CPU.
+# ---------------------------------------------------------------------------
+def sparse_attn_oracle_grads(q, kv, attn_sink, topk_idxs, scale, do):
+    """(o, dq, dkv, dsink) in fp32: autograd of the fp32 restatement of
+    reference.py:24-40 with the -1 masking rule, for upstream gradient do."""
+    q32 = q.detach().cpu().float().requires_grad_(True)
+    kv32 = kv.detach().cpu().float().requires_grad_(True)
+    s32 = attn_sink.detach().cpu().float().requires_grad_(True)
+    idx = topk_idxs.cpu().long()
+    b, m, h, d = q32.shape
+    kv_len = kv32.shape[1]
+    valid = (idx >= 0) & (idx < kv_len)
+    safe = torch.where(valid, idx, torch.zeros_like(idx))
+    g = torch.gather(kv32, 1, safe.reshape(b, -1).unsqueeze(-1).expand(-1, -1, d))
+    g = g.reshape(b, m, -1, d) * valid.unsqueeze(-1)
+    scores = torch.einsum("bmhd,bmtd->bmht", q32, g) * scale
+    scores = scores.masked_fill(~valid.unsqueeze(2), float("-inf"))
+    attn = torch.softmax(torch.cat([scores, s32[None, None, :, None].expand(b, m, h, 1)], -1),
+                         -1)[..., :-1]
+    o = torch.einsum("bmht,bmtd->bmhd", attn, g)
+    o.backward(do.detach().cpu().float())
+    return o.detach(), q32.grad, kv32.grad, s32.grad
