@@ -59,8 +59,10 @@ def parse():
     ap.add_argument("--kv", choices=["bf16", "fp8"], default="bf16",
                     help="KV cache format: bf16 (the reference's) or e4m3 + fp32 per-token "
                          "scale (sparse_attn_fp8)")
-    ap.add_argument("--op", choices=["sparse_attn", "hc_sinkhorn"], default="sparse_attn",
-                    help="hc_sinkhorn: the track-02 op on its 1k-1-64 prefill shape")
+    ap.add_argument("--op", choices=["sparse_attn", "sparse_attn_bwd", "hc_sinkhorn"],
+                    default="sparse_attn",
+                    help="sparse_attn_bwd: the backward pass on --config (default causal); "
+                         "hc_sinkhorn: the track-02 op on its 1k-1-64 prefill shape")
     ap.add_argument("--graph", action="store_true",
                     help="capture one op call in a CUDA graph and time its replays")
     ap.add_argument("--no-launch-count", action="store_true",
@@ -461,10 +463,66 @@ def run_hc_sinkhorn(args):
         flush=True)
 
 
+def run_backward(args):
+    """The backward pass (sa_bwd) on one configuration: query-tokens/s of
+    gradient computation, L2 flushed before every step.  The CPU leg
+    (--impl reference) times autograd of the fp32 oracle on 8 rows."""
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        from oracle.sparse_attn_oracle import sparse_attn_oracle_grads
+        torch.set_num_threads(os.cpu_count() or 1)
+        q, kv, sink, idx, scale, n = cpu_sample_inputs(cfg, 8)
+        do = torch.randn(q.shape).to(torch.bfloat16)
+        t0 = time.perf_counter()
+        for _ in range(max(1, args.steps)):
+            sparse_attn_oracle_grads(q, kv, sink, idx, scale, do)
+        el = time.perf_counter() - t0
+        val = n * max(1, args.steps) / el
+        print(json.dumps({"metric": "sparse_attn backward query-tokens/s", "value": val,
+                          "unit": "query-tokens/s", "impl": "reference",
+                          "config": {"workload": cfg.name, "sample_rows": n},
+                          "cpu_baseline": {"value": val, "unit": "query-tokens/s",
+                                           "cores": os.cpu_count(), "kind": "port",
+                                           "sample": f"{n} rows, autograd of the fp32 oracle"}}),
+              flush=True)
+        return
+    import sparse_attn
+    dev = torch.device("cuda", 0)
+    q, kv, sink, idx = device_inputs(cfg, seed=1000, device=dev)
+    o = sparse_attn.sparse_attn(q, kv, sink, idx, SCALE)
+    do = torch.randn(q.shape, device=dev, dtype=torch.bfloat16)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        sparse_attn.sparse_attn_backward(q, kv, sink, idx, SCALE, o, do)
+    K = args.steps
+    st = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    en = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    torch.cuda.synchronize()
+    for k in range(K):
+        flush.zero_()
+        st[k].record(stream)
+        sparse_attn.sparse_attn_backward(q, kv, sink, idx, SCALE, o, do)
+        en[k].record(stream)
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(e) for a, e in zip(st, en)) / K
+    valid = int(((idx >= 0) & (idx < cfg.kv_len)).sum().item())
+    print(json.dumps({
+        "metric": "sparse_attn backward query-tokens/s", "value": cfg.b * cfg.m / (ms / 1e3),
+        "unit": "query-tokens/s", "n_gpus": 1, "steps": K, "ms_per_step": ms,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": cfg.name, "b": cfg.b, "m": cfg.m, "kv_len": cfg.kv_len,
+                   "topk": cfg.topk, "includes": "zeroing of the fp32 dkv buffer, sa_bwd, "
+                   "dkv cast to bf16"},
+        "gathered_kv_gbs": 2 * valid * D * 2 / (ms / 1e3) / 1e9}), flush=True)
+
+
 def main():
     args = parse()
     if args.op == "hc_sinkhorn":
         return run_hc_sinkhorn(args)
+    if args.op == "sparse_attn_bwd":
+        return run_backward(args)
     if args.impl == "reference":
         return run_reference(args)
 
