@@ -19,7 +19,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/hc_sinkhorn.h"
+#include "hc_sinkhorn.h"
 
 namespace hcs {
 
