@@ -539,7 +539,7 @@ def main():
     cfg = CONFIGS[args.config]
     q, kv, sink, idx = device_inputs(cfg, seed=1000 + rank, device=dev)
     o = torch.empty_like(q)
-    ws = torch.empty(sparse_attn.workspace_bytes(cfg.b, cfg.m, cfg.topk, local_rank),
+    ws = torch.zeros(sparse_attn.workspace_bytes(cfg.b, cfg.m, cfg.topk, local_rank),
                      dtype=torch.uint8, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)

@@ -65,9 +65,11 @@ int sa_variant_available(int variant);
 
 /* fp8 KV cache.  kv8 is [b, kv_len, 512] e4m3 (torch.float8_e4m3fn) bytes,
  * kv_scale is [b, kv_len] fp32, and row t of batch b stands for the bf16 row
- * kv8[b,t,:] * kv_scale[b,t].  The result is sa_fwd on that dequantised cache,
- * computed with e4m3 tensor-core MMAs.  Q and P are split into two e4m3 terms,
- * so accuracy stays close to the bf16 path.  kv_strides are in bytes (rows
+ * kv8[b,t,:] * kv_scale[b,t].  The result is sa_fwd on that dequantised cache.
+ * The e4m3 values are widened to f16 in registers (exact) and both products
+ * run as f16 tensor-core MMAs with fp32 accumulation; q (scaled per head by a
+ * power of two) and the softmax weights are f16, so accuracy is at least the
+ * bf16 path's.  kv_strides are in bytes (rows
  * 16-byte aligned); kv_scale_strides are in elements.  The workspace is sized
  * by sa_workspace_bytes.  grid_ctas = 0 picks one CTA per SM.  q must be
  * 16-byte aligned (it is loaded by TMA).  The gathered bytes per slot are 516
@@ -128,7 +130,10 @@ int sa_last_cuda_error(void);
  * count.  Replaces nothing in the reference: the reference kernel keeps all
  * state in registers (track-01/submission.py:1006-1021); the persistent
  * split kernels here spill per-CTA partial results for query rows that span
- * two CTAs.  Returns 0 on error (e.g. bad device).
+ * two CTAs.  The workspace must be zero-filled before its first use; every
+ * call leaves it zero-filled again (the default kernel keeps one counter per
+ * CTA there), so one memset at allocation suffices.  Returns 0 on error (e.g.
+ * bad device).
  */
 size_t sa_workspace_bytes(int64_t b, int64_t m, int64_t topk, int device);
 

@@ -242,8 +242,14 @@ int sa_fwd_ex(const void* q, const void* kv, const float* sink, const int32_t* i
   if (workspace == nullptr || workspace_bytes < need) return SA_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return SA_ERR_INVALID_ARG;
   char* ws = static_cast<char*>(workspace);
-  p.part_acc = reinterpret_cast<float*>(ws);
-  p.part_ml = reinterpret_cast<float*>(ws + sa::ws_acc_bytes(p.grid));
+  p.tickets = reinterpret_cast<int*>(ws);
+  p.part_acc = reinterpret_cast<float*>(ws + sa::kTicketBytes);
+  p.part_ml = reinterpret_cast<float*>(ws + sa::kTicketBytes + sa::ws_acc_bytes(p.grid));
+  // Split rows: when every CTA covers at least two rows' worth of units
+  // (prefill), the ws kernel merges them itself (the last CTA of each row,
+  // at its end); with fewer units per CTA (decode) nearly every CTA would end
+  // in merges, and the combine kernel spreads them over the whole GPU instead.
+  p.merge_in_kernel = (variant == SA_VARIANT_WS && p.units >= 2 * p.upt * p.grid) ? 1 : 0;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   e = (variant == SA_VARIANT_MMA)       ? sa::launch_mma(p, st)
@@ -322,8 +328,9 @@ int sa_fwd_fp8(const void* q, const void* kv8, const float* kv_scale, const floa
   if (workspace == nullptr || workspace_bytes < need) return SA_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return SA_ERR_INVALID_ARG;
   char* ws = static_cast<char*>(workspace);
-  p.part_acc = reinterpret_cast<float*>(ws);
-  p.part_ml = reinterpret_cast<float*>(ws + sa::ws_acc_bytes(p.grid));
+  p.tickets = reinterpret_cast<int*>(ws);
+  p.part_acc = reinterpret_cast<float*>(ws + sa::kTicketBytes);
+  p.part_ml = reinterpret_cast<float*>(ws + sa::kTicketBytes + sa::ws_acc_bytes(p.grid));
   e = sa::launch_fp8(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail_cuda(e);
   return SA_OK;

@@ -56,6 +56,11 @@ struct Params {
   // bytes) and row t of batch b dequantises as kv8[b,t,:] * kscale[b,t]
   const float* kscale;
   int64_t ks_sb, ks_sn;
+  // One word per CTA (workspace, zero between calls): the number of CTAs that
+  // finished their part of the row split at the start of CTA f's range.  The
+  // last one merges the row and zeroes the word again (sa_ws.cu).
+  int* tickets;
+  int merge_in_kernel;  // sa_ws only: merge split rows by ticket instead of the combine kernel
 };
 
 // Workspace layout shared by the host (sizing) and the kernels.
@@ -68,8 +73,13 @@ __host__ __device__ constexpr size_t ws_acc_bytes(int grid) {
 __host__ __device__ constexpr size_t ws_ml_bytes(int grid) {
   return ((size_t)2 * grid * kPartMlFloats * sizeof(float) + 255) & ~(size_t)255;
 }
+// The ticket words come first, at a fixed offset and sized for the largest
+// grid, so that calls with different grids never find partial data where
+// another call's tickets are expected to be zero.
+constexpr int kMaxGrid = 512;  // >= 2 x the SM count of any supported device
+constexpr size_t kTicketBytes = kMaxGrid * sizeof(int);
 __host__ __device__ constexpr size_t workspace_bytes_for_grid(int grid) {
-  return ws_acc_bytes(grid) + ws_ml_bytes(grid);
+  return kTicketBytes + ws_acc_bytes(grid) + ws_ml_bytes(grid);
 }
 
 __host__ __device__ inline int64_t unit_begin(int64_t g, int64_t units, int64_t grid) {
@@ -214,5 +224,71 @@ __device__ __forceinline__ float sink_factor(float m_run, float l_run, float sin
   float den = l_run * alpha + exp2f(sink_log2 - M);
   return alpha / den;
 }
+
+// Merge of a split row: head h, columns d0..d0+7 of row t, whose units
+// CTAs f..f+np-1 computed; the fp32 partials are combined with the sink as the
+// extra logit (reference.py:34-38) and o is written in bf16.  Partial k of the
+// row sits in slot 2(f+k), except k = 0 when the row starts inside CTA f's
+// range (f_mid): that is f's last segment, slot 2f+1.  All loads of a batch of
+// up to kCombineBatch partials are issued together: one memory round trip.
+constexpr int kCombineBatch = 4;
+__device__ __forceinline__ void merge_split_row(const Params& p, int64_t f, int np, bool f_mid,
+                                                int64_t t, int h, int d0) {
+  auto slot_of = [&](int k) -> int64_t { return (k == 0 && f_mid) ? 2 * f + 1 : 2 * (f + k); };
+  const float sink_l2 = __ldg(p.sink + h) * kLog2e;
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  float M = sink_l2, den = 1.f;  // den relative to M (= exp2(sink - M) for M = sink)
+  for (int k0 = 0; k0 < np; k0 += kCombineBatch) {
+    float mk[kCombineBatch], lk[kCombineBatch];
+    float4 va[kCombineBatch], vb[kCombineBatch];
+#pragma unroll
+    for (int k = 0; k < kCombineBatch; ++k) {
+      mk[k] = -INFINITY;
+      lk[k] = 0.f;
+      va[k] = vb[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k0 + k < np) {
+        const int64_t sl = slot_of(k0 + k);
+        mk[k] = __ldcg(p.part_ml + sl * kPartMlFloats + h);
+        lk[k] = __ldcg(p.part_ml + sl * kPartMlFloats + kHeads + h);
+        const float4* src =
+            reinterpret_cast<const float4*>(p.part_acc + sl * kPartAccFloats + h * kDim + d0);
+        va[k] = __ldcg(src);
+        vb[k] = __ldcg(src + 1);
+      }
+    }
+    float Mb = M;
+#pragma unroll
+    for (int k = 0; k < kCombineBatch; ++k) Mb = fmaxf(Mb, mk[k]);
+    const float r = exp2f(M - Mb);  // rescale what was merged so far
+    den *= r;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] *= r;
+#pragma unroll
+    for (int k = 0; k < kCombineBatch; ++k) {
+      const float w = exp2f(mk[k] - Mb);  // 0 for absent partials
+      den += lk[k] * w;
+      acc[0] += w * va[k].x;
+      acc[1] += w * va[k].y;
+      acc[2] += w * va[k].z;
+      acc[3] += w * va[k].w;
+      acc[4] += w * vb[k].x;
+      acc[5] += w * vb[k].y;
+      acc[6] += w * vb[k].z;
+      acc[7] += w * vb[k].w;
+    }
+    M = Mb;
+  }
+  const float inv = 1.f / den;
+  const int64_t tb = t / p.m, tm = t - tb * p.m;
+  uint4 w;
+  w.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+  w.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+  w.z = pack_bf16x2(acc[4] * inv, acc[5] * inv);
+  w.w = pack_bf16x2(acc[6] * inv, acc[7] * inv);
+  *reinterpret_cast<uint4*>(p.o + tb * p.o_sb + tm * p.o_sm + h * p.o_sh + d0) = w;
+}
+
 
 }  // namespace sa

@@ -301,7 +301,6 @@ __global__ void __launch_bounds__(NT, 1) sa_mma_fwd_kernel(const Params p) {
 // moment griddepcontrol.wait releases them (forward grid complete, stores
 // visible).
 // ----------------------------------------------------------------------------
-constexpr int kCombineBatch = 4;
 constexpr int kMaxOwners = 512;  // >= the largest persistent grid (2 x SM count)
 
 struct OwnerList {
@@ -325,63 +324,8 @@ __global__ void __launch_bounds__(64, 8) sa_combine_kernel(const Params p,
   const int64_t f = cta_of_unit(ts, U, G);
   const bool f_mid = unit_begin(f, U, G) < ts;
   const int np = static_cast<int>(g - f + 1);
-  auto slot_of = [&](int k) -> int64_t { return (k == 0 && f_mid) ? 2 * f + 1 : 2 * (f + k); };
 
-  const int h = blockIdx.y;
-  const int d0 = threadIdx.x * 8;
-  const float sink_l2 = __ldg(p.sink + h) * kLog2e;
-  float acc[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-  float M = sink_l2, den = 1.f;  // den relative to M (= exp2(sink - M) for M = sink)
-  for (int k0 = 0; k0 < np; k0 += kCombineBatch) {
-    float mk[kCombineBatch], lk[kCombineBatch];
-    float4 va[kCombineBatch], vb[kCombineBatch];
-#pragma unroll
-    for (int k = 0; k < kCombineBatch; ++k) {
-      mk[k] = -INFINITY;
-      lk[k] = 0.f;
-      va[k] = vb[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (k0 + k < np) {
-        const int64_t sl = slot_of(k0 + k);
-        mk[k] = __ldcg(p.part_ml + sl * kPartMlFloats + h);
-        lk[k] = __ldcg(p.part_ml + sl * kPartMlFloats + kHeads + h);
-        const float4* src =
-            reinterpret_cast<const float4*>(p.part_acc + sl * kPartAccFloats + h * kDim + d0);
-        va[k] = __ldcg(src);
-        vb[k] = __ldcg(src + 1);
-      }
-    }
-    float Mb = M;
-#pragma unroll
-    for (int k = 0; k < kCombineBatch; ++k) Mb = fmaxf(Mb, mk[k]);
-    const float r = exp2f(M - Mb);  // rescale what was merged so far
-    den *= r;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] *= r;
-#pragma unroll
-    for (int k = 0; k < kCombineBatch; ++k) {
-      const float w = exp2f(mk[k] - Mb);  // 0 for absent partials
-      den += lk[k] * w;
-      acc[0] += w * va[k].x;
-      acc[1] += w * va[k].y;
-      acc[2] += w * va[k].z;
-      acc[3] += w * va[k].w;
-      acc[4] += w * vb[k].x;
-      acc[5] += w * vb[k].y;
-      acc[6] += w * vb[k].z;
-      acc[7] += w * vb[k].w;
-    }
-    M = Mb;
-  }
-  const float inv = 1.f / den;
-  const int64_t tb = t / p.m, tm = t - tb * p.m;
-  uint4 w;
-  w.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
-  w.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
-  w.z = pack_bf16x2(acc[4] * inv, acc[5] * inv);
-  w.w = pack_bf16x2(acc[6] * inv, acc[7] * inv);
-  *reinterpret_cast<uint4*>(p.o + tb * p.o_sb + tm * p.o_sm + h * p.o_sh + d0) = w;
+  merge_split_row(p, f, np, f_mid, t, blockIdx.y, threadIdx.x * 8);
 }
 
 // Owner CTAs of the split rows (the combine kernel's blocks).

@@ -60,7 +60,8 @@ def _cached_workspace(dev: torch.device, stream, nbytes: int) -> torch.Tensor:
     key = (dev.index, stream.cuda_stream)
     ws = _ws_cache.get(key)
     if ws is None or ws.numel() < nbytes:
-        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        # zero-filled once: the library leaves it zero-filled after every call
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
         _ws_cache[key] = ws
     return ws
 
@@ -97,7 +98,8 @@ def sparse_attn_out(o, q, kv, attn_sink, topk_idxs, scale, workspace=None, *,
     """Write ``sparse_attn(q, kv, attn_sink, topk_idxs, scale)`` into ``o``.
 
     No copies: q/kv/o need a unit last-dim stride and 16-byte aligned rows.
-    ``workspace`` (uint8 CUDA tensor of at least :func:`workspace_bytes`) is
+    ``workspace`` (uint8 CUDA tensor of at least :func:`workspace_bytes`,
+    zero-filled before its first use; every call leaves it zero-filled) is
     taken from a per-(device, stream) cache when omitted.  ``variant``/``grid`` select the kernel
     variant and persistent grid size (0 = automatic).
     """

@@ -44,7 +44,7 @@ def main(argv=None):
     sink = torch.randn(H, generator=g, device=dev)
     idx = make_indices(cfg, torch.Generator().manual_seed(0)).to(dev)
     o = torch.empty_like(q)
-    ws = torch.empty(workspace_bytes(cfg.b, cfg.m, cfg.topk, 0), dtype=torch.uint8, device=dev)
+    ws = torch.zeros(workspace_bytes(cfg.b, cfg.m, cfg.topk, 0), dtype=torch.uint8, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     if fp8:
         kv8, ks = quantize_kv_fp8(kv)

@@ -227,3 +227,19 @@ def test_index_faults_counted(variant):
     assert index_faults(reset=True) == expected
     assert index_faults() == 0
     assert_close(o, sparse_attn_oracle(q, kv, sink, idx, scale), what="faulty indices")
+
+
+def test_workspace_reuse_across_grids():
+    """Split rows are merged in the kernel by the last CTA to finish them
+    (per-CTA counters in the workspace, zeroed again by every call): one
+    workspace serves calls with different grids back to back."""
+    from sparse_attn import workspace_bytes
+    q, kv, sink, idx, scale = [t.cuda() if torch.is_tensor(t) else t
+                               for t in make_inputs("plumbing", seed=31)]
+    ref = sparse_attn_oracle(q.cpu(), kv.cpu(), sink.cpu(), idx.cpu(), scale)
+    ws = torch.zeros(workspace_bytes(1, 64, 64, q.device), dtype=torch.uint8, device="cuda")
+    for grid in (5, 37, 3, 64, 5, 0, 7):
+        o = torch.empty_like(q)
+        sparse_attn_out(o, q, kv, sink, idx, scale, ws, variant=SA_VARIANT_WS, grid=grid)
+        torch.cuda.synchronize()
+        assert_close(o, ref, what=f"grid {grid} (reused workspace)")
