@@ -331,6 +331,7 @@ int sa_fwd_fp8(const void* q, const void* kv8, const float* kv_scale, const floa
   p.tickets = reinterpret_cast<int*>(ws);
   p.part_acc = reinterpret_cast<float*>(ws + sa::kTicketBytes);
   p.part_ml = reinterpret_cast<float*>(ws + sa::kTicketBytes + sa::ws_acc_bytes(p.grid));
+  p.merge_in_kernel = p.units >= 2 * p.upt * p.grid ? 1 : 0;  // as for SA_VARIANT_WS
   e = sa::launch_fp8(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail_cuda(e);
   return SA_OK;

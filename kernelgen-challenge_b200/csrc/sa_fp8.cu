@@ -88,6 +88,9 @@ struct __align__(1024) Smem {
   // empty: the four consumer warps finished the unit; q_full: next row's Q
   uint64_t full[NSLOT], empty[NSLOT], q_full;
   int err;
+  // split rows this CTA merges after its last unit (at most its first and last row)
+  int n_merge;
+  int64_t merge_row[2];
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + manual 1 KiB alignment
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -219,6 +222,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     mbar_init(smem_u32(&S.q_full), 1);
     S.err = 0;
+    S.n_merge = 0;
     fence_mbar_init();
   }
   if (warp == 4 && lane == 0) tma_prefetch_desc(&q_map);
@@ -607,6 +611,17 @@ __global__ void __launch_bounds__(NT, 1)
             p.part_ml[pslot * kPartMlFloats + kHeads + g8] = l_lo;
             p.part_ml[pslot * kPartMlFloats + kHeads + g8 + 8] = l_hi;
           }
+          if (p.merge_in_kernel) {  // ticket of the split row, as in sa_ws.cu
+            const int64_t ts = t * upt;
+            const int64_t f = cta_of_unit(ts, p.units, G);
+            const int np = static_cast<int>(cta_of_unit(ts + upt - 1, p.units, G) - f + 1);
+            __threadfence();
+            named_bar(5, NCT);
+            if (tt == 0 && atomicAdd(p.tickets + f, 1) == np - 1) {
+              p.tickets[f] = 0;
+              S.merge_row[S.n_merge++] = t;
+            }
+          }
         }
       }
       if (seg_end) ++seg;
@@ -614,6 +629,25 @@ __global__ void __launch_bounds__(NT, 1)
       if (++kb == upt) {
         kb = 0;
         ++t;
+      }
+    }
+  }
+  // ---- every thread merges the split rows whose last part this CTA stored
+  __syncthreads();
+  if (S.n_merge > 0) {
+    __threadfence();
+    for (int r = 0; r < S.n_merge; ++r) {
+      const int64_t tr = S.merge_row[r], ts = tr * p.upt;
+      const int64_t f = cta_of_unit(ts, p.units, G);
+      const int np = static_cast<int>(cta_of_unit(ts + p.upt - 1, p.units, G) - f + 1);
+      const bool f_mid = unit_begin(f, p.units, G) < ts;
+#pragma unroll
+      for (int k0 = 0; k0 < kHeads * (kDim / 8); k0 += 4 * NT) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int k = k0 + e * NT + tid;
+          merge_split_row(p, f, np, f_mid, tr, k / (kDim / 8), (k % (kDim / 8)) * 8);
+        }
       }
     }
   }
@@ -719,7 +753,7 @@ cudaError_t launch_fp8(const Params& p, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, sa_fp8_fwd_kernel, p, q_map);
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess || p.merge_in_kernel) return e;
   return launch_combine(p, st);
 }
 
