@@ -12,15 +12,17 @@
 //   dkv[idx_t] += scale * ds_t q + p_t dO    (summed over heads; duplicates add)
 //   dsink  = -p_sink * D                     (summed over rows)
 //
-// One CTA (4 warps) per query row.  Its units of 64 gathered rows (the forward's
-// 128-byte-swizzled slab layout) stream through a 2-deep cp.async ring twice:
-//   pass A  S = Q.K^T (warp w: keys 16w..16w+15), online max / sum per head:
-//           the row's log-sum-exp including the sink
-//   pass B  S and dP = dO.V^T again (warp w: keys 16w..16w+15), P and
+// One CTA (8 warps, two per SM sub-partition) per query row.  Its units of 64
+// gathered rows (the forward's 128-byte-swizzled slab layout) stream through a
+// 2-deep cp.async ring twice:
+//   pass A  S = Q.K^T (warp w: keys 8w..8w+7), online max / sum per head: the
+//           row's log-sum-exp including the sink
+//   pass B  S and dP = dO.V^T again (warp w: keys 8w..8w+7), P and
 //           dS = P (dP - D) * scale into shared memory (bf16), then
-//           dq[16 x 128w..] += dS . K       (registers, whole row)
-//           dkv chunk [16 keys x 64 cols] = dS^T . Q + P^T . dO per warp, added
-//           into an fp32 gradient buffer with 8-byte atomics (masked slots skip)
+//           dq[16 x 64w..64w+63] += dS . K   (registers, whole row)
+//           dkv [16 keys of group w & 3 x 256 columns of half w >> 2]
+//             = dS^T . Q + P^T . dO in 64-column chunks, added into an fp32
+//             gradient buffer with 8-byte atomics (masked slots skip)
 // All products are bf16 warp MMAs with fp32 accumulation.
 #include "sa_common.cuh"
 
@@ -28,7 +30,7 @@ namespace sa {
 namespace bwd_path {
 
 constexpr int UK = 64;                      // keys per unit
-constexpr int NW = 4;                       // warps
+constexpr int NW = 8;                       // warps
 constexpr int NT = NW * 32;
 constexpr int SLOT_BYTES = UK * kDim * 2;   // 64 KiB
 constexpr int SLAB_BYTES = UK * 128;        // [64 keys x 64 cols]
@@ -116,13 +118,13 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
     }
   }
 
-  // ---- gather of unit u into ring slot s: thread copies chunk tid & 63 of the
-  // rows of parity tid >> 6
+  // ---- gather of unit u into ring slot s: thread copies chunk tid & 63 of
+  // rows (tid >> 6) + 4k
   auto issue = [&](int64_t u, int s) {
     const int c = tid & 63, par = tid >> 6, j = c >> 3, cc = c & 7;
     const uint32_t dst0 = smem_u32(S.ring[s]) + j * SLAB_BYTES;
-    for (int k = 0; k < UK / 2; ++k) {
-      const int r = par + 2 * k;
+    for (int k = 0; k < UK / 4; ++k) {
+      const int r = par + 4 * k;
       const int64_t key = u * UK + r;
       const int32_t id = key < p.topk ? __ldg(irow + key * p.i_sk) : -1;
       const bool v = id >= 0 && (int64_t)id < p.kv_len;
@@ -133,12 +135,11 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
     cp_async_commit();
   };
 
-  // S (or dP with the dO tile) for keys 16w + 8nt + ..: sa[nt][z] split accumulators
-  auto scores = [&](uint32_t sb, uint32_t abase, float (&sa)[2][2][4]) {
+  // S (or dP with the dO tile) for keys 8w..8w+7: sa[z] split accumulators
+  // (even / odd k-steps)
+  auto scores = [&](uint32_t sb, uint32_t abase, float (&sa)[2][4]) {
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int z = 0; z < 2; ++z) sa[nt][z][0] = sa[nt][z][1] = sa[nt][z][2] = sa[nt][z][3] = 0.f;
+    for (int z = 0; z < 2; ++z) sa[z][0] = sa[z][1] = sa[z][2] = sa[z][3] = 0.f;
     const int arow = (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll 4
     for (int kp = 0; kp < 16; ++kp) {  // columns 32kp..32kp+31
@@ -146,21 +147,18 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
       ldmatrix_x4(a0, abase + t_chunk(arow, 4 * kp + (lane >> 4)));
       ldmatrix_x4(a1, abase + t_chunk(arow, 4 * kp + 2 + (lane >> 4)));
       const int slab = kp >> 1, c0 = (kp & 1) * 4;
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const int key = 16 * warp + 8 * nt + (lane & 7);
-        uint32_t kf[4];
-        ldmatrix_x4(kf, sb + slab * SLAB_BYTES + key * 128 + (((c0 + (lane >> 3)) ^ (key & 7)) << 4));
-        mma_16816(sa[nt][0], a0, kf[0], kf[1]);
-        mma_16816(sa[nt][1], a1, kf[2], kf[3]);
-      }
+      const int key = 8 * warp + (lane & 7);
+      uint32_t kf[4];
+      ldmatrix_x4(kf, sb + slab * SLAB_BYTES + key * 128 + (((c0 + (lane >> 3)) ^ (key & 7)) << 4));
+      mma_16816(sa[0], a0, kf[0], kf[1]);
+      mma_16816(sa[1], a1, kf[2], kf[3]);
     }
   };
 
   float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;  // pass A, this lane's keys
-  float dq[16][4];  // dq[heads g8, g8+8][128w + 8nt + 2q4 + {0,1}]
+  float dq[8][4];  // dq[heads g8, g8+8][64w + 8nt + 2q4 + {0,1}]
 #pragma unroll
-  for (int nt = 0; nt < 16; ++nt) dq[nt][0] = dq[nt][1] = dq[nt][2] = dq[nt][3] = 0.f;
+  for (int nt = 0; nt < 8; ++nt) dq[nt][0] = dq[nt][1] = dq[nt][2] = dq[nt][3] = 0.f;
 
   if (U > 0) issue(0, 0);
   for (int64_t i = 0; i < 2 * U; ++i) {
@@ -209,60 +207,51 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
       }
       __syncthreads();
     }
-    float sa[2][2][4];
+    float sa[2][4];
     scores(sb, qbase, sa);
-    float x[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      const int key = 16 * warp + 8 * nt + 2 * q4;
+    float x[4];  // [0,1] head g8, [2,3] head g8+8; keys 8w + 2q4 + {0,1}
+    {
+      const int key = 8 * warp + 2 * q4;
       const bool v0 = S.ids[s][key] >= 0, v1 = S.ids[s][key + 1] >= 0;
-      x[nt][0] = v0 ? (sa[nt][0][0] + sa[nt][1][0]) * p.scale_log2 : -INFINITY;
-      x[nt][1] = v1 ? (sa[nt][0][1] + sa[nt][1][1]) * p.scale_log2 : -INFINITY;
-      x[nt][2] = v0 ? (sa[nt][0][2] + sa[nt][1][2]) * p.scale_log2 : -INFINITY;
-      x[nt][3] = v1 ? (sa[nt][0][3] + sa[nt][1][3]) * p.scale_log2 : -INFINITY;
+      x[0] = v0 ? (sa[0][0] + sa[1][0]) * p.scale_log2 : -INFINITY;
+      x[1] = v1 ? (sa[0][1] + sa[1][1]) * p.scale_log2 : -INFINITY;
+      x[2] = v0 ? (sa[0][2] + sa[1][2]) * p.scale_log2 : -INFINITY;
+      x[3] = v1 ? (sa[0][3] + sa[1][3]) * p.scale_log2 : -INFINITY;
     }
     if (!passB) {
       // online max / sum of this lane's keys
-      const float b_lo = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
-      const float b_hi = fmaxf(fmaxf(x[0][2], x[0][3]), fmaxf(x[1][2], x[1][3]));
-      const float n_lo = fmaxf(m_lo, b_lo), n_hi = fmaxf(m_hi, b_hi);
+      const float n_lo = fmaxf(m_lo, fmaxf(x[0], x[1])), n_hi = fmaxf(m_hi, fmaxf(x[2], x[3]));
       if (n_lo != -INFINITY) {
-        l_lo = l_lo * exp2f(m_lo - n_lo) + exp2f(x[0][0] - n_lo) + exp2f(x[0][1] - n_lo) +
-               exp2f(x[1][0] - n_lo) + exp2f(x[1][1] - n_lo);
+        l_lo = l_lo * exp2f(m_lo - n_lo) + exp2f(x[0] - n_lo) + exp2f(x[1] - n_lo);
         m_lo = n_lo;
       }
       if (n_hi != -INFINITY) {
-        l_hi = l_hi * exp2f(m_hi - n_hi) + exp2f(x[0][2] - n_hi) + exp2f(x[0][3] - n_hi) +
-               exp2f(x[1][2] - n_hi) + exp2f(x[1][3] - n_hi);
+        l_hi = l_hi * exp2f(m_hi - n_hi) + exp2f(x[2] - n_hi) + exp2f(x[3] - n_hi);
         m_hi = n_hi;
       }
       __syncthreads();  // slot s free for the next issue
       continue;
     }
     // ---- pass B: P, dP, dS
-    float dpa[2][2][4];
+    float dpa[2][4];
     scores(sb, dobase, dpa);
     {
       const float M_lo = S.M[g8], M_hi = S.M[g8 + 8];
       const float iz_lo = S.invZ[g8], iz_hi = S.invZ[g8 + 8];
       const float D_lo = S.D[g8], D_hi = S.D[g8 + 8];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const float p0 = exp2f(x[nt][0] - M_lo) * iz_lo, p1 = exp2f(x[nt][1] - M_lo) * iz_lo;
-        const float p2 = exp2f(x[nt][2] - M_hi) * iz_hi, p3 = exp2f(x[nt][3] - M_hi) * iz_hi;
-        const float d0 = p0 * (dpa[nt][0][0] + dpa[nt][1][0] - D_lo) * bp.scale;
-        const float d1 = p1 * (dpa[nt][0][1] + dpa[nt][1][1] - D_lo) * bp.scale;
-        const float d2 = p2 * (dpa[nt][0][2] + dpa[nt][1][2] - D_hi) * bp.scale;
-        const float d3 = p3 * (dpa[nt][0][3] + dpa[nt][1][3] - D_hi) * bp.scale;
-        const int ch = 2 * warp + nt;
-        *reinterpret_cast<uint32_t*>(S.p + p_chunk(g8, ch) + 4 * q4) = pack_bf16x2(p0, p1);
-        *reinterpret_cast<uint32_t*>(S.p + p_chunk(g8 + 8, ch) + 4 * q4) = pack_bf16x2(p2, p3);
-        *reinterpret_cast<uint32_t*>(S.ds + p_chunk(g8, ch) + 4 * q4) = pack_bf16x2(d0, d1);
-        *reinterpret_cast<uint32_t*>(S.ds + p_chunk(g8 + 8, ch) + 4 * q4) = pack_bf16x2(d2, d3);
-      }
+      const float p0 = exp2f(x[0] - M_lo) * iz_lo, p1 = exp2f(x[1] - M_lo) * iz_lo;
+      const float p2 = exp2f(x[2] - M_hi) * iz_hi, p3 = exp2f(x[3] - M_hi) * iz_hi;
+      const float d0 = p0 * (dpa[0][0] + dpa[1][0] - D_lo) * bp.scale;
+      const float d1 = p1 * (dpa[0][1] + dpa[1][1] - D_lo) * bp.scale;
+      const float d2 = p2 * (dpa[0][2] + dpa[1][2] - D_hi) * bp.scale;
+      const float d3 = p3 * (dpa[0][3] + dpa[1][3] - D_hi) * bp.scale;
+      *reinterpret_cast<uint32_t*>(S.p + p_chunk(g8, warp) + 4 * q4) = pack_bf16x2(p0, p1);
+      *reinterpret_cast<uint32_t*>(S.p + p_chunk(g8 + 8, warp) + 4 * q4) = pack_bf16x2(p2, p3);
+      *reinterpret_cast<uint32_t*>(S.ds + p_chunk(g8, warp) + 4 * q4) = pack_bf16x2(d0, d1);
+      *reinterpret_cast<uint32_t*>(S.ds + p_chunk(g8 + 8, warp) + 4 * q4) = pack_bf16x2(d2, d3);
     }
     __syncthreads();  // P and dS of all 64 keys written
-    // ---- dq[16 x 128w..128w+127] += dS[16 x 64] . K[64 x 128]
+    // ---- dq[16 x 64w..64w+63] += dS[16 x 64] . K[64 x 64] (slab w)
 #pragma unroll
     for (int kst = 0; kst < 4; ++kst) {
       uint32_t da[4];
@@ -272,24 +261,25 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
       }
       const int kr = kst * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
-      for (int np = 0; np < 8; ++np) {
-        const int slab = 2 * warp + (np >> 2);
-        const int ch = ((np & 3) << 1) + (lane >> 4);
+      for (int np = 0; np < 4; ++np) {
+        const int ch = (np << 1) + (lane >> 4);
         uint32_t vb[4];
-        ldmatrix_x4_trans(vb, sb + slab * SLAB_BYTES + kr * 128 + ((ch ^ (kr & 7)) << 4));
+        ldmatrix_x4_trans(vb, sb + warp * SLAB_BYTES + kr * 128 + ((ch ^ (kr & 7)) << 4));
         mma_16816(dq[2 * np], da, vb[0], vb[1]);
         mma_16816(dq[2 * np + 1], da, vb[2], vb[3]);
       }
     }
-    // ---- dkv[keys 16w..16w+15][cols] = dS^T . Q + P^T . dO, 64 columns at a time
+    // ---- dkv[keys 16kg..16kg+15][columns 256ch..+255] = dS^T . Q + P^T . dO,
+    //      64 columns at a time (kg = w & 3, ch = w >> 2)
     {
+      const int kg = warp & 3, chh = warp >> 2;
       // A-fragments (rows = keys, k = heads) by transposed loads of the
-      // [head][key] tiles: matrices (heads 0-7 | 8-15) x (keys 16w..+7 | 16w+8..+15)
-      const int mt = lane >> 3, hr = (lane & 7) + 8 * (mt >> 1), kc = 2 * warp + (mt & 1);
+      // [head][key] tiles: matrices (heads 0-7 | 8-15) x (keys 16kg..+7 | 16kg+8..+15)
+      const int mt = lane >> 3, hr = (lane & 7) + 8 * (mt >> 1), kc = 2 * kg + (mt & 1);
       uint32_t ad[4], ap[4];
       ldmatrix_x4_trans(ad, dsbase + p_chunk(hr, kc));
       ldmatrix_x4_trans(ap, pbase + p_chunk(hr, kc));
-      const int key_lo = 16 * warp + g8, key_hi = key_lo + 8;
+      const int key_lo = 16 * kg + g8, key_hi = key_lo + 8;
       const int32_t id_lo = S.ids[s][key_lo], id_hi = S.ids[s][key_hi];
       float* dlo = bp.dkv + tb * bp.dkv_sb + (int64_t)(id_lo < 0 ? 0 : id_lo) * bp.dkv_sn;
       float* dhi = bp.dkv + tb * bp.dkv_sb + (int64_t)(id_hi < 0 ? 0 : id_hi) * bp.dkv_sn;
@@ -297,7 +287,7 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
       // tiles: matrices (heads 0-7 | 8-15) x (columns n0..n0+7 | n0+8..n0+15)
       const int br = (lane & 7) + 8 * (mt & 1), bcol = (mt >> 1);
 #pragma unroll 1
-      for (int cb = 0; cb < kDim / 64; ++cb) {
+      for (int cb = 4 * chh; cb < 4 * chh + 4; ++cb) {
         float acc[8][4];
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
@@ -326,8 +316,8 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
   // ---- dq of this row (the scale is already in dS)
   __nv_bfloat16* dqr = bp.dq + row * (kHeads * kDim);
 #pragma unroll
-  for (int nt = 0; nt < 16; ++nt) {
-    const int d = 128 * warp + 8 * nt + 2 * q4;
+  for (int nt = 0; nt < 8; ++nt) {
+    const int d = 64 * warp + 8 * nt + 2 * q4;
     *reinterpret_cast<uint32_t*>(dqr + g8 * kDim + d) = pack_bf16x2(dq[nt][0], dq[nt][1]);
     *reinterpret_cast<uint32_t*>(dqr + (g8 + 8) * kDim + d) = pack_bf16x2(dq[nt][2], dq[nt][3]);
   }
