@@ -74,3 +74,75 @@ def test_op_rejects_cpu_tensors_and_bad_rank():
         sparse_attn.sparse_attn(q, kv, sink, idx, 0.1)
     with pytest.raises(AssertionError):
         sparse_attn.sparse_attn(q[0], kv, sink, idx, 0.1)
+
+
+def _i64(*v):
+    return _lib.i64_array(list(v))
+
+
+def test_fp8_entries_validate_before_any_gpu_work():
+    L = _lib.lib()
+    st = _i64(8192, 8192, 512, 1)
+
+    def fwd8(q=16, kv8=16, ks=16, b=1, h=16, kv_strides=(2048, 512, 1)):
+        return L.sa_fwd_fp8(q, kv8, ks, 16, 16, 16, b, 1, h, 512, 4, 4, st, _i64(*kv_strides),
+                            _i64(4, 1), _i64(4, 4, 1), st, 1.0, None, 0, None, 0)
+    assert fwd8(b=0) == _lib.SA_OK
+    assert fwd8(b=-1) == _lib.SA_ERR_INVALID_ARG
+    assert fwd8(h=8) == _lib.SA_ERR_UNSUPPORTED
+    assert fwd8(ks=0) == _lib.SA_ERR_INVALID_ARG
+    assert fwd8(kv8=8) == _lib.SA_ERR_INVALID_ARG                  # misaligned rows
+    assert fwd8(kv_strides=(2048, 520, 1)) == _lib.SA_ERR_INVALID_ARG  # row stride not 16 B
+
+    def quant(kv=16, d=512, b=1):
+        return L.sa_quantize_kv_fp8(kv, 16, 16, b, 4, d, _i64(2048, 512, 1), _i64(2048, 512, 1),
+                                    _i64(4, 1), None)
+    assert quant(b=0) == _lib.SA_OK
+    assert quant(d=256) == _lib.SA_ERR_UNSUPPORTED
+    assert quant(kv=0) == _lib.SA_ERR_INVALID_ARG
+
+
+def test_backward_entry_validates_before_any_gpu_work():
+    L = _lib.lib()
+    st = _i64(8192, 8192, 512, 1)
+
+    def bwd(dq=16, dkv=16, b=1, h=16, dkv_strides=(2048, 512, 1)):
+        return L.sa_bwd(16, 16, 16, 16, 16, 16, dq, dkv, 16, b, 1, h, 512, 4, 4, st,
+                        _i64(2048, 512, 1), _i64(4, 4, 1), st, _i64(*dkv_strides), 1.0, None)
+    assert bwd(b=0) == _lib.SA_OK
+    assert bwd(h=4) == _lib.SA_ERR_UNSUPPORTED
+    assert bwd(dq=0) == _lib.SA_ERR_INVALID_ARG
+    assert bwd(dkv=4) == _lib.SA_ERR_INVALID_ARG                   # misaligned fp32 buffer
+    assert bwd(dkv_strides=(2048, 511, 1)) == _lib.SA_ERR_INVALID_ARG
+
+
+def test_sinkhorn_entry_validates_before_any_gpu_work():
+    L = _lib.lib()
+
+    def hcs(n=1, hc=4, iters=20, mixes=16, stride=24, out=16):
+        return L.hcs_split_sinkhorn(mixes, 16, 16, out, 16, 16, n, stride, hc, iters, 1e-6, None)
+    assert hcs(n=0) == 0
+    assert hcs(n=-1) == -1
+    assert hcs(hc=3) == -4
+    assert hcs(iters=0) == -1
+    assert hcs(mixes=0) == -1
+    assert hcs(stride=23) == -1
+    assert hcs(out=8) == -1                                          # misaligned outputs
+
+
+def test_new_ops_reject_cpu_tensors():
+    q = torch.zeros(1, 1, 16, 512, dtype=torch.bfloat16)
+    kv = torch.zeros(1, 4, 512, dtype=torch.bfloat16)
+    sink = torch.zeros(16)
+    idx = torch.zeros(1, 1, 2, dtype=torch.int32)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        sparse_attn.sparse_attn_fp8(q, kv.to(torch.float8_e4m3fn), torch.ones(1, 4), sink, idx, 0.1)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        sparse_attn.quantize_kv_fp8(kv)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        sparse_attn.sparse_attn_backward(q, kv, sink, idx, 0.1, q, q)
+    with pytest.raises(AssertionError):
+        sparse_attn.hc_split_sinkhorn(torch.zeros(1, 1, 15), torch.zeros(3), torch.zeros(15),
+                                      hc_mult=3)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        sparse_attn.hc_split_sinkhorn(torch.zeros(1, 1, 24), torch.zeros(3), torch.zeros(24))
