@@ -82,8 +82,20 @@ int sa_fwd_fp8(const void* q, const void* kv8, const float* kv_scale, const floa
                const int64_t idx_strides[3], const int64_t o_strides[4], float scale,
                void* workspace, size_t workspace_bytes, void* stream, int grid_ctas);
 
+/* Training forward: sa_fwd (warp-specialized kernel) that also writes
+ * lse[b*m][16] (fp32): log2 of each row's full softmax denominator, the sink
+ * included, in the log2 domain of the scores (weight of slot t =
+ * 2^(s_t * scale * log2(e) - lse)).  sa_bwd then needs one pass instead of
+ * two.  No counterpart in the reference, which has no backward. */
+int sa_fwd_train(const void* q, const void* kv, const float* sink, const int32_t* idx, void* o,
+                 float* lse, int64_t b, int64_t m, int64_t h, int64_t d, int64_t kv_len,
+                 int64_t topk, const int64_t q_strides[4], const int64_t kv_strides[3],
+                 const int64_t idx_strides[3], const int64_t o_strides[4], float scale,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* Backward pass: gradients of sa_fwd.  Given q, kv, sink, idx, the forward's
- * output o and the upstream gradient dout (laid out like o: o_strides), writes
+ * output o, its lse from sa_fwd_train (or NULL: recomputed by a first pass)
+ * and the upstream gradient dout (laid out like o: o_strides), writes
  * dq (bf16, contiguous [b, m, 16, 512]) and ADDS into dkv (fp32 [b, kv_len, 512],
  * element strides dkv_strides, 8-byte aligned) and dsink (fp32 [16]); zero
  * those two first for a plain gradient.  Masked slots (-1 or out of range)
@@ -91,7 +103,8 @@ int sa_fwd_fp8(const void* q, const void* kv8, const float* kv_scale, const floa
  * the reference forward (track-01/reference/reference.py:24-40), which has no
  * backward of its own. */
 int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx, const void* o,
-           const void* dout, void* dq, float* dkv, float* dsink, int64_t b, int64_t m, int64_t h,
+           const void* dout, const float* lse, void* dq, float* dkv, float* dsink, int64_t b,
+           int64_t m, int64_t h,
            int64_t d, int64_t kv_len, int64_t topk, const int64_t q_strides[4],
            const int64_t kv_strides[3], const int64_t idx_strides[3], const int64_t o_strides[4],
            const int64_t dkv_strides[3], float scale, void* stream);

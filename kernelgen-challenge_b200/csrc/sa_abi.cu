@@ -157,12 +157,13 @@ size_t sa_workspace_bytes(int64_t b, int64_t m, int64_t topk, int device) {
   return sa::workspace_bytes_for_grid(static_cast<int>(grid));
 }
 
-int sa_fwd_ex(const void* q, const void* kv, const float* sink, const int32_t* idx, void* o,
-              int64_t b, int64_t m, int64_t h, int64_t d, int64_t kv_len, int64_t topk,
-              const int64_t q_strides[4], const int64_t kv_strides[3],
-              const int64_t idx_strides[3], const int64_t o_strides[4], float scale,
-              void* workspace, size_t workspace_bytes, void* stream, int variant,
-              int grid_ctas) {
+// sa_fwd_ex and sa_fwd_train; lse (nullable) is the training output.
+static int fwd_impl(const void* q, const void* kv, const float* sink, const int32_t* idx, void* o,
+                    int64_t b, int64_t m, int64_t h, int64_t d, int64_t kv_len, int64_t topk,
+                    const int64_t q_strides[4], const int64_t kv_strides[3],
+                    const int64_t idx_strides[3], const int64_t o_strides[4], float scale,
+                    void* workspace, size_t workspace_bytes, void* stream, int variant,
+                    int grid_ctas, float* lse) {
   t_last_cuda_error = 0;
   if (b < 0 || m < 0 || kv_len < 0 || topk < 0) return SA_ERR_INVALID_ARG;
   if (h != sa::kHeads || d != sa::kDim) return SA_ERR_UNSUPPORTED;
@@ -230,6 +231,11 @@ int sa_fwd_ex(const void* q, const void* kv, const float* sink, const int32_t* i
   } else {
     return SA_ERR_INVALID_ARG;
   }
+  if (lse != nullptr) {  // only the warp-specialized kernel writes it
+    if (variant != SA_VARIANT_WS) return SA_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(lse) & 3u) != 0) return SA_ERR_INVALID_ARG;
+  }
+  p.lse = lse;
   p.upt = ceil_div(topk > 0 ? topk : 1, unit_keys);  // topk == 0: one all-masked unit
   p.units = b * m * p.upt;
 
@@ -338,7 +344,8 @@ int sa_fwd_fp8(const void* q, const void* kv8, const float* kv_scale, const floa
 }
 
 int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx, const void* o,
-           const void* dout, void* dq, float* dkv, float* dsink, int64_t b, int64_t m, int64_t h,
+           const void* dout, const float* lse, void* dq, float* dkv, float* dsink, int64_t b,
+           int64_t m, int64_t h,
            int64_t d, int64_t kv_len, int64_t topk, const int64_t q_strides[4],
            const int64_t kv_strides[3], const int64_t idx_strides[3], const int64_t o_strides[4],
            const int64_t dkv_strides[3], float scale, void* stream) {
@@ -388,6 +395,7 @@ int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx,
   p.o_sm = o_strides[1];
   p.o_sh = o_strides[2];
   p.scale_log2 = scale * sa::kLog2e;
+  p.lse = const_cast<float*>(lse);  // read only
   e = sa::launch_bwd(p, static_cast<const __nv_bfloat16*>(dout), static_cast<__nv_bfloat16*>(dq),
                      dkv, dsink, dkv_strides[0], dkv_strides[1], scale,
                      static_cast<cudaStream_t>(stream));
@@ -432,6 +440,28 @@ int sa_quantize_kv_fp8(const void* kv, void* kv8, float* kv_scale, int64_t b, in
   e = sa::launch_quantize_fp8(qp, di->sms, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail_cuda(e);
   return SA_OK;
+}
+
+int sa_fwd_ex(const void* q, const void* kv, const float* sink, const int32_t* idx, void* o,
+              int64_t b, int64_t m, int64_t h, int64_t d, int64_t kv_len, int64_t topk,
+              const int64_t q_strides[4], const int64_t kv_strides[3],
+              const int64_t idx_strides[3], const int64_t o_strides[4], float scale,
+              void* workspace, size_t workspace_bytes, void* stream, int variant,
+              int grid_ctas) {
+  return fwd_impl(q, kv, sink, idx, o, b, m, h, d, kv_len, topk, q_strides, kv_strides,
+                  idx_strides, o_strides, scale, workspace, workspace_bytes, stream, variant,
+                  grid_ctas, nullptr);
+}
+
+int sa_fwd_train(const void* q, const void* kv, const float* sink, const int32_t* idx, void* o,
+                 float* lse, int64_t b, int64_t m, int64_t h, int64_t d, int64_t kv_len,
+                 int64_t topk, const int64_t q_strides[4], const int64_t kv_strides[3],
+                 const int64_t idx_strides[3], const int64_t o_strides[4], float scale,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  if (lse == nullptr) return SA_ERR_INVALID_ARG;
+  return fwd_impl(q, kv, sink, idx, o, b, m, h, d, kv_len, topk, q_strides, kv_strides,
+                  idx_strides, o_strides, scale, workspace, workspace_bytes, stream,
+                  SA_VARIANT_WS, 0, lse);
 }
 
 int sa_fwd(const void* q, const void* kv, const float* sink, const int32_t* idx, void* o,

@@ -160,8 +160,22 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
 #pragma unroll
   for (int nt = 0; nt < 8; ++nt) dq[nt][0] = dq[nt][1] = dq[nt][2] = dq[nt][3] = 0.f;
 
-  if (U > 0) issue(0, 0);
-  for (int64_t i = 0; i < 2 * U; ++i) {
+  // with the forward's log-sum-exp (sa_fwd_train) pass A is skipped
+  const int64_t i0 = p.lse != nullptr ? U : 0;
+  if (p.lse != nullptr && tid < kHeads) {
+    const float sl2 = __ldg(p.sink + tid) * kLog2e;
+    const float L = p.lse[row * kHeads + tid];
+    S.M[tid] = L;
+    S.invZ[tid] = 1.f;
+    // dsink = -p_sink * D once the D of this row is in shared memory (below)
+    S.red[0][0][tid] = exp2f(sl2 - L);
+  }
+  if (i0 < 2 * U) issue(i0 % U, i0 & 1);
+  if (p.lse != nullptr) {
+    __syncthreads();  // D and the sink weights
+    if (tid < kHeads) atomicAdd(bp.dsink + tid, -S.red[0][0][tid] * S.D[tid]);
+  }
+  for (int64_t i = i0; i < 2 * U; ++i) {
     const int s = static_cast<int>(i & 1);
     if (i + 1 < 2 * U) {
       issue((i + 1) % U, s ^ 1);
@@ -172,7 +186,7 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
     __syncthreads();  // unit i landed (and, at i = 0, the Q / dO tiles and D)
     const uint32_t sb = smem_u32(S.ring[s]);
     const bool passB = i >= U;
-    if (i == U) {
+    if (i == U && i0 == 0) {
       // ---- end of pass A: M and 1/Z per head, including the sink
 #pragma unroll
       for (int off = 1; off <= 2; off <<= 1) {

@@ -61,7 +61,19 @@ struct Params {
   // last one merges the row and zeroes the word again (sa_ws.cu).
   int* tickets;
   int merge_in_kernel;  // sa_ws only: merge split rows by ticket instead of the combine kernel
+  // Optional (sa_fwd_train, ws kernel): lse[row][h] = log2 of the row's full
+  // softmax denominator, the sink included, in the log2 domain of the scores
+  // (p_t = 2^(s_t * scale * log2(e) - lse)); the backward pass reads it.
+  float* lse;
 };
+
+// log2 of the full denominator for a running max m and sum l (relative to m),
+// with the sink as the extra logit; all in the log2 domain.
+__device__ __forceinline__ float row_lse2(float m_run, float l_run, float sink_log2) {
+  const float M = fmaxf(m_run, sink_log2);
+  const float den = (m_run == -INFINITY ? 0.f : l_run * exp2f(m_run - M)) + exp2f(sink_log2 - M);
+  return M + log2f(den);
+}
 
 // Workspace layout shared by the host (sizing) and the kernels.
 constexpr size_t kPartAccFloats = (size_t)kHeads * kDim;
@@ -281,6 +293,7 @@ __device__ __forceinline__ void merge_split_row(const Params& p, int64_t f, int 
     M = Mb;
   }
   const float inv = 1.f / den;
+  if (p.lse != nullptr && d0 == 0) p.lse[t * kHeads + h] = M + log2f(den);
   const int64_t tb = t / p.m, tm = t - tb * p.m;
   uint4 w;
   w.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);

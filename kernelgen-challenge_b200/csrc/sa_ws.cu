@@ -117,6 +117,9 @@ __device__ __forceinline__ uint32_t p_chunk(int h, int ch) {
   return h * 128 + ((ch ^ (h & 7)) << 4);
 }
 
+// kLse: also write the row log-sum-exp (training forward); a separate
+// instance, so the inference kernel carries no trace of it.
+template <bool kLse>
 __global__ void __launch_bounds__(NT, 1)
     sa_ws_fwd_kernel(const Params p, const __grid_constant__ CUtensorMap q_map) {
   extern __shared__ uint8_t smem_raw[];
@@ -400,6 +403,10 @@ __global__ void __launch_bounds__(NT, 1)
         if (seg_kb0 == 0 && kb == upt - 1) {
           const float f_lo = sink_factor(m_lo, l_lo, __ldg(p.sink + g8) * kLog2e);
           const float f_hi = sink_factor(m_hi, l_hi, __ldg(p.sink + g8 + 8) * kLog2e);
+          if (kLse && c == 0 && q4 == 0) {
+            p.lse[t * kHeads + g8] = row_lse2(m_lo, l_lo, __ldg(p.sink + g8) * kLog2e);
+            p.lse[t * kHeads + g8 + 8] = row_lse2(m_hi, l_hi, __ldg(p.sink + g8 + 8) * kLog2e);
+          }
           __nv_bfloat16* ob = p.o + tb * p.o_sb + tm * p.o_sm;
 #pragma unroll
           for (int nt = 0; nt < 16; ++nt) {
@@ -513,8 +520,11 @@ cudaError_t launch_ws(const Params& p, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   static PerDeviceOnce attr_once;
   e = once_per_device(attr_once, [] {
-    return cudaFuncSetAttribute(sa_ws_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)kSmemBytes);
+    const cudaError_t e1 = cudaFuncSetAttribute(
+        sa_ws_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e1 != cudaSuccess) return e1;
+    return cudaFuncSetAttribute(sa_ws_fwd_kernel<true>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
   });
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -527,7 +537,8 @@ cudaError_t launch_ws(const Params& p, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, sa_ws_fwd_kernel, p, q_map);
+  e = p.lse != nullptr ? cudaLaunchKernelEx(&cfg, sa_ws_fwd_kernel<true>, p, q_map)
+                       : cudaLaunchKernelEx(&cfg, sa_ws_fwd_kernel<false>, p, q_map);
   if (e != cudaSuccess || p.merge_in_kernel) return e;
   return launch_combine(p, st);
 }

@@ -47,7 +47,9 @@ SIGNATURES = {
                                   ctypes.c_size_t, _P, ctypes.c_int]),
     "sa_quantize_kv_fp8": (ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _I64P, _I64P, _I64P,
                                           _P]),
-    "sa_bwd": (ctypes.c_int, [_P] * 9 + [_I64] * 6 + [_I64P] * 5 + [ctypes.c_float, _P]),
+    "sa_bwd": (ctypes.c_int, [_P] * 10 + [_I64] * 6 + [_I64P] * 5 + [ctypes.c_float, _P]),
+    "sa_fwd_train": (ctypes.c_int, [_P] * 6 + [_I64] * 6 + [_I64P] * 4
+                     + [ctypes.c_float, _P, ctypes.c_size_t, _P]),
     # include/hc_sinkhorn.h
     "hcs_split_sinkhorn": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _I64, _I64, ctypes.c_int,
                                           ctypes.c_int, ctypes.c_float, _P]),

@@ -162,12 +162,45 @@ def _(q, kv, attn_sink, topk_idxs, scale):
     return q.new_empty(q.shape)
 
 
-def sparse_attn_backward(q, kv, attn_sink, topk_idxs, scale, o, do):
+def _forward_train(q, kv, attn_sink, topk_idxs, scale):
+    """(o, lse): the forward through ``sa_fwd_train``, which also returns the
+    per-row, per-head log2 softmax denominator (fp32 [b, m, h]) for the
+    backward pass."""
+    _validate(q, kv, attn_sink, topk_idxs)
+    h = q.shape[2]
+    if h < _KERNEL_HEADS:
+        qp = q.new_zeros(*q.shape[:2], _KERNEL_HEADS, q.shape[3])
+        qp[:, :, :h] = q
+        sp = attn_sink.new_zeros(_KERNEL_HEADS)
+        sp[:h] = attn_sink
+        o, lse = _forward_train(qp, kv, sp, topk_idxs, scale)
+        return o[:, :, :h].contiguous(), lse[:, :, :h].contiguous()
+    q_c = q if _row_ok(q) else q.contiguous()
+    kv_c = kv if _row_ok(kv) else kv.contiguous()
+    b, m, _, d = q.shape
+    o = torch.empty(b, m, h, d, dtype=q.dtype, device=q.device)
+    lse = torch.empty(b, m, h, dtype=torch.float32, device=q.device)
+    if o.numel() == 0:
+        return o, lse
+    with torch.cuda.device(q.device):
+        st = torch.cuda.current_stream(q.device)
+        ws = _cached_workspace(q.device, st, workspace_bytes(b, m, topk_idxs.shape[-1], q.device))
+        _lib.check(_lib.lib().sa_fwd_train(
+            q_c.data_ptr(), kv_c.data_ptr(), attn_sink.contiguous().data_ptr(),
+            topk_idxs.data_ptr(), o.data_ptr(), lse.data_ptr(), b, m, h, d, kv.shape[1],
+            topk_idxs.shape[-1], _lib.i64_array(q_c.stride()), _lib.i64_array(kv_c.stride()),
+            _lib.i64_array(topk_idxs.stride()), _lib.i64_array(o.stride()), float(scale),
+            ws.data_ptr(), ws.numel(), st.cuda_stream))
+    return o, lse
+
+
+def sparse_attn_backward(q, kv, attn_sink, topk_idxs, scale, o, do, lse=None):
     """Gradients of ``sparse_attn`` (``sa_bwd`` in ``libsparse_attn.so``).
 
     Given the forward's inputs, its output ``o`` and the upstream gradient
     ``do``, returns ``(dq, dkv, dsink)`` with the dtypes of q, kv and
-    attn_sink.  Masked slots contribute nothing; duplicated indices add.  The
+    attn_sink.  ``lse`` (from the training forward) saves the kernel its first
+    pass over the gathered rows.  Masked slots contribute nothing; duplicated indices add.  The
     reference has no backward: this is the gradient of its forward
     (track-01/reference/reference.py:24-40).
     """
@@ -176,10 +209,11 @@ def sparse_attn_backward(q, kv, attn_sink, topk_idxs, scale, o, do):
     if h < _KERNEL_HEADS:  # zero heads: zero gradients of their own, none into kv
         pad = _KERNEL_HEADS - h
         zq = q.new_zeros(*q.shape[:2], pad, q.shape[3])
+        lse_p = None if lse is None else torch.cat([lse, lse.new_zeros(*lse.shape[:2], pad)], 2)
         dq, dkv, dsink = sparse_attn_backward(
             torch.cat([q, zq], 2), kv, torch.cat([attn_sink, attn_sink.new_zeros(pad)]),
             topk_idxs, scale, torch.cat([o, torch.zeros_like(zq)], 2),
-            torch.cat([do, torch.zeros_like(zq)], 2))
+            torch.cat([do, torch.zeros_like(zq)], 2), lse_p)
         return dq[:, :, :h].contiguous(), dkv, dsink[:h].contiguous()
     b, m, _, d = q.shape
     q_c = q if _row_ok(q) else q.contiguous()
@@ -192,9 +226,11 @@ def sparse_attn_backward(q, kv, attn_sink, topk_idxs, scale, o, do):
         return dq, dkv.to(kv.dtype), dsink.to(attn_sink.dtype)
     with torch.cuda.device(q.device):
         st = torch.cuda.current_stream(q.device)
+        lse_c = None if lse is None else lse.float().contiguous()
         _lib.check(_lib.lib().sa_bwd(
             q_c.data_ptr(), kv_c.data_ptr(), attn_sink.contiguous().data_ptr(),
-            topk_idxs.data_ptr(), o_c.data_ptr(), do_c.data_ptr(), dq.data_ptr(),
+            topk_idxs.data_ptr(), o_c.data_ptr(), do_c.data_ptr(),
+            None if lse_c is None else lse_c.data_ptr(), dq.data_ptr(),
             dkv.data_ptr(), dsink.data_ptr(), b, m, h, d, kv.shape[1], topk_idxs.shape[-1],
             _lib.i64_array(q_c.stride()), _lib.i64_array(kv_c.stride()),
             _lib.i64_array(topk_idxs.stride()), _lib.i64_array(o_c.stride()),
@@ -218,6 +254,35 @@ torch.library.register_autograd("sparse_attn_b200::fwd", _fwd_backward,
                                 setup_context=_setup_context)
 
 
+@torch.library.custom_op("sparse_attn_b200::fwd_train", mutates_args=())
+def _fwd_train(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor,
+               topk_idxs: torch.Tensor, scale: float) -> tuple[torch.Tensor, torch.Tensor]:
+    return _forward_train(q, kv, attn_sink, topk_idxs, scale)
+
+
+@_fwd_train.register_fake
+def _(q, kv, attn_sink, topk_idxs, scale):
+    assert q.dim() == 4
+    return q.new_empty(q.shape), q.new_empty(q.shape[:3], dtype=torch.float32)
+
+
+def _setup_context_train(ctx, inputs, output):
+    q, kv, attn_sink, topk_idxs, scale = inputs
+    o, lse = output
+    ctx.save_for_backward(q, kv, attn_sink, topk_idxs, o, lse)
+    ctx.scale = scale
+
+
+def _fwd_train_backward(ctx, grad_o, grad_lse):
+    q, kv, attn_sink, topk_idxs, o, lse = ctx.saved_tensors
+    dq, dkv, dsink = sparse_attn_backward(q, kv, attn_sink, topk_idxs, ctx.scale, o, grad_o, lse)
+    return dq, dkv, dsink, None, None
+
+
+torch.library.register_autograd("sparse_attn_b200::fwd_train", _fwd_train_backward,
+                                setup_context=_setup_context_train)
+
+
 def sparse_attn(q, kv, attn_sink, topk_idxs, scale):
     """Top-k sparse attention with attention sink (track-01 signature).
 
@@ -236,5 +301,6 @@ def sparse_attn(q, kv, attn_sink, topk_idxs, scale):
     """
     if torch.is_grad_enabled() and (q.requires_grad or kv.requires_grad or
                                     attn_sink.requires_grad):
-        return torch.ops.sparse_attn_b200.fwd(q, kv, attn_sink, topk_idxs, float(scale))
+        # the training forward keeps the log-sum-exp for a one-pass backward
+        return torch.ops.sparse_attn_b200.fwd_train(q, kv, attn_sink, topk_idxs, float(scale))[0]
     return _forward(q, kv, attn_sink, topk_idxs, float(scale))

@@ -107,7 +107,7 @@ def test_backward_entry_validates_before_any_gpu_work():
     st = _i64(8192, 8192, 512, 1)
 
     def bwd(dq=16, dkv=16, b=1, h=16, dkv_strides=(2048, 512, 1)):
-        return L.sa_bwd(16, 16, 16, 16, 16, 16, dq, dkv, 16, b, 1, h, 512, 4, 4, st,
+        return L.sa_bwd(16, 16, 16, 16, 16, 16, None, dq, dkv, 16, b, 1, h, 512, 4, 4, st,
                         _i64(2048, 512, 1), _i64(4, 4, 1), st, _i64(*dkv_strides), 1.0, None)
     assert bwd(b=0) == _lib.SA_OK
     assert bwd(h=4) == _lib.SA_ERR_UNSUPPORTED
