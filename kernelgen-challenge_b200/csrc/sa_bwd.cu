@@ -13,8 +13,9 @@
 //   dsink  = -p_sink * D                     (summed over rows)
 //
 // One CTA (8 warps, two per SM sub-partition) per query row.  Its units of 64
-// gathered rows (the forward's 128-byte-swizzled slab layout) stream through a
-// 2-deep cp.async ring twice:
+// gathered rows, up to the last unit holding a valid slot (the forward's
+// 128-byte-swizzled slab layout), stream through a 2-deep cp.async ring twice
+// (once when the training forward supplied the log-sum-exp):
 //   pass A  S = Q.K^T (warp w: keys 8w..8w+7), online max / sum per head: the
 //           row's log-sum-exp including the sink
 //   pass B  S and dP = dO.V^T again (warp w: keys 8w..8w+7), P and
@@ -82,8 +83,26 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
   const int g8 = lane >> 2, q4 = lane & 3;
   const int64_t row = blockIdx.x;
   const int64_t tb = row / p.m, tm = row - tb * p.m;
-  const int64_t U = (p.topk + UK - 1) / UK;
   const int32_t* irow = p.idx + tb * p.i_sb + tm * p.i_sm;
+  // Units up to the row's last valid slot: trailing masked slots (causal
+  // prefill pads each row with -1) are neither gathered nor multiplied.  One
+  // CTA per row, so the GPU's own block scheduling balances short rows.
+  __shared__ int64_t units_s;
+  if (warp == 0) {
+    int64_t last = -1;
+    for (int64_t base = ((p.topk - 1) / 32) * 32; base >= 0; base -= 32) {
+      const int64_t k = base + lane;
+      const int32_t id = k < p.topk ? __ldg(irow + k * p.i_sk) : -1;
+      const uint32_t v = __ballot_sync(0xffffffffu, id >= 0 && (int64_t)id < p.kv_len);
+      if (v != 0u) {
+        last = base + 31 - __clz(v);
+        break;
+      }
+    }
+    if (lane == 0) units_s = (last + UK) / UK;  // ceil((last + 1) / UK)
+  }
+  __syncthreads();
+  const int64_t U = units_s;
   const __nv_bfloat16* kvb = p.kv + tb * p.kv_sb;
   const uint32_t qbase = smem_u32(S.q), dobase = smem_u32(S.dout);
   const uint32_t pbase = smem_u32(S.p), dsbase = smem_u32(S.ds);
