@@ -109,6 +109,27 @@ int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx,
            const int64_t kv_strides[3], const int64_t idx_strides[3], const int64_t o_strides[4],
            const int64_t dkv_strides[3], float scale, void* stream);
 
+/* Top-k index producer (lightning indexer): the step that feeds topk_idxs.
+ * The reference takes topk_idxs as an input and has none (track-01/
+ * requirements.md:1-5); this follows the published DeepSeek-V3.2 indexer:
+ *   score[b,t,s] = sum_j weights[b,t,j] * ReLU(q_idx[b,t,j,:] . k_idx[b,s,:])
+ * over keys s < lengths[b,t] (a causal or cache limit), fp32 accumulation of
+ * bf16 products.  topk_idxs[b,t,:] (int32, contiguous rows) receives the topk
+ * keys of largest score in ascending index order, ties at the threshold to
+ * the lower index, then -1 where fewer keys are valid: the layout sa_fwd
+ * takes.  q_idx [b, m, 64, 128] bf16, k_idx [b, kv_len, 128] bf16, weights
+ * [b, m, 64] fp32, lengths [b, m] int32; element strides, last dims
+ * contiguous, q / k rows 16-byte aligned.  The workspace holds the fp32 scores
+ * (sa_indexer_workspace_bytes); after the call it contains them, row b*m + t. */
+size_t sa_indexer_workspace_bytes(int64_t b, int64_t m, int64_t kv_len);
+int sa_indexer_topk(const void* q_idx, const void* k_idx, const float* weights,
+                    const int32_t* lengths, int32_t* topk_idxs, int64_t b, int64_t m,
+                    int64_t n_heads, int64_t head_dim, int64_t kv_len, int64_t topk,
+                    const int64_t q_strides[4], const int64_t k_strides[3],
+                    const int64_t w_strides[3], const int64_t len_strides[2],
+                    const int64_t out_strides[3], void* workspace, size_t workspace_bytes,
+                    void* stream);
+
 /* Quantises a bf16 cache [b, kv_len, 512] to the layout sa_fwd_fp8 reads.  Per
  * row: amax = max |x|, kv8 = e4m3_rn_satfinite(x * (448 / amax)),
  * kv_scale = amax / 448; an all-zero row gives zeros and scale 0.  Strides are

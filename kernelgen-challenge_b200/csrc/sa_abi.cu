@@ -38,6 +38,12 @@ struct QuantParams {
   int64_t kv_sb, kv_sn, o_sb, o_sn, s_sb, s_sn;
 };
 cudaError_t launch_quantize_fp8(const QuantParams& qp, int sms, cudaStream_t st);
+cudaError_t launch_indexer(const __nv_bfloat16* q, const __nv_bfloat16* k, const float* w,
+                           const int32_t* len, int32_t* out, float* score, int64_t b, int64_t m,
+                           int64_t kv_len, int64_t topk, const int64_t q_strides[4],
+                           const int64_t k_strides[3], const int64_t w_strides[3],
+                           const int64_t len_strides[2], const int64_t out_strides[3],
+                           cudaStream_t st);
 cudaError_t launch_bwd(const Params& f, const __nv_bfloat16* dout, __nv_bfloat16* dq, float* dkv,
                        float* dsink, int64_t dkv_sb, int64_t dkv_sn, float scale,
                        cudaStream_t st);
@@ -399,6 +405,51 @@ int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx,
   e = sa::launch_bwd(p, static_cast<const __nv_bfloat16*>(dout), static_cast<__nv_bfloat16*>(dq),
                      dkv, dsink, dkv_strides[0], dkv_strides[1], scale,
                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail_cuda(e);
+  return SA_OK;
+}
+
+size_t sa_indexer_workspace_bytes(int64_t b, int64_t m, int64_t kv_len) {
+  if (b < 0 || m < 0 || kv_len < 0) return 0;
+  return (size_t)(b * m) * (size_t)kv_len * sizeof(float);
+}
+
+int sa_indexer_topk(const void* q_idx, const void* k_idx, const float* weights,
+                    const int32_t* lengths, int32_t* topk_idxs, int64_t b, int64_t m,
+                    int64_t n_heads, int64_t head_dim, int64_t kv_len, int64_t topk,
+                    const int64_t q_strides[4], const int64_t k_strides[3],
+                    const int64_t w_strides[3], const int64_t len_strides[2],
+                    const int64_t out_strides[3], void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  t_last_cuda_error = 0;
+  if (b < 0 || m < 0 || kv_len < 0 || topk < 0) return SA_ERR_INVALID_ARG;
+  if (n_heads != 64 || head_dim != 128) return SA_ERR_UNSUPPORTED;
+  if (b == 0 || m == 0 || topk == 0) return SA_OK;
+  if (!q_idx || !weights || !lengths || !topk_idxs || !q_strides || !k_strides || !w_strides ||
+      !len_strides || !out_strides || (kv_len > 0 && !k_idx))
+    return SA_ERR_INVALID_ARG;
+  if (q_strides[3] != 1 || k_strides[2] != 1 || w_strides[2] != 1 || out_strides[2] != 1)
+    return SA_ERR_INVALID_ARG;
+  if (!aligned16(q_idx) || (kv_len > 0 && !aligned16(k_idx))) return SA_ERR_INVALID_ARG;
+  for (int i = 0; i < 3; ++i)
+    if ((q_strides[i] % 8) != 0) return SA_ERR_INVALID_ARG;
+  for (int i = 0; i < 2; ++i)
+    if ((k_strides[i] % 8) != 0) return SA_ERR_INVALID_ARG;
+  if (kv_len > INT32_MAX || b * m > INT32_MAX) return SA_ERR_INVALID_ARG;
+  const size_t need = sa_indexer_workspace_bytes(b, m, kv_len);
+  if (workspace_bytes < need || (need > 0 && workspace == nullptr)) return SA_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 3u) != 0) return SA_ERR_INVALID_ARG;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e);
+  const DeviceInfo* di = device_info(dev);
+  if (di == nullptr) return SA_ERR_UNSUPPORTED;
+  if (di->err != cudaSuccess) return fail_cuda(di->err);
+  if (di->major != 10) return SA_ERR_UNSUPPORTED;
+  e = sa::launch_indexer(static_cast<const __nv_bfloat16*>(q_idx),
+                         static_cast<const __nv_bfloat16*>(k_idx), weights, lengths, topk_idxs,
+                         static_cast<float*>(workspace), b, m, kv_len, topk, q_strides, k_strides,
+                         w_strides, len_strides, out_strides, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail_cuda(e);
   return SA_OK;
 }

@@ -50,6 +50,9 @@ SIGNATURES = {
     "sa_bwd": (ctypes.c_int, [_P] * 10 + [_I64] * 6 + [_I64P] * 5 + [ctypes.c_float, _P]),
     "sa_fwd_train": (ctypes.c_int, [_P] * 6 + [_I64] * 6 + [_I64P] * 4
                      + [ctypes.c_float, _P, ctypes.c_size_t, _P]),
+    "sa_indexer_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64]),
+    "sa_indexer_topk": (ctypes.c_int, [_P] * 5 + [_I64] * 6 + [_I64P] * 5
+                        + [_P, ctypes.c_size_t, _P]),
     # include/hc_sinkhorn.h
     "hcs_split_sinkhorn": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _I64, _I64, ctypes.c_int,
                                           ctypes.c_int, ctypes.c_float, _P]),

@@ -108,3 +108,14 @@ def test_fp8_quantiser_statement():
     assert bool((err <= amax * 2.0 ** -4 + 1e-30).all())
     assert float(kv8[0].float().abs().max()) == 448.0
     assert float(sc[1, 7]) == 0.0 and bool((kv8[1, 7].float() == 0).all())
+
+
+def test_indexer_selection_statement():
+    """select_topk: largest scores, ties to the lower index, ascending order,
+    -1 padding (CPU)."""
+    from oracle.indexer_oracle import select_topk
+    sc = torch.tensor([[[0.5, 2.0, 2.0, -1.0, 3.0, 2.0]]])
+    ln = torch.tensor([[6]], dtype=torch.int32)
+    assert select_topk(sc, ln, 3).tolist() == [[[1, 2, 4]]]
+    assert select_topk(sc, ln, 8).tolist() == [[[0, 1, 2, 3, 4, 5, -1, -1]]]
+    assert select_topk(sc, torch.tensor([[2]], dtype=torch.int32), 3).tolist() == [[[0, 1, -1]]]
