@@ -59,9 +59,10 @@ def parse():
     ap.add_argument("--kv", choices=["bf16", "fp8"], default="bf16",
                     help="KV cache format: bf16 (the reference's) or e4m3 + fp32 per-token "
                          "scale (sparse_attn_fp8)")
-    ap.add_argument("--op", choices=["sparse_attn", "sparse_attn_bwd", "hc_sinkhorn"],
+    ap.add_argument("--op", choices=["sparse_attn", "sparse_attn_bwd", "hc_sinkhorn", "indexer"],
                     default="sparse_attn",
-                    help="sparse_attn_bwd: the backward pass on --config (default causal); "
+                    help="sparse_attn_bwd: the backward pass on --config; indexer: the top-k "
+                         "index producer on --config's b, m, kv_len, topk; "
                          "hc_sinkhorn: the track-02 op on its 1k-1-64 prefill shape")
     ap.add_argument("--graph", action="store_true",
                     help="capture one op call in a CUDA graph and time its replays")
@@ -518,8 +519,64 @@ def run_backward(args):
         "gathered_kv_gbs": valid * D * 2 / (ms / 1e3) / 1e9}), flush=True)
 
 
+def run_indexer(args):
+    """The top-k index producer on --config's (b, m, kv_len, topk): 64 index
+    heads x 128 dims, bf16, all keys valid; query-tokens/s, L2 flushed before
+    every step.  The CPU leg times the torch oracle on 4 rows."""
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        from oracle.indexer_oracle import indexer_topk_oracle
+        torch.set_num_threads(os.cpu_count() or 1)
+        g = torch.Generator().manual_seed(0)
+        rows = 4
+        q = torch.randn(1, rows, 64, 128, generator=g).to(torch.bfloat16)
+        k = torch.randn(1, cfg.kv_len, 128, generator=g).to(torch.bfloat16)
+        w = torch.rand(1, rows, 64, generator=g)
+        ln = torch.full((1, rows), cfg.kv_len, dtype=torch.int32)
+        t0 = time.perf_counter()
+        for _ in range(max(1, args.steps)):
+            indexer_topk_oracle(q, k, w, ln, cfg.topk)
+        el = time.perf_counter() - t0
+        print(json.dumps({"metric": "indexer query-tokens/s", "impl": "reference",
+                          "value": rows * max(1, args.steps) / el, "unit": "query-tokens/s",
+                          "config": {"workload": cfg.name, "sample_rows": rows}}), flush=True)
+        return
+    import sparse_attn
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(cfg.b, cfg.m, 64, 128, generator=g, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(cfg.b, cfg.kv_len, 128, generator=g, device=dev, dtype=torch.bfloat16)
+    w = torch.rand(cfg.b, cfg.m, 64, generator=g, device=dev)
+    ln = torch.full((cfg.b, cfg.m), cfg.kv_len, dtype=torch.int32, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        sparse_attn.indexer_topk(q, k, w, ln, cfg.topk)
+    K = args.steps
+    st = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    en = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    torch.cuda.synchronize()
+    for i in range(K):
+        flush.zero_()
+        st[i].record(stream)
+        sparse_attn.indexer_topk(q, k, w, ln, cfg.topk)
+        en[i].record(stream)
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(e) for a, e in zip(st, en)) / K
+    rows = cfg.b * cfg.m
+    flops = 2.0 * rows * cfg.kv_len * 64 * 128
+    print(json.dumps({
+        "metric": "indexer query-tokens/s", "value": rows / (ms / 1e3), "unit": "query-tokens/s",
+        "n_gpus": 1, "steps": K, "ms_per_step": ms, "higher_is_better": True, "dtype": "bf16",
+        "config": {"workload": cfg.name, "b": cfg.b, "m": cfg.m, "kv_len": cfg.kv_len,
+                   "topk": cfg.topk, "index_heads": 64, "index_dim": 128},
+        "score_tflops": flops / (ms / 1e3) / 1e12}), flush=True)
+
+
 def main():
     args = parse()
+    if args.op == "indexer":
+        return run_indexer(args)
     if args.op == "hc_sinkhorn":
         return run_hc_sinkhorn(args)
     if args.op == "sparse_attn_bwd":
