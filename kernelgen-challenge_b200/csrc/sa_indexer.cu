@@ -19,10 +19,11 @@
 // sum over its 16 heads reduce the fragments to per-key partial scores.  The
 // four warps' partials are added in shared memory and the 64 scores are
 // written to a fp32 [b*m, kv_len] buffer.
-// Kernel 2, sa_indexer_topk_kernel: one CTA per query row, radix select of
-// the topk-th largest score over order-preserving uint32 keys (four 8-bit
-// histogram rounds in shared memory), then a compaction pass that writes the
-// selected indices in ascending order.
+// Kernel 2, sa_indexer_topk_kernel: one CTA per query row, its scores staged
+// in shared memory (rows up to 48 Ki keys), radix select of the topk-th
+// largest score over order-preserving uint32 keys (four 8-bit histogram
+// rounds), then a compaction pass that writes the selected indices in
+// ascending order.
 #include "sa_common.cuh"
 
 namespace sa {
@@ -204,7 +205,13 @@ __device__ __forceinline__ int block_excl_scan(int v, int* warp_sums, int& total
   return before;
 }
 
+// Rows of up to kSmemKeys scores are staged in shared memory once; the four
+// histogram rounds and the compaction then read them there (longer rows read
+// the fp32 score buffer, L2-resident, every time).
+constexpr int kSmemKeys = 49152;  // 192 KiB
+
 __global__ void __launch_bounds__(NT2) sa_indexer_topk_kernel(const IdxParams P) {
+  extern __shared__ float staged[];
   __shared__ int hist[256];
   __shared__ int warp_sums[32];
   __shared__ uint32_t sel_digit;
@@ -215,6 +222,11 @@ __global__ void __launch_bounds__(NT2) sa_indexer_topk_kernel(const IdxParams P)
   int64_t L = __ldg(P.len + tb * P.l_sb + tm * P.l_sm);
   L = L < 0 ? 0 : (L > P.kv_len ? P.kv_len : L);
   const float* srow = P.score + row * P.kv_len;
+  if (P.kv_len <= kSmemKeys) {
+    for (int64_t s = tid; s < L; s += NT2) staged[s] = srow[s];
+    __syncthreads();
+    srow = staged;
+  }
   int32_t* orow = P.out + tb * P.o_sb + tm * P.o_sm;
   const int64_t K = P.topk;
   const int64_t seg = (L + NT2 - 1) / NT2;
@@ -323,8 +335,11 @@ cudaError_t launch_indexer(const __nv_bfloat16* q, const __nv_bfloat16* k, const
   static PerDeviceOnce attr_once;
   const size_t smem = sizeof(ScoreSmem) + 128;
   cudaError_t e = once_per_device(attr_once, [&] {
-    return cudaFuncSetAttribute(sa_indexer_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)smem);
+    cudaError_t e1 = cudaFuncSetAttribute(sa_indexer_score_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e1 != cudaSuccess) return e1;
+    return cudaFuncSetAttribute(sa_indexer_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)(kSmemKeys * sizeof(float)));
   });
   if (e != cudaSuccess) return e;
   const int64_t rows = P.b * P.m;
@@ -335,7 +350,8 @@ cudaError_t launch_indexer(const __nv_bfloat16* q, const __nv_bfloat16* k, const
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  sa_indexer_topk_kernel<<<static_cast<unsigned>(rows), NT2, 0, st>>>(P);
+  const size_t staged = kv_len <= kSmemKeys ? (size_t)kv_len * sizeof(float) : 0;
+  sa_indexer_topk_kernel<<<static_cast<unsigned>(rows), NT2, staged, st>>>(P);
   return cudaGetLastError();
 }
 
