@@ -43,7 +43,7 @@ extern "C" {
 #define SA_ERR_INVALID_ARG (-1) /* null pointer, bad shape/stride/alignment */
 #define SA_ERR_WORKSPACE (-2)   /* workspace missing or too small          */
 #define SA_ERR_CUDA (-3)        /* CUDA runtime error (see last_cuda_error) */
-#define SA_ERR_UNSUPPORTED (-4) /* h != 16, d != 512, or no sm_100 device   */
+#define SA_ERR_UNSUPPORTED (-4) /* h % 16 != 0, d != 512, or no sm_100 device */
 
 /* Kernel variants for sa_fwd_ex (SA_VARIANT_AUTO picks the fastest, WS). */
 #define SA_VARIANT_AUTO 0
@@ -83,7 +83,7 @@ int sa_fwd_fp8(const void* q, const void* kv8, const float* kv_scale, const floa
                void* workspace, size_t workspace_bytes, void* stream, int grid_ctas);
 
 /* Training forward: sa_fwd (warp-specialized kernel) that also writes
- * lse[b*m][16] (fp32): log2 of each row's full softmax denominator, the sink
+ * lse[b*m][h] (fp32): log2 of each row's full softmax denominator, the sink
  * included, in the log2 domain of the scores (weight of slot t =
  * 2^(s_t * scale * log2(e) - lse)).  sa_bwd then needs one pass instead of
  * two.  No counterpart in the reference, which has no backward. */
@@ -96,8 +96,8 @@ int sa_fwd_train(const void* q, const void* kv, const float* sink, const int32_t
 /* Backward pass: gradients of sa_fwd.  Given q, kv, sink, idx, the forward's
  * output o, its lse from sa_fwd_train (or NULL: recomputed by a first pass)
  * and the upstream gradient dout (laid out like o: o_strides), writes
- * dq (bf16, contiguous [b, m, 16, 512]) and ADDS into dkv (fp32 [b, kv_len, 512],
- * element strides dkv_strides, 8-byte aligned) and dsink (fp32 [16]); zero
+ * dq (bf16, contiguous [b, m, h, 512]) and ADDS into dkv (fp32 [b, kv_len, 512],
+ * element strides dkv_strides, 8-byte aligned) and dsink (fp32 [h]); zero
  * those two first for a plain gradient.  Masked slots (-1 or out of range)
  * contribute nothing; duplicated indices add.  The math is the gradient of
  * the reference forward (track-01/reference/reference.py:24-40), which has no
@@ -182,10 +182,15 @@ size_t sa_workspace_bytes(int64_t b, int64_t m, int64_t topk, int device);
  *   sink  [h]            fp32, contiguous
  *   idx   [b, m, topk]   int32, strides idx_strides (any, elements)
  *   o     [b, m, h, d]   bf16, strides o_strides,            o_strides[3] == 1
- *   h == 16, d == 512; every row start 16-byte aligned (row strides multiples
- *   of 8 elements, base pointers 16-byte aligned).
+ *   h a multiple of 16, d == 512; every row start 16-byte aligned (row
+ *   strides multiples of 8 elements, base pointers 16-byte aligned).  The
+ *   kernels run 16 heads; h = 16k runs as k groups of 16 heads, one after the
+ *   other on `stream`, each gathering the rows again (the reference pads its
+ *   head tile to max(16, next_pow2(h)), submission.py:1004; pad h up to a
+ *   multiple of 16 with zero heads).
  *   workspace: device memory of at least sa_workspace_bytes(b, m, topk, dev)
- *   bytes, 256-byte aligned, contents arbitrary (not preserved).
+ *   bytes, 256-byte aligned, zero-filled before its first use (see
+ *   sa_workspace_bytes); every call leaves it zero-filled.
  */
 int sa_fwd(const void* q, const void* kv, const float* sink, const int32_t* idx, void* o,
            int64_t b, int64_t m, int64_t h, int64_t d, int64_t kv_len, int64_t topk,

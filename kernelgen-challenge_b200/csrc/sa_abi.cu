@@ -44,7 +44,8 @@ cudaError_t launch_indexer(const __nv_bfloat16* q, const __nv_bfloat16* k, const
                            const int64_t k_strides[3], const int64_t w_strides[3],
                            const int64_t len_strides[2], const int64_t out_strides[3],
                            cudaStream_t st);
-cudaError_t launch_bwd(const Params& f, const __nv_bfloat16* dout, __nv_bfloat16* dq, float* dkv,
+cudaError_t launch_bwd(const Params& f, const __nv_bfloat16* dout, __nv_bfloat16* dq,
+                       int64_t dq_rs, float* dkv,
                        float* dsink, int64_t dkv_sb, int64_t dkv_sn, float scale,
                        cudaStream_t st);
 }  // namespace sa
@@ -163,13 +164,14 @@ size_t sa_workspace_bytes(int64_t b, int64_t m, int64_t topk, int device) {
   return sa::workspace_bytes_for_grid(static_cast<int>(grid));
 }
 
-// sa_fwd_ex and sa_fwd_train; lse (nullable) is the training output.
-static int fwd_impl(const void* q, const void* kv, const float* sink, const int32_t* idx, void* o,
+// One group of 16 heads of sa_fwd_ex / sa_fwd_train; lse (nullable) is the
+// training output, lse_rs floats between its rows.
+static int fwd_group(const void* q, const void* kv, const float* sink, const int32_t* idx, void* o,
                     int64_t b, int64_t m, int64_t h, int64_t d, int64_t kv_len, int64_t topk,
                     const int64_t q_strides[4], const int64_t kv_strides[3],
                     const int64_t idx_strides[3], const int64_t o_strides[4], float scale,
                     void* workspace, size_t workspace_bytes, void* stream, int variant,
-                    int grid_ctas, float* lse) {
+                    int grid_ctas, float* lse, int64_t lse_rs) {
   t_last_cuda_error = 0;
   if (b < 0 || m < 0 || kv_len < 0 || topk < 0) return SA_ERR_INVALID_ARG;
   if (h != sa::kHeads || d != sa::kDim) return SA_ERR_UNSUPPORTED;
@@ -242,6 +244,7 @@ static int fwd_impl(const void* q, const void* kv, const float* sink, const int3
     if ((reinterpret_cast<uintptr_t>(lse) & 3u) != 0) return SA_ERR_INVALID_ARG;
   }
   p.lse = lse;
+  p.lse_rs = lse_rs;
   p.upt = ceil_div(topk > 0 ? topk : 1, unit_keys);  // topk == 0: one all-masked unit
   p.units = b * m * p.upt;
 
@@ -271,7 +274,7 @@ static int fwd_impl(const void* q, const void* kv, const float* sink, const int3
   return SA_OK;
 }
 
-int sa_fwd_fp8(const void* q, const void* kv8, const float* kv_scale, const float* sink,
+static int fp8_group(const void* q, const void* kv8, const float* kv_scale, const float* sink,
                const int32_t* idx, void* o, int64_t b, int64_t m, int64_t h, int64_t d,
                int64_t kv_len, int64_t topk, const int64_t q_strides[4],
                const int64_t kv_strides[3], const int64_t kv_scale_strides[2],
@@ -349,12 +352,13 @@ int sa_fwd_fp8(const void* q, const void* kv8, const float* kv_scale, const floa
   return SA_OK;
 }
 
-int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx, const void* o,
-           const void* dout, const float* lse, void* dq, float* dkv, float* dsink, int64_t b,
-           int64_t m, int64_t h,
-           int64_t d, int64_t kv_len, int64_t topk, const int64_t q_strides[4],
-           const int64_t kv_strides[3], const int64_t idx_strides[3], const int64_t o_strides[4],
-           const int64_t dkv_strides[3], float scale, void* stream) {
+static int bwd_group(const void* q, const void* kv, const float* sink, const int32_t* idx,
+                     const void* o, const void* dout, const float* lse, int64_t h_total, void* dq,
+                     float* dkv, float* dsink, int64_t b, int64_t m, int64_t h, int64_t d,
+                     int64_t kv_len, int64_t topk, const int64_t q_strides[4],
+                     const int64_t kv_strides[3], const int64_t idx_strides[3],
+                     const int64_t o_strides[4], const int64_t dkv_strides[3], float scale,
+                     void* stream) {
   t_last_cuda_error = 0;
   if (b < 0 || m < 0 || kv_len < 0 || topk < 0) return SA_ERR_INVALID_ARG;
   if (h != sa::kHeads || d != sa::kDim) return SA_ERR_UNSUPPORTED;
@@ -401,11 +405,90 @@ int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx,
   p.o_sm = o_strides[1];
   p.o_sh = o_strides[2];
   p.scale_log2 = scale * sa::kLog2e;
-  p.lse = const_cast<float*>(lse);  // read only
+  p.lse = const_cast<float*>(lse);  // read only; rows of the caller's h_total heads
+  p.lse_rs = h_total;
   e = sa::launch_bwd(p, static_cast<const __nv_bfloat16*>(dout), static_cast<__nv_bfloat16*>(dq),
-                     dkv, dsink, dkv_strides[0], dkv_strides[1], scale,
+                     h_total * sa::kDim, dkv, dsink, dkv_strides[0], dkv_strides[1], scale,
                      static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail_cuda(e);
+  return SA_OK;
+}
+
+// Head counts above the kernels' 16: the heads run as consecutive groups of
+// 16 on the same stream (heads are independent; each group gathers the rows
+// again).  The reference takes any h by padding its head tile to
+// max(16, next_pow2(h)) (track-01/submission.py:1004); here h must be a
+// multiple of 16, and callers pad smaller remainders with zero heads.
+static int64_t head_groups(int64_t h) {
+  return (h > sa::kHeads && h % sa::kHeads == 0) ? h / sa::kHeads : 1;
+}
+static const __nv_bfloat16* head_group_ptr(const void* base, int64_t g, int64_t sh) {
+  return static_cast<const __nv_bfloat16*>(base) + g * sa::kHeads * sh;
+}
+
+static int fwd_impl(const void* q, const void* kv, const float* sink, const int32_t* idx, void* o,
+                    int64_t b, int64_t m, int64_t h, int64_t d, int64_t kv_len, int64_t topk,
+                    const int64_t q_strides[4], const int64_t kv_strides[3],
+                    const int64_t idx_strides[3], const int64_t o_strides[4], float scale,
+                    void* workspace, size_t workspace_bytes, void* stream, int variant,
+                    int grid_ctas, float* lse) {
+  const int64_t groups = head_groups(h);
+  if (groups == 1 || !q || !o || !sink || !q_strides || !o_strides)
+    return fwd_group(q, kv, sink, idx, o, b, m, h, d, kv_len, topk, q_strides, kv_strides,
+                     idx_strides, o_strides, scale, workspace, workspace_bytes, stream, variant,
+                     grid_ctas, lse, h);
+  for (int64_t g = 0; g < groups; ++g) {
+    const int rc = fwd_group(
+        head_group_ptr(q, g, q_strides[2]), kv, sink + g * sa::kHeads, idx,
+        const_cast<__nv_bfloat16*>(head_group_ptr(o, g, o_strides[2])), b, m, sa::kHeads, d,
+        kv_len, topk, q_strides, kv_strides, idx_strides, o_strides, scale, workspace,
+        workspace_bytes, stream, variant, grid_ctas, lse ? lse + g * sa::kHeads : nullptr, h);
+    if (rc != SA_OK) return rc;
+  }
+  return SA_OK;
+}
+
+int sa_fwd_fp8(const void* q, const void* kv8, const float* kv_scale, const float* sink,
+               const int32_t* idx, void* o, int64_t b, int64_t m, int64_t h, int64_t d,
+               int64_t kv_len, int64_t topk, const int64_t q_strides[4],
+               const int64_t kv_strides[3], const int64_t kv_scale_strides[2],
+               const int64_t idx_strides[3], const int64_t o_strides[4], float scale,
+               void* workspace, size_t workspace_bytes, void* stream, int grid_ctas) {
+  const int64_t groups = head_groups(h);
+  if (groups == 1 || !q || !o || !sink || !q_strides || !o_strides)
+    return fp8_group(q, kv8, kv_scale, sink, idx, o, b, m, h, d, kv_len, topk, q_strides,
+                     kv_strides, kv_scale_strides, idx_strides, o_strides, scale, workspace,
+                     workspace_bytes, stream, grid_ctas);
+  for (int64_t g = 0; g < groups; ++g) {
+    const int rc = fp8_group(
+        head_group_ptr(q, g, q_strides[2]), kv8, kv_scale, sink + g * sa::kHeads, idx,
+        const_cast<__nv_bfloat16*>(head_group_ptr(o, g, o_strides[2])), b, m, sa::kHeads, d,
+        kv_len, topk, q_strides, kv_strides, kv_scale_strides, idx_strides, o_strides, scale,
+        workspace, workspace_bytes, stream, grid_ctas);
+    if (rc != SA_OK) return rc;
+  }
+  return SA_OK;
+}
+
+int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx, const void* o,
+           const void* dout, const float* lse, void* dq, float* dkv, float* dsink, int64_t b,
+           int64_t m, int64_t h, int64_t d, int64_t kv_len, int64_t topk,
+           const int64_t q_strides[4], const int64_t kv_strides[3], const int64_t idx_strides[3],
+           const int64_t o_strides[4], const int64_t dkv_strides[3], float scale, void* stream) {
+  const int64_t groups = head_groups(h);
+  if (groups == 1 || !q || !o || !dout || !dq || !sink || !dsink || !q_strides || !o_strides)
+    return bwd_group(q, kv, sink, idx, o, dout, lse, h, dq, dkv, dsink, b, m, h, d, kv_len, topk,
+                     q_strides, kv_strides, idx_strides, o_strides, dkv_strides, scale, stream);
+  for (int64_t g = 0; g < groups; ++g) {
+    const int64_t k = g * sa::kHeads;
+    const int rc = bwd_group(
+        head_group_ptr(q, g, q_strides[2]), kv, sink + k, idx, head_group_ptr(o, g, o_strides[2]),
+        head_group_ptr(dout, g, o_strides[2]), lse ? lse + k : nullptr, h,
+        const_cast<__nv_bfloat16*>(head_group_ptr(dq, g, sa::kDim)), dkv, dsink + k, b, m,
+        sa::kHeads, d, kv_len, topk, q_strides, kv_strides, idx_strides, o_strides, dkv_strides,
+        scale, stream);
+    if (rc != SA_OK) return rc;
+  }
   return SA_OK;
 }
 

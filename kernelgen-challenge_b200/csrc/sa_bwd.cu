@@ -41,7 +41,8 @@ constexpr int P_BYTES = kHeads * UK * 2;    // 2 KiB: P or dS tile [head][key]
 struct BwdParams {
   Params f;                  // forward arguments (q, kv, sink, idx, o, shapes, strides)
   const __nv_bfloat16* dout; // dO, strides as o
-  __nv_bfloat16* dq;         // [b, m, 16, 512] contiguous
+  __nv_bfloat16* dq;         // rows of [16, 512], dq_rs elements apart
+  int64_t dq_rs;
   float* dkv;                // [b, kv_len, 512] fp32, row stride dkv_sn
   float* dsink;              // [16] fp32
   int64_t dkv_sb, dkv_sn;
@@ -183,7 +184,7 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
   const int64_t i0 = p.lse != nullptr ? U : 0;
   if (p.lse != nullptr && tid < kHeads) {
     const float sl2 = __ldg(p.sink + tid) * kLog2e;
-    const float L = p.lse[row * kHeads + tid];
+    const float L = p.lse[row * p.lse_rs + tid];
     S.M[tid] = L;
     S.invZ[tid] = 1.f;
     // dsink = -p_sink * D once the D of this row is in shared memory (below)
@@ -347,7 +348,7 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
   }
   cp_async_wait<0>();  // (no units: the Q / dO copies)
   // ---- dq of this row (the scale is already in dS)
-  __nv_bfloat16* dqr = bp.dq + row * (kHeads * kDim);
+  __nv_bfloat16* dqr = bp.dq + row * bp.dq_rs;
 #pragma unroll
   for (int nt = 0; nt < 8; ++nt) {
     const int d = 64 * warp + 8 * nt + 2 * q4;
@@ -358,8 +359,8 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
 
 }  // namespace bwd_path
 
-cudaError_t launch_bwd(const Params& f, const __nv_bfloat16* dout, __nv_bfloat16* dq, float* dkv,
-                       float* dsink, int64_t dkv_sb, int64_t dkv_sn, float scale,
+cudaError_t launch_bwd(const Params& f, const __nv_bfloat16* dout, __nv_bfloat16* dq,
+                       int64_t dq_rs, float* dkv, float* dsink, int64_t dkv_sb, int64_t dkv_sn, float scale,
                        cudaStream_t st) {
   using namespace bwd_path;
   static PerDeviceOnce attr_once;
@@ -368,7 +369,7 @@ cudaError_t launch_bwd(const Params& f, const __nv_bfloat16* dout, __nv_bfloat16
                                 (int)kSmemBytes);
   });
   if (e != cudaSuccess) return e;
-  BwdParams bp{f, dout, dq, dkv, dsink, dkv_sb, dkv_sn, scale};
+  BwdParams bp{f, dout, dq, dq_rs, dkv, dsink, dkv_sb, dkv_sn, scale};
   sa_bwd_kernel<<<static_cast<unsigned>(f.b * f.m), NT, kSmemBytes, st>>>(bp);
   return cudaGetLastError();
 }

@@ -65,6 +65,7 @@ struct Params {
   // softmax denominator, the sink included, in the log2 domain of the scores
   // (p_t = 2^(s_t * scale * log2(e) - lse)); the backward pass reads it.
   float* lse;
+  int64_t lse_rs;  // floats between lse rows (the caller's head count)
 };
 
 // log2 of the full denominator for a running max m and sum l (relative to m),
@@ -293,7 +294,7 @@ __device__ __forceinline__ void merge_split_row(const Params& p, int64_t f, int 
     M = Mb;
   }
   const float inv = 1.f / den;
-  if (p.lse != nullptr && d0 == 0) p.lse[t * kHeads + h] = M + log2f(den);
+  if (p.lse != nullptr && d0 == 0) p.lse[t * p.lse_rs + h] = M + log2f(den);
   const int64_t tb = t / p.m, tm = t - tb * p.m;
   uint4 w;
   w.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);

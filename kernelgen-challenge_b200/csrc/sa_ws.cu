@@ -404,8 +404,8 @@ __global__ void __launch_bounds__(NT, 1)
           const float f_lo = sink_factor(m_lo, l_lo, __ldg(p.sink + g8) * kLog2e);
           const float f_hi = sink_factor(m_hi, l_hi, __ldg(p.sink + g8 + 8) * kLog2e);
           if (kLse && c == 0 && q4 == 0) {
-            p.lse[t * kHeads + g8] = row_lse2(m_lo, l_lo, __ldg(p.sink + g8) * kLog2e);
-            p.lse[t * kHeads + g8 + 8] = row_lse2(m_hi, l_hi, __ldg(p.sink + g8 + 8) * kLog2e);
+            p.lse[t * p.lse_rs + g8] = row_lse2(m_lo, l_lo, __ldg(p.sink + g8) * kLog2e);
+            p.lse[t * p.lse_rs + g8 + 8] = row_lse2(m_hi, l_hi, __ldg(p.sink + g8 + 8) * kLog2e);
           }
           __nv_bfloat16* ob = p.o + tb * p.o_sb + tm * p.o_sm;
 #pragma unroll

@@ -14,7 +14,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from .op import _cached_workspace, _row_ok, workspace_bytes
+from .op import _cached_workspace, _pad_heads, _padded_heads, _row_ok, workspace_bytes
 
 __all__ = ["quantize_kv_fp8", "sparse_attn_fp8", "sparse_attn_fp8_out"]
 
@@ -66,15 +66,15 @@ def sparse_attn_fp8(q, kv8, kv_scale, attn_sink, topk_idxs, scale):
     """Top-k sparse attention with sink over an e4m3 cache.
 
     Args:
-        q:          [b, m, 16, 512] bf16
+        q:          [b, m, h, 512] bf16 (any h; padded to a multiple of 16)
         kv8:        [b, kv_len, 512] float8_e4m3fn (K and V shared)
         kv_scale:   [b, kv_len] fp32 (dequantised row = kv8 row * scale)
-        attn_sink:  [16] fp32
+        attn_sink:  [h] fp32
         topk_idxs:  [b, m, topk] int32; -1 (or any index outside [0, kv_len))
                     marks a masked slot
         scale:      float
     Returns:
-        o:          [b, m, 16, 512] bf16
+        o:          [b, m, h, 512] bf16
     """
     assert q.dim() == 4
     for name, t in (("q", q), ("kv8", kv8), ("kv_scale", kv_scale), ("attn_sink", attn_sink),
@@ -87,8 +87,13 @@ def sparse_attn_fp8(q, kv8, kv_scale, attn_sink, topk_idxs, scale):
                            "attn_sink fp32, topk_idxs int32")
     b, m, h, d = q.shape
     if kv8.dim() != 3 or kv8.shape[0] != b or kv8.shape[2] != d or \
-            tuple(kv_scale.shape) != (b, kv8.shape[1]) or tuple(topk_idxs.shape[:2]) != (b, m):
+            tuple(kv_scale.shape) != (b, kv8.shape[1]) or tuple(topk_idxs.shape[:2]) != (b, m) or \
+            tuple(attn_sink.shape) != (h,):
         raise RuntimeError("sparse_attn_fp8: inconsistent shapes")
+    hp = _padded_heads(h)
+    if hp != h:
+        qp, sp = _pad_heads(q, attn_sink, hp)
+        return sparse_attn_fp8(qp, kv8, kv_scale, sp, topk_idxs, scale)[:, :, :h].contiguous()
     q_c = q if _row_ok(q) else q.contiguous()
     kv_c = kv8 if (kv8.stride(-1) == 1 and kv8.data_ptr() % 16 == 0 and
                    all(s % 16 == 0 for s in kv8.stride()[:-1])) else kv8.contiguous()

@@ -6,7 +6,8 @@ shapes and return value:
     sparse_attn(q[b,m,h,512] bf16, kv[b,kv_len,512] bf16, attn_sink[h] fp32,
                 topk_idxs[b,m,topk] int32, scale: float) -> o[b,m,h,512] bf16
 
-with h <= 16 (the kernels run 16 heads; fewer are zero-padded).
+for any h: the kernels run heads in groups of 16, and a head count that is
+not a multiple of 16 is zero-padded up to one.
 
 Like the reference wrapper it asserts ``q.dim() == 4`` (submission.py:989),
 makes the inputs contiguous (:995-998) and allocates the output (:1000); the
@@ -123,19 +124,29 @@ def sparse_attn_out(o, q, kv, attn_sink, topk_idxs, scale, workspace=None, *,
 _KERNEL_HEADS = 16
 
 
+def _padded_heads(h: int) -> int:
+    """The head count the kernels run: h rounded up to a multiple of 16 (the
+    C library takes multiples of 16 as groups of 16; the reference pads its
+    head tile to max(16, next_pow2(h)) and masks, submission.py:1004).  Heads
+    are independent, so padded heads only cost their own work."""
+    return -(-h // _KERNEL_HEADS) * _KERNEL_HEADS
+
+
+def _pad_heads(q, attn_sink, hp):
+    h = q.shape[2]
+    qp = q.new_zeros(*q.shape[:2], hp, q.shape[3])
+    qp[:, :, :h] = q
+    sp = attn_sink.new_zeros(hp)
+    sp[:h] = attn_sink
+    return qp, sp
+
+
 def _forward(q, kv, attn_sink, topk_idxs, scale):
     _validate(q, kv, attn_sink, topk_idxs)
     h = q.shape[2]
-    if h < _KERNEL_HEADS:
-        # fewer heads: pad to the kernel's 16 (the reference pads to
-        # max(16, next_pow2(h)) and masks, submission.py:1004); heads are
-        # independent, so the padded heads only cost their own work
-        if h == 0:
-            return q.new_empty(q.shape)
-        qp = q.new_zeros(*q.shape[:2], _KERNEL_HEADS, q.shape[3])
-        qp[:, :, :h] = q
-        sp = attn_sink.new_zeros(_KERNEL_HEADS)
-        sp[:h] = attn_sink
+    hp = _padded_heads(h)
+    if h != hp:
+        qp, sp = _pad_heads(q, attn_sink, hp)
         return _forward(qp, kv, sp, topk_idxs, scale)[:, :, :h].contiguous()
     q_c = q if _row_ok(q) else q.contiguous()
     kv_c = kv if _row_ok(kv) else kv.contiguous()
@@ -168,11 +179,9 @@ def _forward_train(q, kv, attn_sink, topk_idxs, scale):
     backward pass."""
     _validate(q, kv, attn_sink, topk_idxs)
     h = q.shape[2]
-    if h < _KERNEL_HEADS:
-        qp = q.new_zeros(*q.shape[:2], _KERNEL_HEADS, q.shape[3])
-        qp[:, :, :h] = q
-        sp = attn_sink.new_zeros(_KERNEL_HEADS)
-        sp[:h] = attn_sink
+    hp = _padded_heads(h)
+    if h != hp:
+        qp, sp = _pad_heads(q, attn_sink, hp)
         o, lse = _forward_train(qp, kv, sp, topk_idxs, scale)
         return o[:, :, :h].contiguous(), lse[:, :, :h].contiguous()
     q_c = q if _row_ok(q) else q.contiguous()
@@ -206,8 +215,8 @@ def sparse_attn_backward(q, kv, attn_sink, topk_idxs, scale, o, do, lse=None):
     """
     _validate(q, kv, attn_sink, topk_idxs)
     h = q.shape[2]
-    if h < _KERNEL_HEADS:  # zero heads: zero gradients of their own, none into kv
-        pad = _KERNEL_HEADS - h
+    if h != _padded_heads(h):  # zero heads: zero gradients of their own, none into kv
+        pad = _padded_heads(h) - h
         zq = q.new_zeros(*q.shape[:2], pad, q.shape[3])
         lse_p = None if lse is None else torch.cat([lse, lse.new_zeros(*lse.shape[:2], pad)], 2)
         dq, dkv, dsink = sparse_attn_backward(
@@ -287,7 +296,7 @@ def sparse_attn(q, kv, attn_sink, topk_idxs, scale):
     """Top-k sparse attention with attention sink (track-01 signature).
 
     Args:
-        q:          [b, m, h, d]   bf16 (h <= 16, d = 512)
+        q:          [b, m, h, d]   bf16 (any h, d = 512)
         kv:         [b, kv_len, d] bf16 (K and V shared)
         attn_sink:  [h]            fp32
         topk_idxs:  [b, m, topk]   int32; -1 (or any index outside [0, kv_len))

@@ -59,6 +59,9 @@ def _call(**over):
 def test_validation_before_any_gpu_work():
     assert _call(b=-1) == _lib.SA_ERR_INVALID_ARG
     assert _call(h=8) == _lib.SA_ERR_UNSUPPORTED
+    assert _call(h=24) == _lib.SA_ERR_UNSUPPORTED  # more heads: multiples of 16 only
+    assert _call(h=32, b=0) == _lib.SA_OK
+    assert _call(h=32, q=8) == _lib.SA_ERR_INVALID_ARG  # each group is validated
     assert _call(d=256) == _lib.SA_ERR_UNSUPPORTED
     assert _call(b=0) == _lib.SA_OK           # empty problem: nothing to do
     assert _call(q=0) == _lib.SA_ERR_INVALID_ARG

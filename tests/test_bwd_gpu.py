@@ -11,6 +11,7 @@ import make_golden
 from helpers import load_golden
 from oracle.sparse_attn_oracle import sparse_attn_oracle_grads
 from sparse_attn import sparse_attn, sparse_attn_backward
+from sparse_attn.op import _forward_train
 from sparse_attn.workloads import make_inputs
 
 pytestmark = pytest.mark.gpu
@@ -59,6 +60,39 @@ def test_backward_causal_head():
 def test_backward_fewer_heads():
     q, kv, sink, idx, scale = make_inputs("plumbing", seed=6)
     _check(q[:, :, :5].contiguous(), kv, sink[:5].contiguous(), idx, scale, what="h=5")
+
+
+@pytest.mark.parametrize("h", [32, 40])
+def test_backward_more_heads(h):
+    """h > 16: the groups of 16 heads each add into dkv; dq and dsink per head
+    (h = 40 pads to 48)."""
+    g = torch.Generator().manual_seed(30 + h)
+    b, m, kv_len, topk = 2, 24, 500, 256
+    q = torch.randn(b, m, h, 512, generator=g).to(torch.bfloat16)
+    kv = torch.randn(b, kv_len, 512, generator=g).to(torch.bfloat16)
+    sink = torch.randn(h, generator=g)
+    idx = torch.randint(-1, kv_len, (b, m, topk), generator=g, dtype=torch.int32)
+    _check(q, kv, sink, idx, 512 ** -0.5, seed=h, what=f"h={h}")
+
+
+def test_training_forward_more_heads_lse():
+    """The training forward's lse [b, m, h] for h = 48 gives the one-pass
+    backward the same gradients as the two-pass one."""
+    g = torch.Generator().manual_seed(77)
+    b, m, h, kv_len, topk = 1, 64, 48, 800, 512
+    q = torch.randn(b, m, h, 512, generator=g).to(torch.bfloat16).cuda()
+    kv = torch.randn(b, kv_len, 512, generator=g).to(torch.bfloat16).cuda()
+    sink = torch.randn(h, generator=g).cuda()
+    idx = torch.randint(0, kv_len, (b, m, topk), generator=g, dtype=torch.int32).cuda()
+    do = torch.randn(b, m, h, 512, generator=g).to(torch.bfloat16).cuda()
+    scale = 512 ** -0.5
+    o, lse = _forward_train(q, kv, sink, idx, scale)
+    assert lse.shape == (b, m, h)
+    assert torch.equal(o, sparse_attn(q, kv, sink, idx, scale))
+    one = sparse_attn_backward(q, kv, sink, idx, scale, o, do, lse)
+    two = sparse_attn_backward(q, kv, sink, idx, scale, o, do)
+    for a, e, what in zip(one, two, ("dq", "dkv", "dsink")):
+        _close(a, e, f"one-pass vs two-pass {what}")
 
 
 def test_autograd_through_the_op():

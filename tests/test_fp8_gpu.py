@@ -108,6 +108,23 @@ def test_fp8_public_op_and_gpu_quantiser_agree_with_oracle():
                  what="fp8 vs bf16 cache")
 
 
+@pytest.mark.parametrize("h", [8, 32, 72])
+def test_fp8_head_counts(h):
+    """Other head counts: fewer pad to 16, more run as groups of 16."""
+    g = torch.Generator().manual_seed(h)
+    b, m, kv_len, topk = 2, 20, 600, 320
+    q = torch.randn(b, m, h, 512, generator=g).to(torch.bfloat16)
+    kv = torch.randn(b, kv_len, 512, generator=g).to(torch.bfloat16)
+    sink = torch.randn(h, generator=g)
+    idx = torch.randint(-1, kv_len, (b, m, topk), generator=g, dtype=torch.int32)
+    scale = 512 ** -0.5
+    kv8, ks = quantize_kv_fp8(kv.cuda())
+    o = sparse_attn_fp8(q.cuda(), kv8, ks, sink.cuda(), idx.cuda(), scale)
+    assert o.shape == q.shape
+    ref = sparse_attn_fp8_oracle(q, kv8.cpu(), ks.cpu(), sink, idx, scale)
+    assert_close(o, ref, what=f"fp8 h={h}")
+
+
 def test_fp8_scales_spanning_decades():
     """Token scales that grow along the key order exercise the running
     scale maximum (O rescaled whenever a unit brings a larger scale)."""

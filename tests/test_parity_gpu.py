@@ -180,6 +180,51 @@ def test_fewer_heads_padded(h):
     assert_close(o, sparse_attn_oracle(q, kv, sink, idx, scale), what=f"h={h}")
 
 
+def _many_heads_case(h, seed=21, b=2, m=40, kv_len=700, topk=300):
+    """Ragged rows (trailing -1 padding, interior -1, an all-masked row)."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(b, m, h, 512, generator=g).to(torch.bfloat16)
+    kv = torch.randn(b, kv_len, 512, generator=g).to(torch.bfloat16)
+    sink = torch.randn(h, generator=g)
+    idx = torch.randint(0, kv_len, (b, m, topk), generator=g, dtype=torch.int32)
+    length = torch.randint(0, topk + 1, (b, m, 1), generator=g)
+    idx = torch.where(torch.arange(topk)[None, None, :] < length, idx, torch.full_like(idx, -1))
+    idx[1, 3] = -1
+    return q, kv, sink, idx, 512 ** -0.5
+
+
+@pytest.mark.parametrize("h", [17, 32, 40, 64, 128])
+def test_more_heads_in_groups(h):
+    """h > 16 runs as groups of 16 heads (h not a multiple of 16 is padded),
+    through every kernel variant."""
+    q, kv, sink, idx, scale = _many_heads_case(h)
+    ref = sparse_attn_oracle(q, kv, sink, idx, scale)
+    o = sparse_attn(*_cuda(q, kv, sink, idx, scale))
+    assert o.shape == q.shape
+    assert_close(o, ref, what=f"h={h}")
+    if h % 16 == 0:
+        for variant in VARIANTS:
+            qc, kvc, sc, ic, _ = _cuda(q, kv, sink, idx, scale)
+            o = torch.empty_like(qc)
+            sparse_attn_out(o, qc, kvc, sc, ic, scale, variant=variant, grid=37)
+            assert_close(o, ref, what=f"h={h} variant {variant}")
+
+
+def test_more_heads_strided_q_and_o():
+    """Head groups step through q and o by their head stride: q a slice of a
+    wider buffer, o written into a strided view."""
+    h = 48
+    q, kv, sink, idx, scale = _many_heads_case(h, seed=5)
+    ref = sparse_attn_oracle(q, kv, sink, idx, scale)
+    qc, kvc, sc, ic, _ = _cuda(q, kv, sink, idx, scale)
+    wide = torch.zeros(q.shape[0], q.shape[1], h + 16, 512, dtype=q.dtype, device="cuda")
+    wide[:, :, 8:8 + h] = qc
+    ob = torch.zeros(q.shape[0], q.shape[1], h + 24, 512, dtype=q.dtype, device="cuda")
+    sparse_attn_out(ob[:, :, 16:16 + h], wide[:, :, 8:8 + h], kvc, sc, ic, scale)
+    assert_close(ob[:, :, 16:16 + h], ref, what="strided h=48")
+    assert not ob[:, :, :16].any() and not ob[:, :, 16 + h:].any()
+
+
 def _ragged_case(seed=11):
     """1200 rows (ragged schedule), rows padded with -1 to random lengths,
     interior -1 slots, and a few fully masked rows."""
