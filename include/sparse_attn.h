@@ -164,10 +164,12 @@ int sa_last_cuda_error(void);
  * count.  Replaces nothing in the reference: the reference kernel keeps all
  * state in registers (track-01/submission.py:1006-1021); the persistent
  * split kernels here spill per-CTA partial results for query rows that span
- * two CTAs.  The workspace must be zero-filled before its first use; every
- * call leaves it zero-filled again (the default kernel keeps one counter per
- * CTA there), so one memset at allocation suffices.  Returns 0 on error (e.g.
- * bad device).
+ * two CTAs, and (prefill shapes) one int per row for the row schedule.  The
+ * workspace must be zero-filled before its first use; every call leaves the
+ * counters it relies on zero again (one per CTA, at the start of the
+ * workspace), so one memset at allocation suffices.  A workspace sized by an
+ * older formula, without the per-row ints, still works (contiguous unit
+ * ranges).  Returns 0 on error (e.g. bad device).
  */
 size_t sa_workspace_bytes(int64_t b, int64_t m, int64_t topk, int device);
 

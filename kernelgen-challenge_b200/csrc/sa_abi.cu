@@ -6,6 +6,7 @@
 // an exception), and the kernel launch (:1006-1021).  The reference's
 // five-backend detection and try/except fallback tiers (:919-969,
 // :1026-1271) have no counterpart: there is one target, sm_100a.
+#include <cstdlib>
 #include <mutex>
 
 #include "sparse_attn.h"
@@ -89,6 +90,16 @@ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // Upper bound on the persistent grid of any variant on a device with `sms` SMs.
 int max_grid(int sms) { return 2 * sms; }
 
+// SA_ROW_SCHEDULE=0 in the environment keeps the contiguous unit ranges for
+// every shape (for comparisons); read once per process.
+bool row_schedule_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("SA_ROW_SCHEDULE");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
+
 }  // namespace
 
 extern "C" {
@@ -161,7 +172,7 @@ size_t sa_workspace_bytes(int64_t b, int64_t m, int64_t topk, int device) {
   const int64_t units_min = tokens * ceil_div(topk > 0 ? topk : 1, 16);
   if (units_min > 0 && units_min < grid) grid = units_min;
   if (grid < 1) grid = 1;
-  return sa::workspace_bytes_for_grid(static_cast<int>(grid));
+  return sa::workspace_bytes_for_grid(static_cast<int>(grid)) + sa::row_units_bytes(tokens);
 }
 
 // One group of 16 heads of sa_fwd_ex / sa_fwd_train; lse (nullable) is the
@@ -265,6 +276,14 @@ static int fwd_group(const void* q, const void* kv, const float* sink, const int
   // at its end); with fewer units per CTA (decode) nearly every CTA would end
   // in merges, and the combine kernel spreads them over the whole GPU instead.
   p.merge_in_kernel = (variant == SA_VARIANT_WS && p.units >= 2 * p.upt * p.grid) ? 1 : 0;
+  // With that many rows and room in the workspace for one int per row, the
+  // ws kernel runs whole rows instead (no split rows), each only up to its
+  // last valid slot (sa_ws.cu: row schedule).
+  if (p.merge_in_kernel && row_schedule_enabled() &&
+      workspace_bytes >= need + sa::row_units_bytes(b * m)) {
+    p.merge_in_kernel = 0;
+    p.row_units = reinterpret_cast<const int*>(ws + need);
+  }
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   e = (variant == SA_VARIANT_MMA)       ? sa::launch_mma(p, st)

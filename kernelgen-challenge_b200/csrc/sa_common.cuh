@@ -66,6 +66,10 @@ struct Params {
   // (p_t = 2^(s_t * scale * log2(e) - lse)); the backward pass reads it.
   float* lse;
   int64_t lse_rs;  // floats between lse rows (the caller's head count)
+  // Optional (ws kernel, many rows): units to run per row, written by
+  // sa_row_units_kernel; set, each CTA runs whole rows of a fixed snake
+  // order instead of a contiguous unit range (sa_ws.cu).
+  const int* row_units;
 };
 
 // log2 of the full denominator for a running max m and sum l (relative to m),
@@ -93,6 +97,11 @@ constexpr int kMaxGrid = 512;  // >= 2 x the SM count of any supported device
 constexpr size_t kTicketBytes = kMaxGrid * sizeof(int);
 __host__ __device__ constexpr size_t workspace_bytes_for_grid(int grid) {
   return kTicketBytes + ws_acc_bytes(grid) + ws_ml_bytes(grid);
+}
+
+// Row-unit counts (one int per row) after the partials, for the row schedule.
+__host__ __device__ constexpr size_t row_units_bytes(int64_t rows) {
+  return ((size_t)rows * sizeof(int) + 255) & ~(size_t)255;
 }
 
 __host__ __device__ inline int64_t unit_begin(int64_t g, int64_t units, int64_t grid) {

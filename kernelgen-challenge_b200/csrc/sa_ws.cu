@@ -89,6 +89,7 @@ struct __align__(1024) Smem {
   // split rows this CTA merges after its last unit (at most its first and last row)
   int n_merge;
   int64_t merge_row[2];
+  int n_units;  // row schedule: units of this CTA
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + manual 1 KiB alignment
 
@@ -117,9 +118,73 @@ __device__ __forceinline__ uint32_t p_chunk(int h, int ch) {
   return h * 128 + ((ch ^ (h & 7)) << 4);
 }
 
+// Row schedule (many rows, p.row_units set): CTA g runs whole rows, the
+// positions g, 2G-1-g, 2G+g, 4G-1-g, ... of the rows taken in descending
+// index order (snake rounds of G).  Every thread derives the same sequence.
+// When the costs fall along the row index (causal prefill, where row i holds
+// min(i+1, topk) slots followed by -1 padding) the rounds pair long rows
+// with short ones; equal rows get an equal share of rows.
+__device__ __forceinline__ int64_t snake_row(int64_t k, int64_t g, int64_t G, int64_t R) {
+  const int64_t pos = k * G + ((k & 1) ? (G - 1 - g) : g);
+  return pos < R ? R - 1 - pos : -1;
+}
+__device__ __forceinline__ int64_t units_of_row(const Params& p, int64_t r) {
+  return r >= 0 ? __ldg(p.row_units + r) : 0;
+}
+
+// Units per row for the row schedule: ceil((last valid slot + 1) / UK), at
+// least 1 (a row without a valid slot still writes o = 0).  Slots past that
+// point are masked padding: the forward kernel skips them, and the
+// out-of-range indices among them are counted here instead.  One warp per
+// row.
+__global__ void __launch_bounds__(256) sa_row_units_kernel(const Params p, int* row_units) {
+  const int64_t R = p.b * p.m;
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= R) return;
+  const int64_t tb = r / p.m, tm = r - tb * p.m;
+  const int32_t* row = p.idx + tb * p.i_sb + tm * p.i_sm;
+  int64_t last = -1;
+  const bool vec = p.i_sk == 1 && (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
+  if (vec) {
+    const int64_t nv = p.topk / 4;
+#pragma unroll 4
+    for (int64_t v = lane; v < nv; v += 32) {
+      const int4 w = __ldg(reinterpret_cast<const int4*>(row) + v);
+      if (w.x >= 0 && (int64_t)w.x < p.kv_len) last = 4 * v;
+      if (w.y >= 0 && (int64_t)w.y < p.kv_len) last = 4 * v + 1;
+      if (w.z >= 0 && (int64_t)w.z < p.kv_len) last = 4 * v + 2;
+      if (w.w >= 0 && (int64_t)w.w < p.kv_len) last = 4 * v + 3;
+    }
+    for (int64_t k = 4 * nv + lane; k < p.topk; k += 32) {
+      const int32_t id = __ldg(row + k);
+      if (id >= 0 && (int64_t)id < p.kv_len) last = k;
+    }
+  } else {
+    for (int64_t k = lane; k < p.topk; k += 32) {
+      const int32_t id = __ldg(row + k * p.i_sk);
+      if (id >= 0 && (int64_t)id < p.kv_len) last = k;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const int64_t o = __shfl_xor_sync(0xffffffffu, last, off);
+    last = o > last ? o : last;
+  }
+  const int64_t nu = last < 0 ? 1 : (last + UK) / UK;
+  if (lane == 0) row_units[r] = static_cast<int>(nu);
+  uint32_t faults = 0;
+  for (int64_t k = nu * UK + lane; k < p.topk; k += 32)
+    faults += index_fault(__ldg(row + k * p.i_sk), p.kv_len) ? 1u : 0u;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) faults += __shfl_xor_sync(0xffffffffu, faults, off);
+  if (lane == 0 && faults != 0) atomicAdd(&sa_ws_index_faults, (unsigned long long)faults);
+}
+
 // kLse: also write the row log-sum-exp (training forward); a separate
-// instance, so the inference kernel carries no trace of it.
-template <bool kLse>
+// instance, so the inference kernel carries no trace of it.  kRows: the row
+// schedule above instead of contiguous unit ranges (no split rows).
+template <bool kLse, bool kRows>
 __global__ void __launch_bounds__(NT, 1)
     sa_ws_fwd_kernel(const Params p, const __grid_constant__ CUtensorMap q_map) {
   extern __shared__ uint8_t smem_raw[];
@@ -127,13 +192,20 @@ __global__ void __launch_bounds__(NT, 1)
                                      ~static_cast<uintptr_t>(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t G = p.grid, g = blockIdx.x;
-  const int64_t u0 = unit_begin(g, p.units, G), u1 = unit_begin(g + 1, p.units, G);
-  const int n = static_cast<int>(u1 - u0);
-  if (n <= 0) return;
+  const int64_t R = p.b * p.m;
+  int64_t u0 = 0, u1 = 0;
+  if constexpr (kRows) {
+    if (g >= R) return;  // (the host keeps R >= 2G)
+  } else {
+    u0 = unit_begin(g, p.units, G);
+    u1 = unit_begin(g + 1, p.units, G);
+    if (u1 <= u0) return;
+  }
+  int n = static_cast<int>(u1 - u0);  // units of this CTA (row schedule: below)
   const int64_t upt = p.upt;
-  const int64_t t_first = u0 / upt;
-  const int64_t t_last = (u1 - 1) / upt;
-  const int64_t kb_first = u0 - t_first * upt;
+  const int64_t t_first = kRows ? snake_row(0, g, G, R) : u0 / upt;
+  const int64_t t_last = (u1 - 1) / upt;  // (unit ranges only)
+  const int64_t kb_first = kRows ? 0 : u0 - t_first * upt;
   // the combine kernel of split rows may launch now; it waits for this grid
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
@@ -145,13 +217,29 @@ __global__ void __launch_bounds__(NT, 1)
     mbar_init(smem_u32(&S.q_full), 1);
     S.err = 0;
     S.n_merge = 0;
+    S.n_units = 0;
     fence_mbar_init();
   }
   if (warp == 4 && lane == 0) tma_prefetch_desc(&q_map);
   // launched as a programmatic dependent of the previous kernel in the stream:
   // the set-up above overlaps its tail; inputs are read only after it is done
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if constexpr (kRows) {
+    // units of this CTA: the row-unit counts are the previous grid's output;
+    // every thread loads those of every NT-th row, all loads in flight at once
+    __syncthreads();  // (S.n_units initialised)
+    int part = 0;
+    for (int64_t k = tid;; k += NT) {
+      const int64_t r = snake_row(k, g, G, R);
+      if (r < 0) break;
+      part += static_cast<int>(units_of_row(p, r));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+    if (lane == 0 && part != 0) atomicAdd(&S.n_units, part);
+  }
   __syncthreads();
+  if constexpr (kRows) n = S.n_units;
 
   if (warp < 4) {
     // ------------------------------------------------------------ KV producer
@@ -164,6 +252,12 @@ __global__ void __launch_bounds__(NT, 1)
     const int c = tid & 63, par = tid >> 6, j = c >> 3, cc = c & 7;
     int64_t t = t_first, kb = kb_first;
     int64_t tb = t / p.m, tm = t - tb * p.m;
+    // row schedule: this row's units, the next row's (loaded a row ahead)
+    int64_t sk = 0, nu_t = upt, nu_n = 0;
+    if constexpr (kRows) {
+      nu_t = units_of_row(p, t);
+      nu_n = units_of_row(p, snake_row(1, g, G, R));
+    }
     auto load_ids = [&](int64_t kb_, int64_t tb_, int64_t tm_, int32_t& a, int32_t& b) {
       const int64_t k0 = kb_ * UK + 2 * lane;
       const int32_t* base = p.idx + tb_ * p.i_sb + tm_ * p.i_sm;
@@ -176,12 +270,20 @@ __global__ void __launch_bounds__(NT, 1)
       const int32_t ia = na, ib = nb;
       const int64_t cur_tb = tb;
       // advance the cursor and prefetch the next unit's indices
-      if (++kb == upt) {
+      if (++kb == nu_t) {
         kb = 0;
-        ++t;
-        if (++tm == p.m) {
-          tm = 0;
-          ++tb;
+        if constexpr (kRows) {
+          t = snake_row(++sk, g, G, R);
+          tb = t / p.m;
+          tm = t - tb * p.m;
+          nu_t = nu_n;
+          nu_n = units_of_row(p, snake_row(sk + 1, g, G, R));
+        } else {
+          ++t;
+          if (++tm == p.m) {
+            tm = 0;
+            ++tb;
+          }
         }
       }
       if (i + 1 < n) load_ids(kb, tb, tm, na, nb);
@@ -240,10 +342,15 @@ __global__ void __launch_bounds__(NT, 1)
     };
     if (tt == 0) issue_q(t_first);
     int64_t t = t_first, kb = kb_first, seg_kb0 = kb_first;
+    int64_t sk = 0, nu_t = upt, nu_n = 0;  // as in the producer
+    if constexpr (kRows) {
+      nu_t = units_of_row(p, t);
+      nu_n = units_of_row(p, snake_row(1, g, G, R));
+    }
     int seg = 0;
     bool seg_first = true;
     for (int i = 0; i < n; ++i) {
-      const bool seg_end = (i == n - 1) || kb == upt - 1;
+      const bool seg_end = (i == n - 1) || kb == nu_t - 1;
       if (seg_first) {
         m_lo = m_hi = -INFINITY;
 #pragma unroll
@@ -263,7 +370,12 @@ __global__ void __launch_bounds__(NT, 1)
           }
         }
         named_bar(4, NCT);
-        if (tt == 0 && t < t_last) issue_q(t + 1);
+        if constexpr (kRows) {
+          const int64_t tn = snake_row(sk + 1, g, G, R);
+          if (tt == 0 && tn >= 0) issue_q(tn);
+        } else if (tt == 0 && t < t_last) {
+          issue_q(t + 1);
+        }
       }
       const int slot = i % NSLOT;
       wait_or_err(S, S.full[slot], (i / NSLOT) & 1, 8);
@@ -400,7 +512,7 @@ __global__ void __launch_bounds__(NT, 1)
         // ---------------- epilogue of the segment ending at unit i ----------
         const int64_t tb = t / p.m, tm = t - tb * p.m;
         const float l_lo = lacc[0], l_hi = lacc[2];
-        if (seg_kb0 == 0 && kb == upt - 1) {
+        if (kRows || (seg_kb0 == 0 && kb == upt - 1)) {
           const float f_lo = sink_factor(m_lo, l_lo, __ldg(p.sink + g8) * kLog2e);
           const float f_hi = sink_factor(m_hi, l_hi, __ldg(p.sink + g8 + 8) * kLog2e);
           if (kLse && c == 0 && q4 == 0) {
@@ -452,9 +564,15 @@ __global__ void __launch_bounds__(NT, 1)
       if (seg_end && c == 0 && lane == 0) SA_TRACE_EV(i, 5);
       if (seg_end) ++seg;
       seg_first = seg_end;
-      if (++kb == upt) {
+      if (++kb == nu_t) {
         kb = 0;
-        ++t;
+        if constexpr (kRows) {
+          t = snake_row(++sk, g, G, R);
+          nu_t = nu_n;
+          nu_n = units_of_row(p, snake_row(sk + 1, g, G, R));
+        } else {
+          ++t;
+        }
       }
     }
   }
@@ -520,13 +638,23 @@ cudaError_t launch_ws(const Params& p, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   static PerDeviceOnce attr_once;
   e = once_per_device(attr_once, [] {
-    const cudaError_t e1 = cudaFuncSetAttribute(
-        sa_ws_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-    if (e1 != cudaSuccess) return e1;
-    return cudaFuncSetAttribute(sa_ws_fwd_kernel<true>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    for (auto* k : {sa_ws_fwd_kernel<false, false>, sa_ws_fwd_kernel<true, false>,
+                    sa_ws_fwd_kernel<false, true>, sa_ws_fwd_kernel<true, true>}) {
+      const cudaError_t e1 =
+          cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+      if (e1 != cudaSuccess) return e1;
+    }
+    return cudaSuccess;
   });
   if (e != cudaSuccess) return e;
+  const bool rows = p.row_units != nullptr;
+  if (rows) {  // the row-unit counts; a plain launch (it follows the previous op)
+    const int64_t R = p.b * p.m;
+    sa_row_units_kernel<<<static_cast<unsigned>((R + 7) / 8), 256, 0, st>>>(
+        p, const_cast<int*>(p.row_units));
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
   cfg.blockDim = dim3(NT, 1, 1);
@@ -537,9 +665,10 @@ cudaError_t launch_ws(const Params& p, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = p.lse != nullptr ? cudaLaunchKernelEx(&cfg, sa_ws_fwd_kernel<true>, p, q_map)
-                       : cudaLaunchKernelEx(&cfg, sa_ws_fwd_kernel<false>, p, q_map);
-  if (e != cudaSuccess || p.merge_in_kernel) return e;
+  auto* kern = p.lse != nullptr ? (rows ? sa_ws_fwd_kernel<true, true> : sa_ws_fwd_kernel<true, false>)
+                                : (rows ? sa_ws_fwd_kernel<false, true> : sa_ws_fwd_kernel<false, false>);
+  e = cudaLaunchKernelEx(&cfg, kern, p, q_map);
+  if (e != cudaSuccess || p.merge_in_kernel || rows) return e;
   return launch_combine(p, st);
 }
 

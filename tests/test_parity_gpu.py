@@ -274,6 +274,37 @@ def test_index_faults_counted(variant):
     assert_close(o, sparse_attn_oracle(q, kv, sink, idx, scale), what="faulty indices")
 
 
+@pytest.mark.parametrize("grid", [0, 3, 37])
+def test_row_schedule_trailing_padding(grid):
+    """Prefill shapes (rows >= 2 x grid) run whole rows per CTA, each only up
+    to its last valid slot.  Rows of causal form (valid prefix, then -1), rows
+    with no valid slot, interior -1, and out-of-range indices both inside the
+    run part and in the skipped tail: the output matches the oracle and every
+    out-of-range index is counted once."""
+    from sparse_attn._lib import index_faults
+    g = torch.Generator().manual_seed(41)
+    b, m, kv_len, topk = 2, 300, 900, 320
+    q = torch.randn(b, m, 16, 512, generator=g).to(torch.bfloat16)
+    kv = torch.randn(b, kv_len, 512, generator=g).to(torch.bfloat16)
+    sink = torch.randn(16, generator=g)
+    idx = torch.randint(0, kv_len, (b, m, topk), generator=g, dtype=torch.int32)
+    length = (torch.arange(m) + 1).clamp(max=topk)[None, :, None].expand(b, m, 1)
+    idx = torch.where(torch.arange(topk)[None, None, :] < length, idx, torch.full_like(idx, -1))
+    idx[0, 5] = -1                      # no valid slot
+    idx[1, 250, 3] = -1                 # interior -1
+    idx[1, 40, 7] = kv_len              # counted by the forward kernel (run part)
+    idx[0, 20, 200] = kv_len + 5        # in the skipped tail of a 21-slot row
+    idx[1, 0, 319] = -7                 # in the skipped tail of a 1-slot row
+    expected = 3
+    ref = sparse_attn_oracle(q, kv, sink, idx, 512 ** -0.5)
+    torch.cuda.synchronize()
+    index_faults(reset=True)
+    o = run_gpu(q, kv, sink, idx, 512 ** -0.5, variant=SA_VARIANT_WS, grid=grid)
+    assert index_faults(reset=True) == expected
+    assert_close(o, ref, what=f"row schedule grid={grid}")
+    assert torch.count_nonzero(o[0, 5]) == 0
+
+
 def test_workspace_reuse_across_grids():
     """Split rows are merged in the kernel by the last CTA to finish them
     (per-CTA counters in the workspace, zeroed again by every call): one
