@@ -366,6 +366,11 @@ static int fp8_group(const void* q, const void* kv8, const float* kv_scale, cons
   p.part_acc = reinterpret_cast<float*>(ws + sa::kTicketBytes);
   p.part_ml = reinterpret_cast<float*>(ws + sa::kTicketBytes + sa::ws_acc_bytes(p.grid));
   p.merge_in_kernel = p.units >= 2 * p.upt * p.grid ? 1 : 0;  // as for SA_VARIANT_WS
+  if (p.merge_in_kernel && row_schedule_enabled() &&
+      workspace_bytes >= need + sa::row_units_bytes(b * m)) {  // as in fwd_group
+    p.merge_in_kernel = 0;
+    p.row_units = reinterpret_cast<const int*>(ws + need);
+  }
   e = sa::launch_fp8(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail_cuda(e);
   return SA_OK;

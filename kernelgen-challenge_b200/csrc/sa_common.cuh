@@ -113,6 +113,49 @@ __host__ __device__ inline int64_t cta_of_unit(int64_t u, int64_t units, int64_t
   return ((u + 1) * grid - 1) / units;
 }
 
+// Row schedule (many rows, p.row_units set): CTA g runs whole rows, the
+// positions g, 2G-1-g, 2G+g, 4G-1-g, ... of the rows taken in descending
+// index order (snake rounds of G).  Every thread derives the same sequence.
+// When the costs fall along the row index (causal prefill, where row i holds
+// min(i+1, topk) slots followed by -1 padding) the rounds pair long rows
+// with short ones; equal rows get an equal share of rows.
+__device__ __forceinline__ int64_t snake_row(int64_t k, int64_t g, int64_t G, int64_t R) {
+  const int64_t pos = k * G + ((k & 1) ? (G - 1 - g) : g);
+  return pos < R ? R - 1 - pos : -1;
+}
+__device__ __forceinline__ int64_t units_of_row(const Params& p, int64_t r) {
+  return r >= 0 ? __ldg(p.row_units + r) : 0;
+}
+
+// A producer's place in the row schedule: row t (batch tb, row tm within
+// it), unit kb of its nu_t units; the next row's count is loaded a row ahead.
+struct RowCursor {
+  int64_t kb, tb, tm, t, sk, nu_t, nu_n;
+  __device__ __forceinline__ void start(const Params& p, int64_t g, int64_t G, int64_t R) {
+    sk = 0;
+    kb = 0;
+    t = snake_row(0, g, G, R);
+    tb = t / p.m;
+    tm = t - tb * p.m;
+    nu_t = units_of_row(p, t);
+    nu_n = units_of_row(p, snake_row(1, g, G, R));
+  }
+  __device__ __forceinline__ void advance(const Params& p, int64_t g, int64_t G, int64_t R) {
+    if (++kb == nu_t) {
+      kb = 0;
+      t = snake_row(++sk, g, G, R);
+      tb = t / p.m;
+      tm = t - tb * p.m;
+      nu_t = nu_n;
+      nu_n = units_of_row(p, snake_row(sk + 1, g, G, R));
+    }
+  }
+};
+
+// Writes p.row_units for the row schedule (sa_ws.cu; any forward kernel
+// with a kRows instance runs after it in the same stream).
+cudaError_t launch_row_units(const Params& p, cudaStream_t st);
+
 // Runs `fn` (returning cudaError_t) once per CUDA device, the first time it is
 // called with that device current; later calls return the first result.
 struct PerDeviceOnce {

@@ -47,6 +47,7 @@
 //
 // Every mbarrier wait is bounded; on a timeout the CTA records an error code
 // in sa_fp8_error (readable through sa_device_status) and stops issuing work.
+#include <type_traits>
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -91,6 +92,7 @@ struct __align__(1024) Smem {
   // split rows this CTA merges after its last unit (at most its first and last row)
   int n_merge;
   int64_t merge_row[2];
+  int n_units;  // row schedule: units of this CTA
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + manual 1 KiB alignment
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -198,6 +200,9 @@ struct Cursor {
   }
 };
 
+// kRows: the row schedule of sa_common.cuh (whole rows in snake order, each
+// up to its last valid slot) instead of contiguous unit ranges.
+template <bool kRows>
 __global__ void __launch_bounds__(NT, 1)
     sa_fp8_fwd_kernel(const Params p, const __grid_constant__ CUtensorMap q_map) {
   extern __shared__ uint8_t smem_raw[];
@@ -205,13 +210,20 @@ __global__ void __launch_bounds__(NT, 1)
                                      ~static_cast<uintptr_t>(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t G = p.grid, g = blockIdx.x;
-  const int64_t u0 = unit_begin(g, p.units, G), u1 = unit_begin(g + 1, p.units, G);
-  const int n = static_cast<int>(u1 - u0);
-  if (n <= 0) return;
+  const int64_t nrows = p.b * p.m;
+  int64_t u0 = 0, u1 = 0;
+  if constexpr (kRows) {
+    if (g >= nrows) return;  // (the host keeps rows >= 2G)
+  } else {
+    u0 = unit_begin(g, p.units, G);
+    u1 = unit_begin(g + 1, p.units, G);
+    if (u1 <= u0) return;
+  }
+  int n = static_cast<int>(u1 - u0);  // units of this CTA (row schedule: below)
   const int64_t upt = p.upt;
-  const int64_t t_first = u0 / upt;
-  const int64_t t_last = (u1 - 1) / upt;
-  const int64_t kb_first = u0 - t_first * upt;
+  const int64_t t_first = kRows ? snake_row(0, g, G, nrows) : u0 / upt;
+  const int64_t t_last = (u1 - 1) / upt;  // (unit ranges only)
+  const int64_t kb_first = kRows ? 0 : u0 - t_first * upt;
   // the combine kernel of split rows may launch now; it waits for this grid
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
@@ -223,11 +235,25 @@ __global__ void __launch_bounds__(NT, 1)
     mbar_init(smem_u32(&S.q_full), 1);
     S.err = 0;
     S.n_merge = 0;
+    S.n_units = 0;
     fence_mbar_init();
   }
   if (warp == 4 && lane == 0) tma_prefetch_desc(&q_map);
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if constexpr (kRows) {  // units of this CTA, all row counts loaded at once
+    __syncthreads();      // (S.n_units initialised)
+    int part = 0;
+    for (int64_t k = tid;; k += NT) {
+      const int64_t r = snake_row(k, g, G, nrows);
+      if (r < 0) break;
+      part += static_cast<int>(units_of_row(p, r));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+    if (lane == 0 && part != 0) atomicAdd(&S.n_units, part);
+  }
   __syncthreads();
+  if constexpr (kRows) n = S.n_units;
 
   if (warp < 4) {
     // ------------------------------------------------------------ producer
@@ -237,7 +263,7 @@ __global__ void __launch_bounds__(NT, 1)
     // dependent global load stalls the copy issue.
     const uint64_t pol = l2_policy_evict_first();
     const uint8_t* kv8 = reinterpret_cast<const uint8_t*>(p.kv);
-    auto load_ids = [&](const Cursor& cu, int32_t& a, int32_t& b) {
+    auto load_ids = [&](const auto& cu, int32_t& a, int32_t& b) {
       const int64_t k0 = cu.kb * UK + 2 * lane;
       const int32_t* base = p.idx + cu.tb * p.i_sb + cu.tm * p.i_sm;
       a = k0 < p.topk ? __ldg(base + k0 * p.i_sk) : -1;
@@ -249,13 +275,25 @@ __global__ void __launch_bounds__(NT, 1)
       sa_ = valid(a) ? __ldg(base + (int64_t)a * p.ks_sn) : 0.f;
       sb_ = valid(b) ? __ldg(base + (int64_t)b * p.ks_sn) : 0.f;
     };
-    Cursor cu{kb_first, t_first / p.m, t_first - (t_first / p.m) * p.m};
+    std::conditional_t<kRows, RowCursor, Cursor> cu;
+    if constexpr (kRows) {
+      cu.start(p, g, G, nrows);
+    } else {
+      cu = Cursor{kb_first, t_first / p.m, t_first - (t_first / p.m) * p.m};
+    }
+    auto advance = [&] {
+      if constexpr (kRows) {
+        cu.advance(p, g, G, nrows);
+      } else {
+        cu.advance(upt, p.m);
+      }
+    };
     int32_t xa0, xb0, xa1 = -1, xb1 = -1;  // indices of units i and i+1
     int64_t tb0 = cu.tb, tb1 = cu.tb;
     float sa0 = 0.f, sb0 = 0.f;           // scales of unit i (warp 0)
     load_ids(cu, xa0, xb0);
     if (warp == 0) load_scales(tb0, xa0, xb0, sa0, sb0);
-    cu.advance(upt, p.m);
+    advance();
     if (n > 1) {
       load_ids(cu, xa1, xb1);
       tb1 = cu.tb;
@@ -267,7 +305,7 @@ __global__ void __launch_bounds__(NT, 1)
       xa0 = xa1;
       xb0 = xb1;
       tb0 = tb1;
-      cu.advance(upt, p.m);  // unit i + 2
+      advance();  // unit i + 2
       if (i + 2 < n) {
         load_ids(cu, xa1, xb1);
         tb1 = cu.tb;
@@ -335,10 +373,15 @@ __global__ void __launch_bounds__(NT, 1)
     };
     if (tt == 0) issue_q(t_first);
     int64_t t = t_first, kb = kb_first, seg_kb0 = kb_first;
+    int64_t sk = 0, nu_t = upt, nu_n = 0;  // row schedule: as RowCursor
+    if constexpr (kRows) {
+      nu_t = units_of_row(p, t);
+      nu_n = units_of_row(p, snake_row(1, g, G, nrows));
+    }
     int seg = 0;
     bool seg_first = true;
     for (int i = 0; i < n; ++i) {
-      const bool seg_end = (i == n - 1) || kb == upt - 1;
+      const bool seg_end = (i == n - 1) || kb == nu_t - 1;
       if (seg_first) {
         m_lo = m_hi = -INFINITY;
         R = invR = 0.f;
@@ -393,7 +436,12 @@ __global__ void __launch_bounds__(NT, 1)
         // (The previous row's f16 tile reads all came before the previous
         // unit's vote barrier; its red_max reads before its P barrier.)
         named_bar(4, NCT);
-        if (tt == 0 && t < t_last) issue_q(t + 1);
+        if constexpr (kRows) {
+          const int64_t tn = snake_row(sk + 1, g, G, nrows);
+          if (tt == 0 && tn >= 0) issue_q(tn);
+        } else if (tt == 0 && t < t_last) {
+          issue_q(t + 1);
+        }
 #pragma unroll
         for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
         lacc[0] = lacc[1] = lacc[2] = lacc[3] = 0.f;
@@ -569,7 +617,7 @@ __global__ void __launch_bounds__(NT, 1)
         // ---------------- epilogue of the segment ending at unit i ----------
         const int64_t tb = t / p.m, tm = t - tb * p.m;
         const float l_lo = lacc[0], l_hi = lacc[2];
-        if (seg_kb0 == 0 && kb == upt - 1) {
+        if (kRows || (seg_kb0 == 0 && kb == upt - 1)) {
           const float f_lo = sink_factor(m_lo, l_lo, __ldg(p.sink + g8) * kLog2e) * R;
           const float f_hi = sink_factor(m_hi, l_hi, __ldg(p.sink + g8 + 8) * kLog2e) * R;
           __nv_bfloat16* ob = p.o + tb * p.o_sb + tm * p.o_sm;
@@ -626,9 +674,15 @@ __global__ void __launch_bounds__(NT, 1)
       }
       if (seg_end) ++seg;
       seg_first = seg_end;
-      if (++kb == upt) {
+      if (++kb == nu_t) {
         kb = 0;
-        ++t;
+        if constexpr (kRows) {
+          t = snake_row(++sk, g, G, nrows);
+          nu_t = nu_n;
+          nu_n = units_of_row(p, snake_row(sk + 1, g, G, nrows));
+        } else {
+          ++t;
+        }
       }
     }
   }
@@ -738,10 +792,18 @@ cudaError_t launch_fp8(const Params& p, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   static PerDeviceOnce attr_once;
   e = once_per_device(attr_once, [] {
-    return cudaFuncSetAttribute(sa_fp8_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)kSmemBytes);
+    const cudaError_t e1 = cudaFuncSetAttribute(
+        sa_fp8_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e1 != cudaSuccess) return e1;
+    return cudaFuncSetAttribute(sa_fp8_fwd_kernel<true>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
   });
   if (e != cudaSuccess) return e;
+  const bool rows = p.row_units != nullptr;
+  if (rows) {
+    e = launch_row_units(p, st);
+    if (e != cudaSuccess) return e;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
   cfg.blockDim = dim3(NT, 1, 1);
@@ -752,8 +814,9 @@ cudaError_t launch_fp8(const Params& p, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, sa_fp8_fwd_kernel, p, q_map);
-  if (e != cudaSuccess || p.merge_in_kernel) return e;
+  e = cudaLaunchKernelEx(&cfg, rows ? sa_fp8_fwd_kernel<true> : sa_fp8_fwd_kernel<false>, p,
+                         q_map);
+  if (e != cudaSuccess || p.merge_in_kernel || rows) return e;
   return launch_combine(p, st);
 }
 

@@ -118,20 +118,6 @@ __device__ __forceinline__ uint32_t p_chunk(int h, int ch) {
   return h * 128 + ((ch ^ (h & 7)) << 4);
 }
 
-// Row schedule (many rows, p.row_units set): CTA g runs whole rows, the
-// positions g, 2G-1-g, 2G+g, 4G-1-g, ... of the rows taken in descending
-// index order (snake rounds of G).  Every thread derives the same sequence.
-// When the costs fall along the row index (causal prefill, where row i holds
-// min(i+1, topk) slots followed by -1 padding) the rounds pair long rows
-// with short ones; equal rows get an equal share of rows.
-__device__ __forceinline__ int64_t snake_row(int64_t k, int64_t g, int64_t G, int64_t R) {
-  const int64_t pos = k * G + ((k & 1) ? (G - 1 - g) : g);
-  return pos < R ? R - 1 - pos : -1;
-}
-__device__ __forceinline__ int64_t units_of_row(const Params& p, int64_t r) {
-  return r >= 0 ? __ldg(p.row_units + r) : 0;
-}
-
 // Units per row for the row schedule: ceil((last valid slot + 1) / UK), at
 // least 1 (a row without a valid slot still writes o = 0).  Slots past that
 // point are masked padding: the forward kernel skips them, and the
@@ -631,6 +617,15 @@ int read_ws_error(int* flags) {
 
 cudaError_t encode_q_map(const Params& p, CUtensorMap* q_map);  // sa_tc.cu
 
+// A plain launch: it follows the previous op in the stream, and the forward
+// kernel after it waits for it (griddepcontrol.wait) before reading counts.
+cudaError_t launch_row_units(const Params& p, cudaStream_t st) {
+  const int64_t R = p.b * p.m;
+  ws_path::sa_row_units_kernel<<<static_cast<unsigned>((R + 7) / 8), 256, 0, st>>>(
+      p, const_cast<int*>(p.row_units));
+  return cudaGetLastError();
+}
+
 cudaError_t launch_ws(const Params& p, cudaStream_t st) {
   using namespace ws_path;
   CUtensorMap q_map;
@@ -648,11 +643,8 @@ cudaError_t launch_ws(const Params& p, cudaStream_t st) {
   });
   if (e != cudaSuccess) return e;
   const bool rows = p.row_units != nullptr;
-  if (rows) {  // the row-unit counts; a plain launch (it follows the previous op)
-    const int64_t R = p.b * p.m;
-    sa_row_units_kernel<<<static_cast<unsigned>((R + 7) / 8), 256, 0, st>>>(
-        p, const_cast<int*>(p.row_units));
-    e = cudaGetLastError();
+  if (rows) {
+    e = launch_row_units(p, st);
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg = {};

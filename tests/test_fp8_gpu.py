@@ -125,6 +125,33 @@ def test_fp8_head_counts(h):
     assert_close(o, ref, what=f"fp8 h={h}")
 
 
+@pytest.mark.parametrize("grid", [0, 3, 37])
+def test_fp8_row_schedule_trailing_padding(grid):
+    """Prefill shapes run whole rows per CTA up to each row's last valid slot
+    (the bf16 kernel's row schedule); out-of-range indices in the skipped
+    tails are still counted."""
+    from sparse_attn._lib import index_faults
+    g = torch.Generator().manual_seed(43)
+    b, m, kv_len, topk = 2, 300, 900, 320
+    q = torch.randn(b, m, 16, 512, generator=g).to(torch.bfloat16)
+    kv = torch.randn(b, kv_len, 512, generator=g).to(torch.bfloat16)
+    sink = torch.randn(16, generator=g)
+    idx = torch.randint(0, kv_len, (b, m, topk), generator=g, dtype=torch.int32)
+    length = (torch.arange(m) + 1).clamp(max=topk)[None, :, None].expand(b, m, 1)
+    idx = torch.where(torch.arange(topk)[None, None, :] < length, idx, torch.full_like(idx, -1))
+    idx[0, 5] = -1
+    idx[1, 40, 7] = kv_len
+    idx[0, 20, 200] = kv_len + 5
+    kv8, ks = quantize_kv_fp8_ref(kv)
+    ref = sparse_attn_fp8_oracle(q, kv8, ks, sink, idx, 512 ** -0.5)
+    torch.cuda.synchronize()
+    index_faults(reset=True)
+    o = run_fp8(q, kv8, ks, sink, idx, 512 ** -0.5, grid=grid)
+    assert index_faults(reset=True) == 2
+    assert_close(o, ref, what=f"fp8 row schedule grid={grid}")
+    assert torch.count_nonzero(o[0, 5]) == 0
+
+
 def test_fp8_scales_spanning_decades():
     """Token scales that grow along the key order exercise the running
     scale maximum (O rescaled whenever a unit brings a larger scale)."""
