@@ -296,8 +296,9 @@ def measure_e2e(cfg, q, kv, kscale, sink, idx, dev, stream, flush, K, barrier, w
     """The metric through the public op with host-resident q and indices.
 
     Every step copies its q and indices from pinned host memory to the GPU,
-    runs ``sparse_attn`` (or ``sparse_attn_fp8``) and copies o back to pinned
-    host memory.  Pipelined, as a serving loop runs it (captured in CUDA
+    runs ``sparse_attn_out`` (or ``sparse_attn_fp8_out``: the public op with a
+    caller-owned output, as a serving loop calls it) and copies o back to
+    pinned host memory.  Pipelined, as a serving loop runs it (captured in CUDA
     graphs, see below): the copies of later steps overlap the op of earlier
     ones, on two copy streams.  L2 is not flushed here; instead the steps rotate over four
     distinct index sets, whose gathered rows (4 x the valid slots x row bytes)
@@ -308,26 +309,42 @@ def measure_e2e(cfg, q, kv, kscale, sink, idx, dev, stream, flush, K, barrier, w
     ke = min(K, 100)
     nset = 4
     q_h = q.cpu().pin_memory()
-    idx_hs = [idx.cpu().pin_memory()] + [
-        make_indices(cfg, torch.Generator().manual_seed(seed + 7919 * r)).pin_memory()
-        for r in range(1, nset)]
-    o_hs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(2)]
+    idx_cpu = [idx.cpu()] + [make_indices(cfg, torch.Generator().manual_seed(seed + 7919 * r))
+                             for r in range(1, nset)]
+    idx_hs = [t.pin_memory() for t in idx_cpu]
+    # A serving loop stages each step's q and indices in one pinned slab, so
+    # one host-to-device copy per step carries both (two copies cost ~15 %).
+    qb, ib = q.numel() * q.element_size(), idx.numel() * idx.element_size()
+    slab_h = []
+    for r in range(nset):
+        h = torch.empty(qb + ib, dtype=torch.uint8).pin_memory()
+        h[:qb].copy_(q_h.reshape(-1).view(torch.uint8))
+        h[qb:].copy_(idx_hs[r].reshape(-1).view(torch.uint8))
+        slab_h.append(h)
 
-    def op(qd, idd):
-        return (sparse_attn.sparse_attn_fp8(qd, kv, kscale, sink, idd, SCALE) if fp8
-                else sparse_attn.sparse_attn(qd, kv, sink, idd, SCALE))
+    def op_out(o, qd, idd):
+        if fp8:
+            sparse_attn.sparse_attn_fp8_out(o, qd, kv, kscale, sink, idd, SCALE)
+        else:
+            sparse_attn.sparse_attn_out(o, qd, kv, sink, idd, SCALE)
+        return o
 
     # One CUDA graph holds S steps, each with its own device buffers: the
     # host-to-device copies run in order on one copy stream, step j's op waits
     # only for its own inputs (so it overlaps the copies of later steps), and
     # its device-to-host copy runs on a second copy stream.  Replaying the
-    # graph keeps the host out of the loop, as a decode server does.
-    S = 8
+    # graph keeps the host out of the loop, as a decode server does.  S is as
+    # large as 256 MiB of step buffers allows (32 at decode): every graph
+    # boundary drains the pipeline once.
+    step_bytes = qb + ib + qb
+    S = int(max(2, min(32, (256 << 20) // step_bytes)))
     cin, cout = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    qd = [torch.empty_like(q) for _ in range(S)]
-    idd = [torch.empty_like(idx) for _ in range(S)]
+    slab_d = [torch.empty(qb + ib, dtype=torch.uint8, device=dev) for _ in range(S)]
+    qd = [x[:qb].view(q.dtype).view(q.shape) for x in slab_d]
+    idd = [x[qb:].view(idx.dtype).view(idx.shape) for x in slab_d]
+    od = [torch.empty_like(q) for _ in range(S)]
     o_hs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(S)]
-    op(qd[0].copy_(q), idd[0].copy_(idx))  # workspace of the capture stream, module loads
+    op_out(od[0], qd[0].copy_(q), idd[0].copy_(idx))  # workspace of the capture stream, module loads
     torch.cuda.synchronize()
     graphs = []
     for gi in range(nset):  # one graph per rotation of the index sets
@@ -339,14 +356,13 @@ def measure_e2e(cfg, q, kv, kscale, sink, idx, dev, stream, flush, K, barrier, w
             ins = []
             with torch.cuda.stream(cin):
                 for j in range(S):
-                    qd[j].copy_(q_h, non_blocking=True)
-                    idd[j].copy_(idx_hs[(gi * S + j) % nset], non_blocking=True)
+                    slab_d[j].copy_(slab_h[(gi * S + j) % nset], non_blocking=True)
                     ev = torch.cuda.Event()
                     ev.record(cin)
                     ins.append(ev)
             for j in range(S):
                 cs.wait_event(ins[j])
-                out = op(qd[j], idd[j])
+                out = op_out(od[j], qd[j], idd[j])
                 ev = torch.cuda.Event()
                 ev.record(cs)
                 with torch.cuda.stream(cout):
@@ -370,10 +386,12 @@ def measure_e2e(cfg, q, kv, kscale, sink, idx, dev, stream, flush, K, barrier, w
     ke_p = reps * S
 
     # serial: copy in, op, copy out on one stream, L2 flushed before each step
-    def serial_step(k):
+    def serial_step(k):  # the drop-in call, as a caller with no staging would make it
         qs = q_h.to(dev, non_blocking=True)
         ids = idx_hs[k % nset].to(dev, non_blocking=True)
-        o_hs[0].copy_(op(qs, ids), non_blocking=True)
+        o = (sparse_attn.sparse_attn_fp8(qs, kv, kscale, sink, ids, SCALE) if fp8
+             else sparse_attn.sparse_attn(qs, kv, sink, ids, SCALE))
+        o_hs[0].copy_(o, non_blocking=True)
 
     es = [torch.cuda.Event(enable_timing=True) for _ in range(ke)]
     ee = [torch.cuda.Event(enable_timing=True) for _ in range(ke)]
@@ -394,12 +412,15 @@ def measure_e2e(cfg, q, kv, kscale, sink, idx, dev, stream, flush, K, barrier, w
             + idx_hs[0].numel() * idx_hs[0].element_size(),
             "d2h_bytes_per_step": q.numel() * q.element_size(),
             "steps": ke_p, "kv_cache_resident": True,
-            "api": "sparse_attn.sparse_attn_fp8" if fp8 else "sparse_attn.sparse_attn",
-            "pipelined": f"CUDA graphs of {S} steps replayed: each step's H2D copy (pinned), "
-                         "op and D2H copy; copies of later steps overlap the op of earlier "
-                         "ones (two copy streams); 4 rotating index sets instead of an L2 flush",
+            "api": "sparse_attn.sparse_attn_fp8_out" if fp8 else "sparse_attn.sparse_attn_out",
+            "pipelined": f"CUDA graphs of {S} steps replayed: each step's H2D copy of q and "
+                         "the indices (one pinned slab), op into a preallocated o, D2H copy "
+                         "of o; copies of later steps overlap the op of earlier ones (two "
+                         "copy streams); 4 rotating index sets instead of an L2 flush",
             "serial": {"value": world * tokens * ke / (s_ms / 1e3),
-                       "note": "no overlap, 256 MiB L2 flush before every step"}}
+                       "api": "sparse_attn.sparse_attn_fp8" if fp8 else "sparse_attn.sparse_attn",
+                       "note": "no overlap, two H2D copies, 256 MiB L2 flush before every "
+                               "step"}}
 
 
 def run_hc_sinkhorn(args):
