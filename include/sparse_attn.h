@@ -141,8 +141,9 @@ int sa_quantize_kv_fp8(const void* kv, void* kv8, float* kv_scale, int64_t b, in
 
 /* Debug/health query, synchronous: copies into *flags the error word that the
  * pipelined kernels (SA_VARIANT_TCGEN05, SA_VARIANT_WS; the latter reported
- * as 100 + code, sa_fwd_fp8 as 200 + code) set on the current device when one of their bounded
- * pipeline waits gave up (0 = never).  Intended for tests and health checks,
+ * as 100 + code, sa_fwd_fp8 as 200 + code, the tensor-core scorer of
+ * sa_indexer_topk as 300 + code) set on the current device when one of their
+ * bounded pipeline waits gave up (0 = never).  Intended for tests and health checks,
  * not the hot path.  No counterpart in the reference. */
 int sa_device_status(int* flags);
 

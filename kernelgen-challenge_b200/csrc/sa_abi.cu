@@ -30,6 +30,7 @@ int read_mma_index_faults(unsigned long long* out, bool reset);
 cudaError_t launch_fp8(const Params& p, cudaStream_t st);
 int fp8_unit_keys();
 int read_fp8_error(int* flags);
+int read_indexer_error(int* flags);
 int read_fp8_index_faults(unsigned long long* out, bool reset);
 struct QuantParams {
   const __nv_bfloat16* kv;
@@ -127,12 +128,13 @@ int sa_last_cuda_error(void) { return t_last_cuda_error; }
 
 int sa_device_status(int* flags) {
   if (flags == nullptr) return SA_ERR_INVALID_ARG;
-  int a = 0, b = 0, f = 0;
+  int a = 0, b = 0, f = 0, x = 0;
   int e = sa::read_tc_error(&a);
   if (e == 0) e = sa::read_ws_error(&b);
   if (e == 0) e = sa::read_fp8_error(&f);
+  if (e == 0) e = sa::read_indexer_error(&x);
   if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
-  *flags = a != 0 ? a : (b != 0 ? 100 + b : (f != 0 ? 200 + f : 0));
+  *flags = a != 0 ? a : (b != 0 ? 100 + b : (f != 0 ? 200 + f : (x != 0 ? 300 + x : 0)));
   return SA_OK;
 }
 

@@ -533,6 +533,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 
 }  // namespace
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return encoder(); }
+
 bool tc_available() { return true; }
 int tc_unit_keys() { return tc_path::UK; }
 int tc_ctas_per_sm() { return 1; }

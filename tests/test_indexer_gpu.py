@@ -91,3 +91,47 @@ def test_indexer_feeds_sparse_attn():
     ref = sparse_attn_oracle(qa, kv, sink, idx.cpu(), 512 ** -0.5)
     from helpers import assert_close
     assert_close(o, ref, what="indexer -> sparse_attn")
+
+
+def test_strided_inputs_and_many_rows_per_cta():
+    """q and k as slices of wider buffers (the tensor maps take the strides);
+    130 rows of 700 keys put several rows and a partial last tile in every
+    persistent CTA's range."""
+    from sparse_attn import indexer_topk
+    q, k, w, ln = _inputs(2, 65, 700, seed=7)
+    ln[0, 3] = 0
+    ln[1, 10] = 129
+    qw = torch.zeros(2, 65, 80, 128, dtype=torch.bfloat16)
+    qw[:, :, 8:72] = q
+    kw = torch.zeros(2, 700, 192, dtype=torch.bfloat16)
+    kw[:, :, 64:] = k
+    qs, ks = qw.cuda()[:, :, 8:72], kw.cuda()[:, :, 64:]
+    idx, sc = indexer_topk(qs, ks, w.cuda(), ln.cuda(), 100, return_scores=True)
+    idx0, sc0 = indexer_topk(q.cuda(), k.cuda(), w.cuda(), ln.cuda(), 100, return_scores=True)
+    assert torch.equal(sc, sc0) and torch.equal(idx, idx0)
+    _check(q, k, w, ln, 100, "many rows per CTA")
+
+
+@pytest.mark.parametrize("m", [2, 5, 9])
+def test_row_groups_of_four(m):
+    """m > 1 runs groups of four rows against each k tile (the last group
+    partial), with different length limits inside a group."""
+    q, k, w, _ = _inputs(3, m, 1000, seed=20 + m)
+    ln = torch.randint(0, 1001, (3, m), generator=torch.Generator().manual_seed(m),
+                       dtype=torch.int32)
+    ln[0, 0] = 1000
+    _check(q, k, w, ln, 64, f"groups m={m}")
+
+
+def test_unaligned_weight_rows_use_the_warp_mma_scorer():
+    """Weight rows whose stride is not a multiple of 16 bytes cannot be
+    described by a tensor map: the same results come from the other scorer."""
+    from sparse_attn import indexer_topk
+    q, k, w, ln = _inputs(1, 6, 600, seed=9)
+    wb = torch.zeros(1, 6, 65)
+    wb[:, :, :64] = w
+    idx, sc = indexer_topk(q.cuda(), k.cuda(), wb.cuda()[:, :, :64], ln.cuda(), 50,
+                           return_scores=True)
+    _check(q, k, w, ln, 50, "unaligned weights (reference run)")
+    ref = indexer_scores_oracle(q, k, w, ln)
+    assert bool(((sc.cpu() - ref).abs() <= 1e-4 * ref.abs().max() + 1e-6).all())
