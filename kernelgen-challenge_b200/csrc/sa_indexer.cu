@@ -453,7 +453,6 @@ __global__ void __launch_bounds__(NTX, 1)
 // owns a contiguous block of keys, read 32 at a time, with ballots giving the
 // output positions.  The output row is contiguous.
 // ---------------------------------------------------------------------------
-constexpr int NT2 = 512;
 
 __device__ __forceinline__ uint32_t order_key(float x) {  // larger float -> larger key
   const uint32_t u = __float_as_uint(x);
@@ -465,7 +464,11 @@ __device__ __forceinline__ uint32_t order_key(float x) {  // larger float -> lar
 // the fp32 score buffer, L2-resident, every time).
 constexpr int kSmemKeys = 49152;  // 192 KiB
 
-__global__ void __launch_bounds__(NT2, 1) sa_indexer_topk_kernel(const IdxParams P) {
+// NT2 threads per row: 512 for long rows, 128 for rows of up to kShortRow
+// keys, so that more rows (each a chain of barriers) run side by side.
+constexpr int kShortRow = 8192;
+template <int NT2>
+__global__ void __launch_bounds__(NT2) sa_indexer_topk_kernel(const IdxParams P) {
   extern __shared__ float staged[];
   __shared__ int hist[256];
   __shared__ uint32_t sel_digit;
@@ -722,7 +725,12 @@ cudaError_t launch_indexer(const __nv_bfloat16* q, const __nv_bfloat16* k, const
     cudaError_t e1 = cudaFuncSetAttribute(sa_indexer_score_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e1 != cudaSuccess) return e1;
-    return cudaFuncSetAttribute(sa_indexer_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e1 = cudaFuncSetAttribute(sa_indexer_topk_kernel<128>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)(kShortRow * sizeof(float)));
+    if (e1 != cudaSuccess) return e1;
+    return cudaFuncSetAttribute(sa_indexer_topk_kernel<512>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)(kSmemKeys * sizeof(float)));
   });
   if (e != cudaSuccess) return e;
@@ -743,7 +751,11 @@ cudaError_t launch_indexer(const __nv_bfloat16* q, const __nv_bfloat16* k, const
     if (e != cudaSuccess) return e;
   }
   const size_t staged = kv_len <= kSmemKeys ? (size_t)kv_len * sizeof(float) : 0;
-  sa_indexer_topk_kernel<<<static_cast<unsigned>(rows), NT2, staged, st>>>(P);
+  if (kv_len <= kShortRow) {
+    sa_indexer_topk_kernel<128><<<static_cast<unsigned>(rows), 128, staged, st>>>(P);
+  } else {
+    sa_indexer_topk_kernel<512><<<static_cast<unsigned>(rows), 512, staged, st>>>(P);
+  }
   return cudaGetLastError();
 }
 
