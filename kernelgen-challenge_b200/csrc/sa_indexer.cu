@@ -11,7 +11,10 @@
 //     order, ties at the threshold to the lower index, -1 padded when fewer
 //     keys are valid.
 //
-// Kernel 1, sa_indexer_score_kernel: one CTA per (query row, 4096-key span),
+// Kernel 1, the scores: sa_indexer_score_tc_kernel (tcgen05, described at its
+// definition) by default; sa_indexer_score_kernel, the warp-MMA version, when
+// the weight rows cannot be described by a tensor map.  The latter runs one
+// CTA per (query row, 4096-key span),
 // 4 warps.  The row's q (H = 64 heads x 128 dims, bf16) sits in shared
 // memory; 64-key tiles of k stream through a 2-deep cp.async ring.  Warp w
 // computes heads 16w..16w+15 against the tile: 8 n-tiles x 8 k-steps of
@@ -21,9 +24,9 @@
 // written to a fp32 [b*m, kv_len] buffer.
 // Kernel 2, sa_indexer_topk_kernel: one CTA per query row, its scores staged
 // in shared memory (rows up to 48 Ki keys), radix select of the topk-th
-// largest score over order-preserving uint32 keys (four 8-bit histogram
-// rounds), then a compaction pass that writes the selected indices in
-// ascending order.
+// largest score over order-preserving uint32 keys (an 11-bit round over the
+// row, then 11- and 10-bit rounds over the keys of the selected bin), then a
+// compaction pass that writes the selected indices in ascending order.
 #include <cstdlib>
 
 #include <cuda.h>
@@ -459,19 +462,101 @@ __device__ __forceinline__ uint32_t order_key(float x) {  // larger float -> lar
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Rows of up to kSmemKeys scores are staged in shared memory once; the four
+// Rows of up to kSmemKeys scores are staged in shared memory once; the
 // histogram rounds and the compaction then read them there (longer rows read
 // the fp32 score buffer, L2-resident, every time).
 constexpr int kSmemKeys = 49152;  // 192 KiB
 
+// Inclusive prefix sum over the block (NT threads); `scratch` holds NT/32 ints.
+template <int NT>
+__device__ __forceinline__ int block_incl_scan(int v, int* scratch) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int inc = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, inc, off);
+    if (lane >= off) inc += y;
+  }
+  if (lane == 31) scratch[wid] = inc;
+  __syncthreads();
+  int before = 0;
+#pragma unroll
+  for (int w = 0; w < NT / 32; ++w) before += w < wid ? scratch[w] : 0;
+  __syncthreads();  // scratch reused by the next scan
+  return before + inc;
+}
+
+// One radix round over n keys (get(i) -> order key): among the keys whose
+// bits under `pmask` equal `prefix`, histogram the BITS-bit digit at `shift`
+// (warp-aggregated shared-memory adds: most keys share few digits), then find
+// the digit holding rank kk counted from the largest.  Returns the digit and
+// leaves in kk the rank still to find among the keys with that digit.
+template <int NT, int BITS, class Get>
+__device__ __forceinline__ uint32_t radix_round(Get get, int n, uint32_t prefix, uint32_t pmask,
+                                                int shift, int& kk, int* hist, int* scratch,
+                                                int* sh) {
+  constexpr int NB = 1 << BITS, BPT = (NB + NT - 1) / NT;
+  const int tid = threadIdx.x;
+  for (int d = tid; d < NB; d += NT) hist[d] = 0;
+  __syncthreads();
+  for (int base = 0; base < n; base += NT) {
+    const int i = base + tid;
+    uint32_t d = NB;  // no bin
+    if (i < n) {
+      const uint32_t key = get(i);
+      if ((key & pmask) == prefix) d = (key >> shift) & (NB - 1);
+    }
+    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    if (d < NB && (__ffs(peers) - 1) == (tid & 31)) atomicAdd(&hist[d], __popc(peers));
+  }
+  __syncthreads();
+  // thread t owns bins NB-1-t*BPT down to NB-(t+1)*BPT: counts from the top
+  int c = 0;
+#pragma unroll
+  for (int e = 0; e < BPT; ++e) {
+    const int b = NB - 1 - tid * BPT - e;
+    if (b >= 0) c += hist[b];
+  }
+  const int inc = block_incl_scan<NT>(c, scratch);
+  const int before = inc - c;
+  if (before < kk && kk <= inc) {
+    int acc = before;
+    for (int e = 0; e < BPT; ++e) {
+      const int b = NB - 1 - tid * BPT - e;
+      if (acc + hist[b] >= kk) {
+        sh[0] = b;
+        sh[1] = kk - acc;
+        break;
+      }
+      acc += hist[b];
+    }
+  }
+  __syncthreads();
+  const uint32_t digit = static_cast<uint32_t>(sh[0]);
+  kk = sh[1];
+  __syncthreads();  // hist and sh reused by the next round
+  return digit;
+}
+
 // NT2 threads per row: 512 for long rows, 128 for rows of up to kShortRow
 // keys, so that more rows (each a chain of barriers) run side by side.
+// Selection: an 11-bit round over the whole row (sign, exponent and three
+// mantissa bits of the scores) finds the bin holding the topk-th largest key;
+// that bin's keys are gathered into a short candidate list, and two more
+// rounds (11 and 10 bits) over the list give the exact threshold key.  A bin
+// too large for the list runs those rounds over the whole row instead.
 constexpr int kShortRow = 8192;
 template <int NT2>
-__global__ void __launch_bounds__(NT2) sa_indexer_topk_kernel(const IdxParams P) {
+constexpr int cand_cap() { return NT2 == 128 ? 1024 : 4096; }
+
+template <int NT2>
+__global__ void __launch_bounds__(NT2, 1) sa_indexer_topk_kernel(const IdxParams P) {
   extern __shared__ float staged[];
-  __shared__ int hist[256];
-  __shared__ uint32_t sel_digit;
+  __shared__ int hist[2048];
+  __shared__ uint32_t cand[cand_cap<NT2>()];
+  __shared__ int scratch[NT2 / 32];
+  __shared__ int sh[2];
+  __shared__ int cand_n;
   __shared__ int sel_rem;
   const int tid = threadIdx.x;
   const int64_t row = blockIdx.x;
@@ -487,9 +572,10 @@ __global__ void __launch_bounds__(NT2) sa_indexer_topk_kernel(const IdxParams P)
     } else {
       for (int64_t s = tid; s < L; s += NT2) staged[s] = srow[s];
     }
-    __syncthreads();
     srow = staged;
   }
+  if (tid == 0) cand_n = 0;
+  __syncthreads();
   int32_t* orow = P.out + tb * P.o_sb + tm * P.o_sm;
   const int64_t K = P.topk;
 
@@ -498,56 +584,36 @@ __global__ void __launch_bounds__(NT2) sa_indexer_topk_kernel(const IdxParams P)
   int take_eq = 0;
   const bool all = L <= K;  // every valid key is selected
   if (!all) {
-    uint32_t prefix = 0, pmask = 0;
-    int kk = static_cast<int>(K);  // rank still to find among keys matching prefix
-    for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int d = tid; d < 256; d += NT2) hist[d] = 0;
-      __syncthreads();
-      // coalesced pass (order does not matter here); warp-aggregated adds,
-      // since most keys share the leading digits
-      for (int64_t base = 0; base < L; base += NT2) {
-        const int64_t s = base + tid;
-        uint32_t d = 256;  // no bin
-        if (s < L) {
-          const uint32_t key = order_key(srow[s]);
-          if ((key & pmask) == prefix) d = (key >> shift) & 255;
-        }
-        const uint32_t peers = __match_any_sync(0xffffffffu, d);
-        if (d < 256 && (__ffs(peers) - 1) == (tid & 31)) atomicAdd(&hist[d], __popc(peers));
-      }
-      __syncthreads();
-      if (tid < 32) {  // scan the 256 bins from the top: bin holding rank kk
-        // lane l covers bins 255-8l .. 248-8l
-        int c = 0;
-        for (int e = 0; e < 8; ++e) c += hist[255 - 8 * tid - e];
-        int inc = c;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const int y = __shfl_up_sync(0xffffffffu, inc, off);
-          if (tid >= off) inc += y;
-        }
-        const int before = inc - c;
-        const bool mine = before < kk && kk <= inc;
-        if (mine) {
-          int acc = before;
-          for (int e = 0; e < 8; ++e) {
-            const int d = 255 - 8 * tid - e;
-            if (acc + hist[d] >= kk) {
-              sel_digit = static_cast<uint32_t>(d);
-              sel_rem = kk - acc;
-              break;
-            }
-            acc += hist[d];
-          }
-        }
-      }
-      __syncthreads();
-      prefix |= sel_digit << shift;
-      pmask |= 255u << shift;
-      kk = sel_rem;
-      __syncthreads();
+    const int n = static_cast<int>(L);
+    auto row_key = [&](int i) { return order_key(srow[i]); };
+    int kk = static_cast<int>(K);  // rank still to find among keys matching the prefix
+    const uint32_t b0 = radix_round<NT2, 11>(row_key, n, 0u, 0u, 21, kk, hist, scratch, sh);
+    const uint32_t p0 = b0 << 21, m0 = 0x7FFu << 21;
+    // gather the keys of bin b0 (order does not matter for the threshold)
+    for (int base = 0; base < n; base += NT2) {
+      const int i = base + tid;
+      const uint32_t key = i < n ? row_key(i) : 0u;
+      const bool in = i < n && (key & m0) == p0;
+      const uint32_t bal = __ballot_sync(0xffffffffu, in);
+      int at = 0;
+      if ((tid & 31) == 0 && bal != 0) at = atomicAdd(&cand_n, __popc(bal));
+      at = __shfl_sync(0xffffffffu, at, 0) + __popc(bal & ((1u << (tid & 31)) - 1u));
+      if (in && at < cand_cap<NT2>()) cand[at] = key;
     }
-    T = prefix;
+    __syncthreads();
+    const int nc = cand_n;
+    uint32_t b1, b2;
+    if (nc <= cand_cap<NT2>()) {
+      auto cand_key = [&](int i) { return cand[i]; };
+      b1 = radix_round<NT2, 11>(cand_key, nc, p0, m0, 10, kk, hist, scratch, sh);
+      b2 = radix_round<NT2, 10>(cand_key, nc, p0 | (b1 << 10), m0 | (0x7FFu << 10), 0, kk, hist,
+                                scratch, sh);
+    } else {
+      b1 = radix_round<NT2, 11>(row_key, n, p0, m0, 10, kk, hist, scratch, sh);
+      b2 = radix_round<NT2, 10>(row_key, n, p0 | (b1 << 10), m0 | (0x7FFu << 10), 0, kk, hist,
+                                scratch, sh);
+    }
+    T = p0 | (b1 << 10) | b2;
     take_eq = kk;  // keys equal to T to take, lowest indices first
   }
   // Ordered compaction.  Warp w owns the contiguous keys [w*C, (w+1)*C), read
