@@ -9,7 +9,12 @@
 //   comb = softmax_rows(mixes[8:24] * hc_scale[2] + hc_base[8:24]) + eps
 //   comb = comb / (column sums + eps)
 //   (iters - 1) times: comb = comb / (row sums + eps); comb = comb / (column sums + eps)
-// Every division divides each element (IEEE division), as the reference does.
+// The reference divides each element (torch fp32 division); here each row or
+// column sum is inverted once (IEEE round-to-nearest reciprocal) and the four
+// elements multiplied by it: a quarter of the divisions, within one extra
+// rounding per normalisation (the reference's tolerance is atol 1e-5,
+// rtol 1e-4; measured against the per-element-division oracle: < 3e-7
+// absolute, 1.5e-6 relative, on the 1k-1-64 prefill shape).
 //
 // Layout: one thread per token holds its 16 matrix entries in registers.  A
 // token's 24 inputs are six 16-byte loads (rows are 96 bytes, so a warp's
@@ -40,7 +45,8 @@ struct Params {
   float eps;
 };
 
-__device__ __forceinline__ float sigmoidf_ref(float x) { return 1.f / (1.f + expf(-x)); }
+// 1 / y by the correctly rounded reciprocal: the same value as the division
+__device__ __forceinline__ float sigmoidf_ref(float x) { return __frcp_rn(1.f + expf(-x)); }
 
 __global__ void __launch_bounds__(kThreads) hc_split_sinkhorn_kernel(const Params p) {
   const int64_t r = (int64_t)blockIdx.x * kThreads + threadIdx.x;
@@ -82,23 +88,24 @@ __global__ void __launch_bounds__(kThreads) hc_split_sinkhorn_kernel(const Param
       c[i][j] = expf(c[i][j] - mx);
       sum += c[i][j];
     }
+    const float r = __frcp_rn(sum);
 #pragma unroll
-    for (int j = 0; j < HC; ++j) c[i][j] = c[i][j] / sum + p.eps;
+    for (int j = 0; j < HC; ++j) c[i][j] = c[i][j] * r + p.eps;
   }
   auto col_norm = [&]() {
 #pragma unroll
     for (int j = 0; j < HC; ++j) {
-      const float d = ((c[0][j] + c[1][j]) + c[2][j]) + c[3][j] + p.eps;
+      const float r = __frcp_rn(((c[0][j] + c[1][j]) + c[2][j]) + c[3][j] + p.eps);
 #pragma unroll
-      for (int i = 0; i < HC; ++i) c[i][j] = c[i][j] / d;
+      for (int i = 0; i < HC; ++i) c[i][j] = c[i][j] * r;
     }
   };
   auto row_norm = [&]() {
 #pragma unroll
     for (int i = 0; i < HC; ++i) {
-      const float d = ((c[i][0] + c[i][1]) + c[i][2]) + c[i][3] + p.eps;
+      const float r = __frcp_rn(((c[i][0] + c[i][1]) + c[i][2]) + c[i][3] + p.eps);
 #pragma unroll
-      for (int j = 0; j < HC; ++j) c[i][j] = c[i][j] / d;
+      for (int j = 0; j < HC; ++j) c[i][j] = c[i][j] * r;
     }
   };
   col_norm();
