@@ -100,8 +100,8 @@ def sparse_attn_out(o, q, kv, attn_sink, topk_idxs, scale, workspace=None, *,
 
     No copies: q/kv/o need a unit last-dim stride and 16-byte aligned rows.
     ``workspace`` (uint8 CUDA tensor of at least :func:`workspace_bytes`,
-    zero-filled before its first use; every call leaves it zero-filled) is
-    taken from a per-(device, stream) cache when omitted.  ``variant``/``grid`` select the kernel
+    zero-filled before its first use; every call leaves its merge counters
+    zero) is taken from a per-(device, stream) cache when omitted.  ``variant``/``grid`` select the kernel
     variant and persistent grid size (0 = automatic).
     """
     b, m, h, d = q.shape
