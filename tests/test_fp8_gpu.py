@@ -206,3 +206,21 @@ def test_fp8_no_pipeline_timeouts():
     args, _ = load_golden_fp8("fp8_plumbing")
     run_fp8(*args)
     assert device_status() == 0
+
+
+def test_fp8_ticket_merge_with_a_short_workspace():
+    """A workspace without room for the per-row ints (a size from an older
+    formula) makes prefill-shaped grids merge split rows by ticket instead of
+    running the row schedule; both give the oracle's result."""
+    from sparse_attn import workspace_bytes
+    args, ref = load_golden_fp8("fp8_plumbing")
+    q, kv8, ks, sink, idx, scale = args
+    q, kv8, ks, sink, idx = _cuda(q, kv8, ks, sink, idx)
+    ws = torch.zeros(workspace_bytes(1, 64, 64, q.device), dtype=torch.uint8, device="cuda")
+    short = ws[:ws.numel() - (64 * 4 + 255) // 256 * 256]
+    for w in (short, ws, short):
+        for grid in (3, 5, 0):
+            o = torch.empty_like(q)
+            sparse_attn_fp8_out(o, q, kv8, ks, sink, idx, scale, w, grid=grid)
+            torch.cuda.synchronize()
+            assert_close(o, ref, what=f"fp8 grid {grid}, workspace {w.numel()} B")
