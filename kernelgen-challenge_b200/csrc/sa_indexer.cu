@@ -207,7 +207,6 @@ using namespace tc;
 constexpr int TKEYS = 128;         // keys per tile (M)
 constexpr int KSLAB = TKEYS * 128; // 16 KiB: 128 keys x 64 dims
 constexpr int KTILE = 2 * KSLAB;   // 32 KiB
-constexpr int NTX = 256;
 
 template <int R>
 struct Cfg {
@@ -215,6 +214,10 @@ struct Cfg {
   static constexpr int QSLAB = R * IH * 128;     // R rows x 64 heads x 64 dims
   static constexpr int QTILE = 2 * QSLAB;
   static constexpr uint32_t kTmemCols = 128 * R; // two accumulators of 64R columns
+  // epilogue warps: four (one per TMEM lane quarter) for R = 1; eight for
+  // R = 4, the second four taking the odd rows of each group
+  static constexpr int NE = R == 1 ? 4 : 8;
+  static constexpr int NTX = 128 + 32 * NE;
 };
 
 template <int R>
@@ -283,7 +286,7 @@ struct Walk {
 };
 
 template <int R>
-__global__ void __launch_bounds__(NTX, 1)
+__global__ void __launch_bounds__(Cfg<R>::NTX, 1)
     sa_indexer_score_tc_kernel(const IdxParams P, const __grid_constant__ CUtensorMap k_map,
                                const __grid_constant__ CUtensorMap q_map,
                                const __grid_constant__ CUtensorMap w_map) {
@@ -307,11 +310,11 @@ __global__ void __launch_bounds__(NTX, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&S.q_full[b]), 1);
-      // freed by the MMA commit after a group's last tile and by the four
+      // freed by the MMA commit after a group's last tile and by the
       // epilogue warps (they read the group's weights from the buffer)
-      mbar_init(smem_u32(&S.q_empty[b]), 1 + 4);
+      mbar_init(smem_u32(&S.q_empty[b]), 1 + C::NE);
       mbar_init(smem_u32(&S.acc_full[b]), 1);
-      mbar_init(smem_u32(&S.acc_empty[b]), 4);
+      mbar_init(smem_u32(&S.acc_empty[b]), C::NE);
     }
     mbar_init(smem_u32(&S.done), 1);
     S.err = 0;
@@ -397,7 +400,8 @@ __global__ void __launch_bounds__(NTX, 1)
     __syncwarp();
   } else if (warp >= 4) {
     // --------------------------------------------------------------- epilogue
-    const int qd = warp - 4;
+    constexpr int RSTEP = C::NE / 4;  // rows per group step of one warp
+    const int qd = (warp - 4) & 3, half = (warp - 4) >> 2;
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * qd) << 16);
     Walk<R> w{};
     for (int i = 0; i < n; ++i) {
@@ -411,10 +415,14 @@ __global__ void __launch_bounds__(NTX, 1)
       const int64_t key = w.tile * TKEYS + 32 * qd + lane;
       const bool active = ok && w.tile * TKEYS < w.Lmax;
 #pragma unroll
-      for (int k = 0; k < R; ++k) {
+      for (int kk = 0; kk < R; kk += RSTEP) {
+        // row k = kk + half (RSTEP = 2) or kk (RSTEP = 1); the length limit is
+        // picked without indexing L by a run-time value
+        const int k = kk + (RSTEP == 2 ? half : 0);
+        const int64_t Lk = (RSTEP == 2 && half) ? w.L[(kk + 1) % R] : w.L[kk];
         if (w.m0 + k >= P.m) break;
         float score = -INFINITY;
-        if (active && w.tile * TKEYS < w.L[k]) {
+        if (active && w.tile * TKEYS < Lk) {
           float v[4][16];  // the row's 64 head scores of this key, one wait
 #pragma unroll
           for (int c = 0; c < IH / 16; ++c)
@@ -427,7 +435,7 @@ __global__ void __launch_bounds__(NTX, 1)
 #pragma unroll
             for (int e = 0; e < 16; ++e)
               acc[c] = fmaf(wt[16 * c + e], fmaxf(v[c][e], 0.f), acc[c]);
-          if (key < w.L[k]) score = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+          if (key < Lk) score = (acc[0] + acc[1]) + (acc[2] + acc[3]);
         }
         const int64_t row = w.tb * P.m + w.m0 + k;
         if (key < P.kv_len) P.score[row * P.kv_len + key] = score;
@@ -760,7 +768,8 @@ cudaError_t launch_score_tc(const idx_path::IdxParams& P, const int64_t q_stride
   if (e != cudaSuccess) return e;
   const int64_t items = P.b * ((P.m + R - 1) / R) * ((P.kv_len + TKEYS - 1) / TKEYS);
   const int64_t grid = items < sms ? items : sms;
-  kern<<<static_cast<unsigned>(grid), NTX, smem, st>>>(P, k_map, q_map, w_map);
+  kern<<<static_cast<unsigned>(grid), R == 1 ? Cfg<1>::NTX : Cfg<4>::NTX, smem, st>>>(
+      P, k_map, q_map, w_map);
   return cudaGetLastError();
 }
 
