@@ -459,10 +459,11 @@ static int fwd_impl(const void* q, const void* kv, const float* sink, const int3
                     void* workspace, size_t workspace_bytes, void* stream, int variant,
                     int grid_ctas, float* lse) {
   const int64_t groups = head_groups(h);
+  // (null pointers with several groups: the first group's checks report them)
   if (groups == 1 || !q || !o || !sink || !q_strides || !o_strides)
-    return fwd_group(q, kv, sink, idx, o, b, m, h, d, kv_len, topk, q_strides, kv_strides,
-                     idx_strides, o_strides, scale, workspace, workspace_bytes, stream, variant,
-                     grid_ctas, lse, h);
+    return fwd_group(q, kv, sink, idx, o, b, m, groups == 1 ? h : sa::kHeads, d, kv_len, topk,
+                     q_strides, kv_strides, idx_strides, o_strides, scale, workspace,
+                     workspace_bytes, stream, variant, grid_ctas, lse, h);
   for (int64_t g = 0; g < groups; ++g) {
     const int rc = fwd_group(
         head_group_ptr(q, g, q_strides[2]), kv, sink + g * sa::kHeads, idx,
@@ -482,9 +483,9 @@ int sa_fwd_fp8(const void* q, const void* kv8, const float* kv_scale, const floa
                void* workspace, size_t workspace_bytes, void* stream, int grid_ctas) {
   const int64_t groups = head_groups(h);
   if (groups == 1 || !q || !o || !sink || !q_strides || !o_strides)
-    return fp8_group(q, kv8, kv_scale, sink, idx, o, b, m, h, d, kv_len, topk, q_strides,
-                     kv_strides, kv_scale_strides, idx_strides, o_strides, scale, workspace,
-                     workspace_bytes, stream, grid_ctas);
+    return fp8_group(q, kv8, kv_scale, sink, idx, o, b, m, groups == 1 ? h : sa::kHeads, d,
+                     kv_len, topk, q_strides, kv_strides, kv_scale_strides, idx_strides,
+                     o_strides, scale, workspace, workspace_bytes, stream, grid_ctas);
   for (int64_t g = 0; g < groups; ++g) {
     const int rc = fp8_group(
         head_group_ptr(q, g, q_strides[2]), kv8, kv_scale, sink + g * sa::kHeads, idx,
@@ -503,8 +504,9 @@ int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx,
            const int64_t o_strides[4], const int64_t dkv_strides[3], float scale, void* stream) {
   const int64_t groups = head_groups(h);
   if (groups == 1 || !q || !o || !dout || !dq || !sink || !dsink || !q_strides || !o_strides)
-    return bwd_group(q, kv, sink, idx, o, dout, lse, h, dq, dkv, dsink, b, m, h, d, kv_len, topk,
-                     q_strides, kv_strides, idx_strides, o_strides, dkv_strides, scale, stream);
+    return bwd_group(q, kv, sink, idx, o, dout, lse, h, dq, dkv, dsink, b, m,
+                     groups == 1 ? h : sa::kHeads, d, kv_len, topk, q_strides, kv_strides,
+                     idx_strides, o_strides, dkv_strides, scale, stream);
   for (int64_t g = 0; g < groups; ++g) {
     const int64_t k = g * sa::kHeads;
     const int rc = bwd_group(

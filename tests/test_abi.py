@@ -93,6 +93,9 @@ def test_fp8_entries_validate_before_any_gpu_work():
     assert fwd8(b=0) == _lib.SA_OK
     assert fwd8(b=-1) == _lib.SA_ERR_INVALID_ARG
     assert fwd8(h=8) == _lib.SA_ERR_UNSUPPORTED
+    assert fwd8(h=40) == _lib.SA_ERR_UNSUPPORTED                   # more heads: multiples of 16
+    assert fwd8(h=32, b=0) == _lib.SA_OK
+    assert fwd8(h=32, kv8=8) == _lib.SA_ERR_INVALID_ARG
     assert fwd8(ks=0) == _lib.SA_ERR_INVALID_ARG
     assert fwd8(kv8=8) == _lib.SA_ERR_INVALID_ARG                  # misaligned rows
     assert fwd8(kv_strides=(2048, 520, 1)) == _lib.SA_ERR_INVALID_ARG  # row stride not 16 B
@@ -114,6 +117,10 @@ def test_backward_entry_validates_before_any_gpu_work():
                         _i64(2048, 512, 1), _i64(4, 4, 1), st, _i64(*dkv_strides), 1.0, None)
     assert bwd(b=0) == _lib.SA_OK
     assert bwd(h=4) == _lib.SA_ERR_UNSUPPORTED
+    assert bwd(h=24) == _lib.SA_ERR_UNSUPPORTED
+    assert bwd(h=48, b=0) == _lib.SA_OK
+    assert bwd(h=48, dq=0) == _lib.SA_ERR_INVALID_ARG
+    assert bwd(h=48, dkv=4) == _lib.SA_ERR_INVALID_ARG
     assert bwd(dq=0) == _lib.SA_ERR_INVALID_ARG
     assert bwd(dkv=4) == _lib.SA_ERR_INVALID_ARG                   # misaligned fp32 buffer
     assert bwd(dkv_strides=(2048, 511, 1)) == _lib.SA_ERR_INVALID_ARG
