@@ -135,3 +135,13 @@ def test_unaligned_weight_rows_use_the_warp_mma_scorer():
     _check(q, k, w, ln, 50, "unaligned weights (reference run)")
     ref = indexer_scores_oracle(q, k, w, ln)
     assert bool(((sc.cpu() - ref).abs() <= 1e-4 * ref.abs().max() + 1e-6).all())
+
+
+@pytest.mark.parametrize("m", [1, 3])
+def test_negative_weights_and_tied_scores(m):
+    """Signed weights give negative scores (order keys below the sign bit);
+    repeated k rows give exactly tied scores, taken lowest index first."""
+    q, k, w, ln = _inputs(2, m, 3000, seed=30 + m)
+    w = w * 20 - 1.0                       # about half the weights negative
+    k[:, 1000:1500] = k[:, 0:1].expand(-1, 500, -1)   # 501 keys with one score
+    _check(q, k, w, ln, 700, f"signed weights, ties m={m}")
