@@ -156,6 +156,34 @@ int sa_device_status(int* flags);
  * and leaves other indices undefined. */
 int sa_index_faults(uint64_t* count, int reset);
 
+/* Zeroes the error words that sa_device_status reads, on the current device
+ * (synchronous).  A caller that saw a nonzero status and dealt with it calls
+ * this before its next health check.  No counterpart in the reference. */
+int sa_device_status_reset(void);
+
+/* Process-wide options for tests and comparisons; the defaults are what the
+ * library is tuned for and a caller never needs to change them.
+ *   SA_OPT_ROW_SCHEDULE  1 (default): prefill shapes run whole rows (row
+ *                        schedule); 0: contiguous unit ranges for every shape.
+ *   SA_OPT_INDEXER_TC    1 (default): sa_indexer_topk scores on tcgen05;
+ *                        0: the warp-MMA scorer.
+ *   SA_OPT_SPIN_LIMIT    polls before a pipeline wait of the sa_fwd and
+ *                        sa_fwd_fp8 kernels gives up (0 = the default, 2^22).
+ *   SA_OPT_TEST_STALL    1: the next launches of those kernels withhold one
+ *                        arrival on the first ring slot, so a consumer wait
+ *                        runs out (with a small SA_OPT_SPIN_LIMIT, quickly);
+ *                        the kernel then records its error code, issues no
+ *                        more copies, waits for those in flight and returns.
+ *                        For testing the failure path; 0 (default) = off.
+ * Options are read when a call is made; returns SA_ERR_INVALID_ARG for an
+ * unknown option or value.  No counterpart in the reference. */
+#define SA_OPT_ROW_SCHEDULE 1
+#define SA_OPT_INDEXER_TC 2
+#define SA_OPT_SPIN_LIMIT 3
+#define SA_OPT_TEST_STALL 4
+int sa_set_option(int option, int64_t value);
+int64_t sa_get_option(int option);
+
 /* Last cudaError_t observed by this thread inside the library (0 if none). */
 int sa_last_cuda_error(void);
 

@@ -6,7 +6,7 @@
 // an exception), and the kernel launch (:1006-1021).  The reference's
 // five-backend detection and try/except fallback tiers (:919-969,
 // :1026-1271) have no counterpart: there is one target, sm_100a.
-#include <cstdlib>
+#include <atomic>
 #include <mutex>
 
 #include "sparse_attn.h"
@@ -91,19 +91,72 @@ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // Upper bound on the persistent grid of any variant on a device with `sms` SMs.
 int max_grid(int sms) { return 2 * sms; }
 
-// SA_ROW_SCHEDULE=0 in the environment keeps the contiguous unit ranges for
-// every shape (for comparisons); read once per process.
-bool row_schedule_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("SA_ROW_SCHEDULE");
-    return !(v != nullptr && v[0] == '0');
-  }();
-  return on;
-}
+std::atomic<int> g_opt_row_schedule{1};
+std::atomic<int> g_opt_indexer_tc{1};
+std::atomic<uint32_t> g_opt_spin{0};
+std::atomic<int> g_opt_test_stall{0};
 
 }  // namespace
 
+namespace sa {
+bool opt_row_schedule() { return g_opt_row_schedule.load(std::memory_order_relaxed) != 0; }
+bool opt_indexer_tc() { return g_opt_indexer_tc.load(std::memory_order_relaxed) != 0; }
+uint32_t opt_spin_limit() { return g_opt_spin.load(std::memory_order_relaxed); }
+int opt_test_stall() { return g_opt_test_stall.load(std::memory_order_relaxed); }
+int reset_ws_error();
+int reset_tc_error();
+int reset_fp8_error();
+int reset_indexer_error();
+}  // namespace sa
+
 extern "C" {
+
+int sa_set_option(int option, int64_t value) {
+  switch (option) {
+    case SA_OPT_ROW_SCHEDULE:
+      if (value != 0 && value != 1) return SA_ERR_INVALID_ARG;
+      g_opt_row_schedule.store(static_cast<int>(value));
+      return SA_OK;
+    case SA_OPT_INDEXER_TC:
+      if (value != 0 && value != 1) return SA_ERR_INVALID_ARG;
+      g_opt_indexer_tc.store(static_cast<int>(value));
+      return SA_OK;
+    case SA_OPT_SPIN_LIMIT:
+      if (value < 0 || value > UINT32_MAX) return SA_ERR_INVALID_ARG;
+      g_opt_spin.store(static_cast<uint32_t>(value));
+      return SA_OK;
+    case SA_OPT_TEST_STALL:
+      if (value != 0 && value != 1) return SA_ERR_INVALID_ARG;
+      g_opt_test_stall.store(static_cast<int>(value));
+      return SA_OK;
+    default:
+      return SA_ERR_INVALID_ARG;
+  }
+}
+
+int64_t sa_get_option(int option) {
+  switch (option) {
+    case SA_OPT_ROW_SCHEDULE:
+      return g_opt_row_schedule.load();
+    case SA_OPT_INDEXER_TC:
+      return g_opt_indexer_tc.load();
+    case SA_OPT_SPIN_LIMIT:
+      return g_opt_spin.load();
+    case SA_OPT_TEST_STALL:
+      return g_opt_test_stall.load();
+    default:
+      return -1;
+  }
+}
+
+int sa_device_status_reset(void) {
+  int e = sa::reset_tc_error();
+  if (e == 0) e = sa::reset_ws_error();
+  if (e == 0) e = sa::reset_fp8_error();
+  if (e == 0) e = sa::reset_indexer_error();
+  if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
+  return SA_OK;
+}
 
 int sa_version(void) { return 10000; }
 
@@ -118,7 +171,7 @@ const char* sa_strerror(int code) {
     case SA_ERR_CUDA:
       return "CUDA runtime error (see sa_last_cuda_error)";
     case SA_ERR_UNSUPPORTED:
-      return "unsupported configuration (needs h == 16, d == 512 and an sm_100 device)";
+      return "unsupported configuration (needs h a multiple of 16, d == 512 and an sm_100 device)";
     default:
       return "unknown sparse_attn status code";
   }
@@ -232,6 +285,8 @@ static int fwd_group(const void* q, const void* kv, const float* sink, const int
   p.o_sm = o_strides[1];
   p.o_sh = o_strides[2];
   p.scale_log2 = scale * sa::kLog2e;
+  p.spin = sa::opt_spin_limit();
+  p.test_stall = sa::opt_test_stall();
 
   // variant: the tensor-core path whenever its TMA maps can describe the
   // inputs, the warp-MMA path otherwise
@@ -281,7 +336,7 @@ static int fwd_group(const void* q, const void* kv, const float* sink, const int
   // With that many rows and room in the workspace for one int per row, the
   // ws kernel runs whole rows instead (no split rows), each only up to its
   // last valid slot (sa_ws.cu: row schedule).
-  if (p.merge_in_kernel && row_schedule_enabled() &&
+  if (p.merge_in_kernel && sa::opt_row_schedule() &&
       workspace_bytes >= need + sa::row_units_bytes(b * m)) {
     p.merge_in_kernel = 0;
     p.row_units = reinterpret_cast<const int*>(ws + need);
@@ -352,6 +407,8 @@ static int fp8_group(const void* q, const void* kv8, const float* kv_scale, cons
   p.o_sm = o_strides[1];
   p.o_sh = o_strides[2];
   p.scale_log2 = scale * sa::kLog2e;
+  p.spin = sa::opt_spin_limit();
+  p.test_stall = sa::opt_test_stall();
   if (!sa::tc_supports(p)) return SA_ERR_UNSUPPORTED;
   p.upt = ceil_div(topk > 0 ? topk : 1, sa::fp8_unit_keys());
   p.units = b * m * p.upt;
@@ -368,7 +425,7 @@ static int fp8_group(const void* q, const void* kv8, const float* kv_scale, cons
   p.part_acc = reinterpret_cast<float*>(ws + sa::kTicketBytes);
   p.part_ml = reinterpret_cast<float*>(ws + sa::kTicketBytes + sa::ws_acc_bytes(p.grid));
   p.merge_in_kernel = p.units >= 2 * p.upt * p.grid ? 1 : 0;  // as for SA_VARIANT_WS
-  if (p.merge_in_kernel && row_schedule_enabled() &&
+  if (p.merge_in_kernel && sa::opt_row_schedule() &&
       workspace_bytes >= need + sa::row_units_bytes(b * m)) {  // as in fwd_group
     p.merge_in_kernel = 0;
     p.row_units = reinterpret_cast<const int*>(ws + need);

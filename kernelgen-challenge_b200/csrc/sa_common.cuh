@@ -70,7 +70,18 @@ struct Params {
   // sa_row_units_kernel; set, each CTA runs whole rows of a fixed snake
   // order instead of a contiguous unit range (sa_ws.cu).
   const int* row_units;
+  // Polls before a pipeline wait gives up (sa_set_option(SA_OPT_SPIN_LIMIT));
+  // test_stall != 0 withholds one arrival on the first ring slot so that a
+  // wait runs out (the failure-path test, SA_OPT_TEST_STALL).
+  uint32_t spin;
+  int test_stall;
 };
+
+// Process-wide options (sa_set_option, sa_abi.cu).
+bool opt_row_schedule();
+bool opt_indexer_tc();
+uint32_t opt_spin_limit();
+int opt_test_stall();
 
 // log2 of the full denominator for a running max m and sum l (relative to m),
 // with the sink as the extra logit; all in the log2 domain.

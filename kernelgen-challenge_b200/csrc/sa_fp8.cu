@@ -89,6 +89,7 @@ struct __align__(1024) Smem {
   // empty: the four consumer warps finished the unit; q_full: next row's Q
   uint64_t full[NSLOT], empty[NSLOT], q_full;
   int err;
+  uint32_t spin;  // polls before a wait gives up
   // split rows this CTA merges after its last unit (at most its first and last row)
   int n_merge;
   int64_t merge_row[2];
@@ -105,7 +106,7 @@ __device__ __forceinline__ void set_err(Smem& S, int code) {
 __device__ __forceinline__ bool wait_or_err(Smem& S, uint64_t& bar, uint32_t parity, int code) {
   const uint32_t b = smem_u32(&bar);
   if (*reinterpret_cast<volatile int*>(&S.err) != 0) return false;
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  for (uint32_t i = 0; i < S.spin; ++i) {
     if (mbar_try_wait(b, parity)) return true;
     if ((i & 1023u) == 1023u && *reinterpret_cast<volatile int*>(&S.err) != 0) return false;
   }
@@ -234,6 +235,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     mbar_init(smem_u32(&S.q_full), 1);
     S.err = 0;
+    S.spin = p.spin != 0u ? p.spin : kSpinLimit;
     S.n_merge = 0;
     S.n_units = 0;
     fence_mbar_init();
@@ -345,7 +347,9 @@ __global__ void __launch_bounds__(NT, 1)
         __syncwarp();
         // release: the slot's full barrier also counts this arrival, made
         // after every lane's scale and mask writes
-        if (lane == 0) mbar_arrive(smem_u32(&S.full[slot]));
+        // (failure-path test: the first slot's release is withheld, so the
+        // consumers' wait on it runs out)
+        if (lane == 0 && !(p.test_stall && i == 0)) mbar_arrive(smem_u32(&S.full[slot]));
       }
     }
     cp_async_wait<0>();
@@ -362,7 +366,12 @@ __global__ void __launch_bounds__(NT, 1)
     float R = 0.f, invR = 0.f;       // running max of the token scales seen
     float o[16][4];  // O / R; n-tile 4G+j: heads g8, g8+8, columns 128c+32G+8q4+{j, 4+j}
     float lacc[4];   // running row sums: [0] head g8, [2] head g8+8
+    // Q loads issued by consumer thread 0; after an error none is issued, and
+    // the one possibly in flight is waited for before the CTA exits.
+    int q_issued = 0;
     auto issue_q = [&](int64_t row) {
+      if (*reinterpret_cast<volatile int*>(&S.err) != 0) return;
+      ++q_issued;
       const int64_t qb = row / p.m, qm = row - qb * p.m;
       fence_proxy_async_smem();  // the Q reads above precede the TMA refill
       mbar_arrive_expect_tx(smem_u32(&S.q_full), Q_BYTES);
@@ -685,6 +694,13 @@ __global__ void __launch_bounds__(NT, 1)
         }
       }
     }
+    // After an error the last Q load issued may still be in flight: wait for
+    // it (its phase is the only one not yet seen) before the CTA exits.
+    if (tt == 0 && q_issued > 0 && *reinterpret_cast<volatile int*>(&S.err) != 0) {
+      const uint32_t qb = smem_u32(&S.q_full);
+      for (uint32_t k = 0; k < kSpinLimit && !mbar_try_wait(qb, (q_issued - 1) & 1); ++k) {
+      }
+    }
   }
   // ---- every thread merges the split rows whose last part this CTA stored
   __syncthreads();
@@ -775,6 +791,11 @@ int read_fp8_error(int* flags) {
   if (e != cudaSuccess) return (int)e;
   *flags = v;
   return 0;
+}
+
+int reset_fp8_error() {
+  const int zero = 0;
+  return (int)cudaMemcpyToSymbol(sa_fp8_error, &zero, sizeof(int));
 }
 
 int read_fp8_index_faults(unsigned long long* out, bool reset) {

@@ -699,16 +699,6 @@ __global__ void __launch_bounds__(NT2, 1) sa_indexer_topk_kernel(const IdxParams
 
 namespace {
 
-// SA_INDEXER_MMA=1 in the environment selects the warp-MMA scorer (for
-// comparisons); read once per process.
-bool indexer_tc_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("SA_INDEXER_MMA");
-    return !(v != nullptr && v[0] == '1');
-  }();
-  return on;
-}
-
 cudaError_t launch_score_tc(const idx_path::IdxParams& P, const int64_t q_strides[4],
                             const int64_t k_strides[3], const int64_t w_strides[3],
                             cudaStream_t st) {
@@ -783,6 +773,11 @@ int read_indexer_error(int* flags) {
   return 0;
 }
 
+int reset_indexer_error() {
+  const int zero = 0;
+  return (int)cudaMemcpyToSymbol(sa_idx_error, &zero, sizeof(int));
+}
+
 cudaError_t launch_indexer(const __nv_bfloat16* q, const __nv_bfloat16* k, const float* w,
                            const int32_t* len, int32_t* out, float* score, int64_t b, int64_t m,
                            int64_t kv_len, int64_t topk, const int64_t q_strides[4],
@@ -816,7 +811,7 @@ cudaError_t launch_indexer(const __nv_bfloat16* q, const __nv_bfloat16* k, const
     // checked by the caller); otherwise the warp-MMA scorer runs
     const bool w_ok = (reinterpret_cast<uintptr_t>(w) & 15u) == 0 && w_strides[0] % 4 == 0 &&
                       w_strides[1] % 4 == 0;
-    if (indexer_tc_enabled() && w_ok) {
+    if (sa::opt_indexer_tc() && w_ok) {
       e = launch_score_tc(P, q_strides, k_strides, w_strides, st);
     } else {
       sa_indexer_score_kernel<<<dim3(static_cast<unsigned>(rows), static_cast<unsigned>(spans)),

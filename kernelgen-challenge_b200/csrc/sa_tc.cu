@@ -50,31 +50,6 @@ namespace sa {
 __device__ int sa_tc_error;  // nonzero after a bounded wait gave up
 __device__ unsigned long long sa_tc_index_faults;  // out-of-range indices seen
 
-#ifdef SA_TRACE
-// Pipeline timeline for development builds only (-DSA_TRACE): per CTA (first
-// kTraceCtas), per unit (first kTraceUnits), per event, %globaltimer in ns.
-constexpr int kTraceCtas = 160, kTraceUnits = 16, kTraceEvents = 8;
-__device__ unsigned long long sa_trace[kTraceCtas][kTraceUnits][kTraceEvents];
-__device__ __forceinline__ void trace_ev(int64_t cta, int unit, int ev) {
-  if (cta < kTraceCtas && unit < kTraceUnits) {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    sa_trace[cta][unit][ev] = t;
-  }
-}
-#define SA_TRACE_EV(u, e) trace_ev(blockIdx.x, (u), (e))
-__device__ unsigned long long sa_trace_cta[1024][8];  // start, end, epilogue stages
-
-__device__ __forceinline__ void trace_cta(int e) {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  if (blockIdx.x < 1024) sa_trace_cta[blockIdx.x][e] = t;
-}
-#define SA_TRACE_CTA(e) trace_cta(e)
-#else
-#define SA_TRACE_EV(u, e) ((void)0)
-#define SA_TRACE_CTA(e) ((void)0)
-#endif
 
 namespace tc_path {
 using namespace tc;
@@ -143,7 +118,6 @@ __global__ void __launch_bounds__(NT, 1)
   const int64_t t_first = u0 / upt;
   const int64_t t_last = (u1 - 1) / upt;
   const int64_t kb_first = u0 - t_first * upt;
-  if (tid == 0) SA_TRACE_CTA(0);
   // let the combine kernel of split rows launch now; it waits for this grid
   // to complete before reading any partial (griddepcontrol.wait)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -206,7 +180,6 @@ __global__ void __launch_bounds__(NT, 1)
       const int slot = i % NSLOT;
       const bool ok = i < NSLOT || wait_or_err(S, S.empty[slot], ((i / NSLOT) - 1) & 1, 1);
       if (!__all_sync(0xffffffffu, ok)) continue;
-      if (tid == 0) SA_TRACE_EV(i, 0);
       if (warp == 0) {
         const uint32_t ma = __ballot_sync(0xffffffffu, ia >= 0 && (int64_t)ia < p.kv_len);
         const uint32_t mb = __ballot_sync(0xffffffffu, ib >= 0 && (int64_t)ib < p.kv_len);
@@ -254,7 +227,6 @@ __global__ void __launch_bounds__(NT, 1)
         // TMEM buffer i&1 was last read by the softmax of unit i-2
         ok = ok && (i < 2 || wait_or_err(S, S.s_free[i & 1], ((i - 2) >> 1) & 1, 5));
         if (ok) {
-          SA_TRACE_EV(i, 1);
           fence_proxy_async_smem();  // cp.async (generic proxy) writes -> MMA reads
           tc_fence_after();
           const uint32_t slot_base = smem_u32(S.ring[slot]);
@@ -276,7 +248,6 @@ __global__ void __launch_bounds__(NT, 1)
               }
           mma_commit(smem_u32(&S.s_full[i & 1]));
           if (seg_end) mma_commit(smem_u32(&S.q_empty));
-          SA_TRACE_EV(i, 2);
         }
         seg_first = seg_end;
         if (seg_end) ++seg;
@@ -325,7 +296,6 @@ __global__ void __launch_bounds__(NT, 1)
       const int slot = i % NSLOT;
       wait_or_err(S, S.full[slot], (i / NSLOT) & 1, 7);
       wait_or_err(S, S.s_full[i & 1], (i >> 1) & 1, 8);
-      if (qd == 0 && lane == 0) SA_TRACE_EV(i, 3);
       tc_fence_after();
       float x[kHeads];
       {
@@ -412,7 +382,6 @@ __global__ void __launch_bounds__(NT, 1)
         *reinterpret_cast<uint4*>(S.p + p_off(key, 1)) = hi;
       }
       named_bar(3, 128);  // P^T of all 64 keys written
-      if (qd == 0 && lane == 0) SA_TRACE_EV(i, 4);
 
       // O[16 x 128 cols of this warp] += P[16 x 64] . V[64 x 128]
       const uint32_t slot_base = smem_u32(S.ring[slot]);
@@ -438,19 +407,9 @@ __global__ void __launch_bounds__(NT, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&S.empty[slot]));  // slot free for the producer
-#ifdef SA_TRACE
-      {  // development builds: wait for the P.V results before stamping
-        float dep = 0.f;
-#pragma unroll
-        for (int nt = 0; nt < 16; ++nt) dep += o[nt][0] + o[nt][3];
-        if (dep == 1.2345e-30f) sa_trace[0][0][0] = 1;
-      }
-#endif
-      if (qd == 0 && lane == 0) SA_TRACE_EV(i, 5);
 
       if (seg_end) {
         // ---------------- epilogue of the segment ending at unit i ----------
-        if (qd == 0 && lane == 0) SA_TRACE_EV(i, 6);
         float m_lo = 0.f, m_hi = 0.f;
 #pragma unroll
         for (int h = 0; h < kHeads; ++h) {
@@ -472,7 +431,6 @@ __global__ void __launch_bounds__(NT, 1)
                 pack_bf16x2(o[nt][2] * f_hi, o[nt][3] * f_hi);
           }
         } else {
-          if (tid == 128) SA_TRACE_CTA(2);
           const int64_t pslot = 2 * g + (t == t_first ? 0 : 1);
           float* pacc = p.part_acc + pslot * kPartAccFloats;
 #pragma unroll
@@ -489,7 +447,6 @@ __global__ void __launch_bounds__(NT, 1)
             p.part_ml[pslot * kPartMlFloats + kHeads + g8 + 8] = l_hi;
           }
         }
-        if (qd == 0 && lane == 0) SA_TRACE_EV(i, 7);
       }
       seg_first = seg_end;
       if (++kb == upt) {
@@ -506,7 +463,6 @@ __global__ void __launch_bounds__(NT, 1)
     tc_fence_after();
     tmem_dealloc<kTmemCols>(tmem);
   }
-  if (tid == 0) SA_TRACE_CTA(1);
 }
 
 }  // namespace tc_path
@@ -600,20 +556,6 @@ cudaError_t launch_tc(const Params& p, cudaStream_t st) {
   return launch_combine(p, st);
 }
 
-#ifdef SA_TRACE
-extern "C" int sa_trace_read(unsigned long long* out, size_t bytes) {
-  if (bytes < sizeof(sa_trace)) return -1;
-  return (int)cudaMemcpyFromSymbol(out, sa_trace, sizeof(sa_trace));
-}
-extern "C" int sa_trace_cta_read(unsigned long long* out, size_t bytes) {
-  if (bytes < sizeof(sa_trace_cta)) return -1;
-  return (int)cudaMemcpyFromSymbol(out, sa_trace_cta, sizeof(sa_trace_cta));
-}
-extern "C" int sa_trace_clear() {
-  static unsigned long long zero[kTraceCtas * kTraceUnits * kTraceEvents] = {};
-  return (int)cudaMemcpyToSymbol(sa_trace, zero, sizeof(zero));
-}
-#endif
 
 int read_tc_index_faults(unsigned long long* out, bool reset) {
   return index_fault_io(sa_tc_index_faults, out, reset);
@@ -625,6 +567,11 @@ int read_tc_error(int* flags) {
   if (e != cudaSuccess) return (int)e;
   *flags = v;
   return 0;
+}
+
+int reset_tc_error() {
+  const int zero = 0;
+  return (int)cudaMemcpyToSymbol(sa_tc_error, &zero, sizeof(int));
 }
 
 }  // namespace sa

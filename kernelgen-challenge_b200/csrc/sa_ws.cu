@@ -45,22 +45,6 @@ namespace sa {
 __device__ int sa_ws_error;  // nonzero after a bounded wait gave up
 __device__ unsigned long long sa_ws_index_faults;  // out-of-range indices seen
 
-#ifdef SA_TRACE
-// Pipeline timeline for development builds only (-DSA_TRACE): per CTA, per
-// unit (first kTraceUnits), per event, %globaltimer in ns.
-constexpr int kTraceCtas = 160, kTraceUnits = 16, kTraceEvents = 8;
-__device__ unsigned long long sa_ws_trace[kTraceCtas][kTraceUnits][kTraceEvents];
-__device__ __forceinline__ void ws_trace_ev(int unit, int ev) {
-  if (blockIdx.x < kTraceCtas && unit < kTraceUnits) {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    sa_ws_trace[blockIdx.x][unit][ev] = t;
-  }
-}
-#define SA_TRACE_EV(u, e) ws_trace_ev((u), (e))
-#else
-#define SA_TRACE_EV(u, e) ((void)0)
-#endif
 
 namespace ws_path {
 using namespace tc;
@@ -86,6 +70,7 @@ struct __align__(1024) Smem {
   // consumer warps finished the unit; q_full: the Q tile of the next row
   uint64_t full[NSLOT], empty[NSLOT], q_full;
   int err;
+  uint32_t spin;  // polls before a wait gives up
   // split rows this CTA merges after its last unit (at most its first and last row)
   int n_merge;
   int64_t merge_row[2];
@@ -103,7 +88,7 @@ __device__ __forceinline__ void set_err(Smem& S, int code) {
 __device__ __forceinline__ bool wait_or_err(Smem& S, uint64_t& bar, uint32_t parity, int code) {
   const uint32_t b = smem_u32(&bar);
   if (*reinterpret_cast<volatile int*>(&S.err) != 0) return false;
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  for (uint32_t i = 0; i < S.spin; ++i) {
     if (mbar_try_wait(b, parity)) return true;
     if ((i & 1023u) == 1023u && *reinterpret_cast<volatile int*>(&S.err) != 0) return false;
   }
@@ -202,6 +187,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     mbar_init(smem_u32(&S.q_full), 1);
     S.err = 0;
+    S.spin = p.spin != 0u ? p.spin : kSpinLimit;
     S.n_merge = 0;
     S.n_units = 0;
     fence_mbar_init();
@@ -277,7 +263,6 @@ __global__ void __launch_bounds__(NT, 1)
       const int slot = i % NSLOT;
       const bool ok = i < NSLOT || wait_or_err(S, S.empty[slot], ((i / NSLOT) - 1) & 1, 1);
       if (!__all_sync(0xffffffffu, ok)) continue;
-      if (tid == 0) SA_TRACE_EV(i, 0);
       if (warp == 0) {
         const uint32_t ma = __ballot_sync(0xffffffffu, ia >= 0 && (int64_t)ia < p.kv_len);
         const uint32_t mb = __ballot_sync(0xffffffffu, ib >= 0 && (int64_t)ib < p.kv_len);
@@ -303,7 +288,9 @@ __global__ void __launch_bounds__(NT, 1)
       // the slot's full barrier counts 128 hardware arrivals (one per thread,
       // when its copies land) plus the mask writer's release arrival
       cp_async_mbar_arrive_noinc(smem_u32(&S.full[slot]));
-      if (warp == 0 && lane == 0) mbar_arrive(smem_u32(&S.full[slot]));
+      // (failure-path test: the first slot's release is withheld, so the
+      // consumers' wait on it runs out)
+      if (warp == 0 && lane == 0 && !(p.test_stall && i == 0)) mbar_arrive(smem_u32(&S.full[slot]));
     }
     cp_async_wait<0>();
   } else {
@@ -317,7 +304,12 @@ __global__ void __launch_bounds__(NT, 1)
     float m_lo = -INFINITY, m_hi = -INFINITY;  // running max, heads g8 / g8+8 (log2)
     float o[16][4];  // O[heads g8, g8+8][128c + 8nt + 2q4 + {0,1}]
     float lacc[4];   // running row sums: [0] head g8, [2] head g8+8
+    // Q loads issued by consumer thread 0; after an error none is issued, and
+    // the one possibly in flight is waited for before the CTA exits.
+    int q_issued = 0;
     auto issue_q = [&](int64_t row) {
+      if (*reinterpret_cast<volatile int*>(&S.err) != 0) return;
+      ++q_issued;
       const int64_t qb = row / p.m, qm = row - qb * p.m;
       fence_proxy_async_smem();  // the Q fragment reads above precede the TMA refill
       mbar_arrive_expect_tx(smem_u32(&S.q_full), Q_BYTES);
@@ -346,7 +338,6 @@ __global__ void __launch_bounds__(NT, 1)
         // this row's Q into registers; once every consumer holds it, the tile
         // is refilled with the next row's Q (one TMA box per 64 columns)
         wait_or_err(S, S.q_full, seg & 1, 7);
-        if (c == 0 && lane == 0) SA_TRACE_EV(i, 6);
         {
           const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
@@ -365,7 +356,6 @@ __global__ void __launch_bounds__(NT, 1)
       }
       const int slot = i % NSLOT;
       wait_or_err(S, S.full[slot], (i / NSLOT) & 1, 8);
-      if (c == 0 && lane == 0) SA_TRACE_EV(i, 1);
       const uint32_t sb = smem_u32(S.ring[slot]);
 
       // ---- S for keys 16c + 8nt + {0..7}: 2 n-tiles x 32 k-steps, 2-way split
@@ -388,13 +378,6 @@ __global__ void __launch_bounds__(NT, 1)
       }
       // ---- softmax on the fragments: x[nt][0,1] head g8, x[nt][2,3] head g8+8,
       //      keys 16c + 8nt + 2q4 + {0,1}
-#ifdef SA_TRACE
-      {  // development builds: wait for S before stamping
-        const float dep = sa[0][0][0] + sa[1][1][3];
-        if (dep == 1.2345e-30f) sa_ws_trace[0][0][0] = 1;
-        if (c == 0 && lane == 0) SA_TRACE_EV(i, 2);
-      }
-#endif
       const uint32_t mw0 = S.mask[slot][0], mw1 = S.mask[slot][1];
       float x[2][4];
       bool over = false;
@@ -460,7 +443,6 @@ __global__ void __launch_bounds__(NT, 1)
         }
       }
       named_bar(3, NCT);  // P of all 64 keys written
-      if (c == 0 && lane == 0) SA_TRACE_EV(i, 3);
 
       // ---- O[16 x 128 cols of this warp] += P[16 x 64] . V[64 x 128]
 #pragma unroll
@@ -484,15 +466,6 @@ __global__ void __launch_bounds__(NT, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&S.empty[slot]));  // slot free for the producer
-#ifdef SA_TRACE
-      {  // development builds: wait for P.V before stamping
-        float dep = 0.f;
-#pragma unroll
-        for (int nt = 0; nt < 16; ++nt) dep += o[nt][0];
-        if (dep == 1.2345e-30f) sa_ws_trace[0][0][0] = 1;
-        if (c == 0 && lane == 0) SA_TRACE_EV(i, 4);
-      }
-#endif
 
       if (seg_end) {
         // ---------------- epilogue of the segment ending at unit i ----------
@@ -547,7 +520,6 @@ __global__ void __launch_bounds__(NT, 1)
           }
         }
       }
-      if (seg_end && c == 0 && lane == 0) SA_TRACE_EV(i, 5);
       if (seg_end) ++seg;
       seg_first = seg_end;
       if (++kb == nu_t) {
@@ -559,6 +531,13 @@ __global__ void __launch_bounds__(NT, 1)
         } else {
           ++t;
         }
+      }
+    }
+    // After an error the last Q load issued may still be in flight: wait for
+    // it (its phase is the only one not yet seen) before the CTA exits.
+    if (tt == 0 && q_issued > 0 && *reinterpret_cast<volatile int*>(&S.err) != 0) {
+      const uint32_t qb = smem_u32(&S.q_full);
+      for (uint32_t k = 0; k < kSpinLimit && !mbar_try_wait(qb, (q_issued - 1) & 1); ++k) {
       }
     }
   }
@@ -592,16 +571,6 @@ __global__ void __launch_bounds__(NT, 1)
 // ---------------------------------------------------------------------------
 int ws_unit_keys() { return ws_path::UK; }
 
-#ifdef SA_TRACE
-extern "C" int sa_ws_trace_read(unsigned long long* out, size_t bytes) {
-  if (bytes < sizeof(sa_ws_trace)) return -1;
-  return (int)cudaMemcpyFromSymbol(out, sa_ws_trace, sizeof(sa_ws_trace));
-}
-extern "C" int sa_ws_trace_clear() {
-  static unsigned long long zero[kTraceCtas * kTraceUnits * kTraceEvents] = {};
-  return (int)cudaMemcpyToSymbol(sa_ws_trace, zero, sizeof(zero));
-}
-#endif
 
 int read_ws_index_faults(unsigned long long* out, bool reset) {
   return index_fault_io(sa_ws_index_faults, out, reset);
@@ -613,6 +582,11 @@ int read_ws_error(int* flags) {
   if (e != cudaSuccess) return (int)e;
   *flags = v;
   return 0;
+}
+
+int reset_ws_error() {
+  const int zero = 0;
+  return (int)cudaMemcpyToSymbol(sa_ws_error, &zero, sizeof(int));
 }
 
 cudaError_t encode_q_map(const Params& p, CUtensorMap* q_map);  // sa_tc.cu

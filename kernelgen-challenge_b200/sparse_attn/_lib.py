@@ -6,13 +6,10 @@ shared object is missing or cannot be loaded, :func:`lib` raises.
 from __future__ import annotations
 
 import ctypes
-import os
 import pathlib
 import threading
 
-# SPARSE_ATTN_LIB overrides the library path (e.g. an instrumented build)
-LIB_PATH = pathlib.Path(os.environ.get("SPARSE_ATTN_LIB") or
-                        pathlib.Path(__file__).resolve().parent / "libsparse_attn.so")
+LIB_PATH = pathlib.Path(__file__).resolve().parent / "libsparse_attn.so"
 
 SA_OK = 0
 SA_ERR_INVALID_ARG = -1
@@ -24,6 +21,11 @@ SA_VARIANT_AUTO = 0
 SA_VARIANT_MMA = 1
 SA_VARIANT_TCGEN05 = 2
 SA_VARIANT_WS = 3
+
+SA_OPT_ROW_SCHEDULE = 1
+SA_OPT_INDEXER_TC = 2
+SA_OPT_SPIN_LIMIT = 3
+SA_OPT_TEST_STALL = 4
 
 # every function the header declares, with its ctypes signature
 _I64 = ctypes.c_int64
@@ -37,6 +39,9 @@ SIGNATURES = {
     "sa_last_cuda_error": (ctypes.c_int, []),
     "sa_variant_available": (ctypes.c_int, [ctypes.c_int]),
     "sa_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "sa_device_status_reset": (ctypes.c_int, []),
+    "sa_set_option": (ctypes.c_int, [ctypes.c_int, _I64]),
+    "sa_get_option": (_I64, [ctypes.c_int]),
     "sa_index_faults": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]),
     "sa_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, ctypes.c_int]),
     "sa_fwd": (ctypes.c_int, _FWD_ARGS),
@@ -99,6 +104,18 @@ def device_status() -> int:
     v = ctypes.c_int(0)
     check(lib().sa_device_status(ctypes.byref(v)))
     return v.value
+
+
+def device_status_reset() -> None:
+    """Zero the error words that :func:`device_status` reads (current device)."""
+    check(lib().sa_device_status_reset())
+
+
+def set_option(option: int, value: int) -> int:
+    """Set a process-wide library option (SA_OPT_*); returns the old value."""
+    old = lib().sa_get_option(option)
+    check(lib().sa_set_option(option, int(value)))
+    return old
 
 
 def index_faults(reset: bool = False) -> int:

@@ -2,10 +2,11 @@
 CPU statement, attention against the oracle on the dequantised cache and
 against the live reference's golden outputs on that cache.
 
-Tolerance: atol = rtol = 2e-2 on the bf16 output, as for the bf16 path.  Q
-and P run as two e4m3 terms each, so the error budget is close to the bf16
-kernels'.  The K/V quantisation is not an error here: the oracle uses the
-same e4m3 values.
+Tolerance: atol = rtol = 2e-2 on the bf16 output, as for the bf16 path.  The
+kernel widens the e4m3 K/V to f16 in registers (exact) and runs f16 MMAs with
+f16 Q (scaled per head by a power of two) and f16 P, so its error budget is at
+most the bf16 kernels'.  The K/V quantisation is not an error here: the
+oracle uses the same e4m3 values.
 """
 import pytest
 import torch
