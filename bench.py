@@ -1,20 +1,31 @@
 """Benchmark of the B200 ``sparse_attn`` hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config decode] [--variant auto|mma|tcgen05]
+                    [--config long] [--kv bf16|fp8] [--variant auto|mma|tcgen05|ws]
+    python bench.py --op gather          random-row gather ceiling (no math)
+    python bench.py --suite reftable     the reference's own 10-workload table
 
-A "step" is one call of the op over one batch of the configuration (default:
-BASELINE config "decode", b=64 m=1 kv_len=32768 topk=2048, h=16 d=512).
-``value`` is query-tokens/s of the whole job with inputs resident in HBM,
-timed with CUDA events on the launching stream, L2 flushed (256 MiB write)
-before every timed step and the flush kept outside the events.  ``e2e`` is the
-same metric through the public op ``sparse_attn`` with the step's q and
-topk_idxs copied from pinned host memory and o copied back inside the timed
-region (the KV cache and sink stay resident, as a serving KV cache does).
+A "step" is one pass of the op over the configuration's whole batch (default:
+BASELINE config "long", b=2 m=8192 kv_len=65536 topk=2048, h=16 d=512, the
+largest configuration that fits one GPU).  With N ranks (torchrun, one
+process per GPU) the job is strong-scaled: rank r runs the query rows
+``shard.partition_blocks(b, m, N, r)`` gives it (contiguous row ranges, no
+collective on the data path) with its batch items' KV caches resident; the
+step time is the max over ranks and ``value`` = the job's query-tokens / that
+time.  The one collective of the sharded op, the all-gather of o, is timed
+separately (``allgather``), outside the op's timed region.
 
-Multi-GPU (torchrun, one process per GPU): every rank runs its own batch of
-the configuration (weak scaling, query rows sharded by batch, no collective on
-the data path); the time is the max over ranks.
+``value`` is timed with CUDA events on the launching stream, inputs resident
+in HBM, L2 flushed (256 MiB write) before every timed step and the flush kept
+outside the events.  ``e2e`` is the same metric through the public op with the
+step's q and topk_idxs copied from pinned host memory and o copied back inside
+the timed region (the KV cache and sink stay resident, as a serving KV cache
+does).  ``per_config`` repeats the measurement for the other BASELINE configs
+(decode, causal, MTP at one GPU; MTP batch-sharded at N > 1), each with its
+roofline, CPU baseline and e2e.  ``triton_reference`` times the reference's
+own GPU kernel (its Triton "universal" kernel, track-01/submission.py:276-347,
+called through its unmodified ``sparse_attn``) on the same inputs when the
+reference is installed under ``baseline/_ref``.
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle port of
 track-01/reference/reference.py) on all host cores, rank 0 only.
@@ -22,7 +33,9 @@ track-01/reference/reference.py) on all host cores, rank 0 only.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
+import math
 import os
 import pathlib
 import statistics
@@ -42,6 +55,10 @@ METRIC = "sparse_attn query-tokens/s at topk=2048"
 UNIT = "query-tokens/s"
 FALLBACK_HBM_GBS = 6650.0
 L2_FLUSH_BYTES = 256 << 20
+REF_DIR = ROOT / "baseline" / "_ref" / "track-01"
+# steps of each per-config measurement: enough timed work (>= ~0.1 s of op
+# time) for the clock sampler to see the load
+PER_CONFIG_STEPS = {"decode": 3000, "mtp": 1000, "causal": 200, "long": 50}
 
 
 def parse():
@@ -50,20 +67,30 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="decode")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="long")
     ap.add_argument("--variant", choices=["auto", "mma", "tcgen05", "ws"], default="auto")
     ap.add_argument("--grid", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true",
-                    help="skip the CPU baseline leg (profiling runs)")
+                    help="skip the CPU baseline legs (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-per-config", action="store_true",
+                    help="measure the --config line only")
+    ap.add_argument("--no-triton", action="store_true",
+                    help="skip the reference Triton kernel timing")
     ap.add_argument("--kv", choices=["bf16", "fp8"], default="bf16",
                     help="KV cache format: bf16 (the reference's) or e4m3 + fp32 per-token "
                          "scale (sparse_attn_fp8)")
-    ap.add_argument("--op", choices=["sparse_attn", "sparse_attn_bwd", "hc_sinkhorn", "indexer"],
+    ap.add_argument("--op", choices=["sparse_attn", "sparse_attn_bwd", "hc_sinkhorn", "indexer",
+                                     "gather"],
                     default="sparse_attn",
                     help="sparse_attn_bwd: the backward pass on --config; indexer: the top-k "
                          "index producer on --config's b, m, kv_len, topk; "
-                         "hc_sinkhorn: the track-02 op on its 1k-1-64 prefill shape")
+                         "hc_sinkhorn: the track-02 op on its 1k-1-64 prefill shape; "
+                         "gather: the random-row gather ceiling (copies only, no math)")
+    ap.add_argument("--suite", choices=["none", "reftable"], default="none",
+                    help="reftable: the reference's 10-workload table "
+                         "(track-01/workloads.py:15-26) through the reference's torch "
+                         "oracle, its Triton kernel and this library")
     ap.add_argument("--graph", action="store_true",
                     help="capture one op call in a CUDA graph and time its replays")
     ap.add_argument("--no-launch-count", action="store_true",
@@ -162,13 +189,23 @@ class ClockSampler:
 # ----------------------------------------------------------------------------
 # inputs
 # ----------------------------------------------------------------------------
-def device_inputs(cfg, seed, device):
-    """Seeded inputs made directly on the GPU (indices on the CPU, then copied)."""
-    g = torch.Generator(device=device).manual_seed(seed)
-    q = torch.randn(cfg.b, cfg.m, H, D, generator=g, device=device, dtype=torch.bfloat16)
-    kv = torch.randn(cfg.b, cfg.kv_len, D, generator=g, device=device, dtype=torch.bfloat16)
-    sink = torch.randn(H, generator=g, device=device, dtype=torch.float32)
-    idx = make_indices(cfg, torch.Generator().manual_seed(seed)).to(device)
+def block_inputs(cfg, blk, seed, device):
+    """Seeded inputs of the row block ``blk`` of ``cfg``, made on the device
+    (indices on the CPU, then copied).  The KV cache of batch item j is seeded
+    by j alone, so ranks that hold rows of the same batch item see the same
+    cache; q and the indices are seeded by the block's first row."""
+    nb, mm = blk.b1 - blk.b0, blk.m1 - blk.m0
+    g = torch.Generator(device=device).manual_seed(seed * 7919 + blk.b0 * 65537 + blk.m0)
+    q = torch.randn(nb, mm, H, D, generator=g, device=device, dtype=torch.bfloat16)
+    kv = torch.empty(nb, cfg.kv_len, D, device=device, dtype=torch.bfloat16)
+    for i in range(nb):
+        kv[i].normal_(generator=torch.Generator(device=device).manual_seed(
+            seed * 1000003 + blk.b0 + i))
+    sink = torch.randn(H, generator=torch.Generator(device=device).manual_seed(seed),
+                       device=device, dtype=torch.float32)
+    icfg = dataclasses.replace(cfg, b=nb, m=mm)
+    idx = make_indices(icfg, torch.Generator().manual_seed(seed + 104729 * blk.b0 + blk.m0),
+                       m0=blk.m0).to(device)
     return q, kv, sink, idx
 
 
@@ -190,7 +227,7 @@ def profile_our_kernels(fn, flush, reps=5):
         per, gaps, spans, n = {}, [], [], 0
         prev_end, first_start, last_end = None, None, None
         for e in kern:
-            ours = "sa_" in e.name and ("fwd_kernel" in e.name or "combine" in e.name)
+            ours = "sa_" in e.name and "_kernel" in e.name
             if ours:
                 short = e.name.split("(")[0].split("::")[-1]
                 per.setdefault(short, []).append(e.time_range.end - e.time_range.start)
@@ -277,7 +314,7 @@ def run_reference(args):
     line = {
         "metric": METRIC, "value": val, "unit": UNIT, "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded CPU generator)",
         "config": {"workload": cfg.name, "b": cfg.b, "m": cfg.m, "h": H, "d": D,
                    "kv_len": cfg.kv_len, "topk": cfg.topk, "sample_rows_per_step": n},
@@ -291,8 +328,8 @@ def run_reference(args):
 # ----------------------------------------------------------------------------
 # GPU leg
 # ----------------------------------------------------------------------------
-def measure_e2e(cfg, q, kv, kscale, sink, idx, dev, stream, flush, K, barrier, world, tokens,
-                fp8, seed):
+def measure_e2e(idx_maker, q, kv, kscale, sink, idx, dev, stream, flush, K, barrier, world,
+                job_tokens, fp8):
     """The metric through the public op with host-resident q and indices.
 
     Every step copies its q and indices from pinned host memory to the GPU,
@@ -309,8 +346,7 @@ def measure_e2e(cfg, q, kv, kscale, sink, idx, dev, stream, flush, K, barrier, w
     ke = min(K, 100)
     nset = 4
     q_h = q.cpu().pin_memory()
-    idx_cpu = [idx.cpu()] + [make_indices(cfg, torch.Generator().manual_seed(seed + 7919 * r))
-                             for r in range(1, nset)]
+    idx_cpu = [idx.cpu()] + [idx_maker(r) for r in range(1, nset)]
     idx_hs = [t.pin_memory() for t in idx_cpu]
     # A serving loop stages each step's q and indices in one pinned slab, so
     # one host-to-device copy per step carries both (two copies cost ~15 %).
@@ -407,7 +443,7 @@ def measure_e2e(cfg, q, kv, kscale, sink, idx, dev, stream, flush, K, barrier, w
     if world > 1:
         torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
     p_ms, s_ms = float(te[0]), float(te[1])
-    return {"value": world * tokens * ke_p / (p_ms / 1e3), "unit": UNIT,
+    return {"value": job_tokens * ke_p / (p_ms / 1e3), "unit": UNIT,
             "h2d_bytes_per_step": q_h.numel() * q_h.element_size()
             + idx_hs[0].numel() * idx_hs[0].element_size(),
             "d2h_bytes_per_step": q.numel() * q.element_size(),
@@ -417,7 +453,7 @@ def measure_e2e(cfg, q, kv, kscale, sink, idx, dev, stream, flush, K, barrier, w
                          "the indices (one pinned slab), op into a preallocated o, D2H copy "
                          "of o; copies of later steps overlap the op of earlier ones (two "
                          "copy streams); 4 rotating index sets instead of an L2 flush",
-            "serial": {"value": world * tokens * ke / (s_ms / 1e3),
+            "serial": {"value": job_tokens * ke / (s_ms / 1e3),
                        "api": "sparse_attn.sparse_attn_fp8" if fp8 else "sparse_attn.sparse_attn",
                        "note": "no overlap, two H2D copies, 256 MiB L2 flush before every "
                                "step"}}
@@ -594,6 +630,402 @@ def run_indexer(args):
         "score_tflops": flops / (ms / 1e3) / 1e12}), flush=True)
 
 
+# ----------------------------------------------------------------------------
+# GPU leg: one configuration, this rank's rows
+# ----------------------------------------------------------------------------
+class Case:
+    """This rank's share of one configuration, resident on the device: one op
+    call per row block (``shard.partition_blocks``; one block at one GPU)."""
+
+    def __init__(self, cfg, rank, world, dev, seed, fp8=False, variant=0, grid=0):
+        import sparse_attn
+        from sparse_attn.shard import partition_blocks
+        self.cfg, self.dev, self.fp8, self.variant, self.grid = cfg, dev, fp8, variant, grid
+        self.seed = seed
+        self.blocks = partition_blocks(cfg.b, cfg.m, world, rank)
+        self.parts = []
+        valid = 0
+        for blk in self.blocks:
+            q, kv, sink, idx = block_inputs(cfg, blk, seed, dev)
+            valid += int(((idx >= 0) & (idx < cfg.kv_len)).sum().item())
+            ks = None
+            if fp8:  # quantised once, outside every timed region, by the library's kernel
+                kv, ks = sparse_attn.quantize_kv_fp8(kv)
+            self.parts.append((q, kv, ks, sink, idx, torch.empty_like(q)))
+        torch.cuda.synchronize(dev)
+        self.valid = valid
+        self.gathered = valid * (D + 4 if fp8 else 2 * D)
+        self.rows = sum(b.rows for b in self.blocks)
+        nbytes = max([sparse_attn.workspace_bytes(b.b1 - b.b0, b.m1 - b.m0, cfg.topk, dev)
+                      for b in self.blocks] + [256])
+        self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+
+    def step(self):
+        import sparse_attn
+        st = torch.cuda.current_stream(self.dev)
+        for q, kv, ks, sink, idx, o in self.parts:
+            if self.fp8:
+                sparse_attn.sparse_attn_fp8_out(o, q, kv, ks, sink, idx, SCALE, self.ws,
+                                                grid=self.grid, stream=st)
+            else:
+                sparse_attn.sparse_attn_out(o, q, kv, sink, idx, SCALE, self.ws,
+                                            variant=self.variant, grid=self.grid, stream=st)
+
+    def idx_maker(self, r):
+        """A fresh index set for the single block (e2e's rotating sets)."""
+        blk = self.blocks[0]
+        icfg = dataclasses.replace(self.cfg, b=blk.b1 - blk.b0, m=blk.m1 - blk.m0)
+        return make_indices(icfg, torch.Generator().manual_seed(self.seed + 7919 * r), m0=blk.m0)
+
+
+def timed_steps(step, K, flush, stream, barrier, clocks_dev=None):
+    """K L2-flushed steps timed by CUDA events (flush outside the events).
+    Returns (per-step ms list, clock summary)."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    sampler = ClockSampler(clocks_dev) if clocks_dev is not None else None
+    barrier()
+    if sampler:
+        sampler.start()
+    for k in range(K):
+        flush.zero_()
+        starts[k].record(stream)
+        step()
+        ends[k].record(stream)
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    return [s.elapsed_time(e) for s, e in zip(starts, ends)], clocks
+
+
+def max_over_ranks(vals, dev, world):
+    t = torch.tensor(vals, device=dev, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return [float(x) for x in t.tolist()]
+
+
+def l2_copy_gbs(dev, reps=50):
+    """Measured L2 bandwidth denominator: a plain device copy of a 24 MiB
+    buffer into another (48 MiB, L2-resident after the first pass), read +
+    write bytes over the best CUDA-event time of ``reps`` back-to-back copies."""
+    n = 24 << 20
+    a = torch.empty(n, dtype=torch.uint8, device=dev).fill_(1)
+    b = torch.empty_like(a)
+    st = torch.cuda.current_stream(dev)
+    for _ in range(5):
+        b.copy_(a)
+    best = None
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(10):
+            b.copy_(a)
+        e1.record(st)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / 10
+        best = ms if best is None else min(best, ms)
+    return 2 * n / (best / 1e3) / 1e9
+
+
+def traffic_for(key):
+    tpath = ROOT / "profiles" / "traffic.json"
+    if not tpath.exists():
+        return None
+    try:
+        return json.loads(tpath.read_text()).get(key)
+    except Exception:
+        return None
+
+
+def measure_config(cfg, args, rank, world, dev, flush, barrier, K, *, headline, fp8,
+                   variant, l2_gbs, with_e2e, with_cpu):
+    """Time this rank's share of ``cfg``; returns the result dict (rank 0's
+    view: times are max over ranks, bytes and launches are this rank's)."""
+    case = Case(cfg, rank, world, dev, seed=1000, fp8=fp8, variant=variant, grid=args.grid)
+    stream = torch.cuda.current_stream(dev)
+    step = case.step
+    if args.graph:
+        case.step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            case.step()
+        step = graph.replay
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    per_call, kernel_us = (None, {}) if args.no_launch_count else profile_our_kernels(step, flush)
+    step_ms, clocks = timed_steps(step, K, flush, stream, barrier, dev.index)
+    total_ms = sum(step_ms)
+    max_total_ms, = max_over_ranks([total_ms], dev, world)
+    job_tokens = cfg.b * cfg.m
+    value = job_tokens * K / (max_total_ms / 1e3)
+    mean_ms = total_ms / K
+    peak, peak_kind = measured_peaks()
+    achieved = case.gathered / (mean_ms / 1e3) / 1e9
+    key = f"{cfg.name}:fp8" if fp8 else f"{cfg.name}:{args.variant}"
+    traffic = traffic_for(key)
+    if traffic is None and not fp8:
+        traffic = traffic_for(f"{cfg.name}:auto")
+    res = {
+        "value": value, "unit": UNIT, "ms_per_step": max_total_ms / K, "steps": K,
+        "config": {"workload": cfg.name, "b": cfg.b, "m": cfg.m, "h": H, "d": D,
+                   "kv_len": cfg.kv_len, "topk": cfg.topk,
+                   "rows_this_rank": case.rows, "blocks_this_rank": len(case.blocks)},
+        "gathered_kv_gbs": case.gathered / (mean_ms / 1e3) / 1e9,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)"
+                     if peak_kind == "measured" else "fallback 6650 GB/s",
+                     "algorithmic_bytes_per_step": case.gathered,
+                     "note": "achieved = valid gathered KV bytes of this GPU's rows ("
+                             + ("516" if fp8 else "1024") + " per slot) / mean event time of "
+                             "one step (every kernel of the op call)"},
+        "gpu_launches": None if per_call is None else per_call * K,
+        "kernel_us": kernel_us,
+        "step_ms": {"mean": mean_ms, "min": min(step_ms), "median": statistics.median(step_ms)},
+        "clocks": clocks,
+    }
+    # KV caches that fit in L2 are served from it: report the L2 fraction too
+    kv_bytes = cfg.kv_len * (D + 4 if fp8 else 2 * D) * sum(b.b1 - b.b0 for b in case.blocks)
+    if l2_gbs and kv_bytes <= (128 << 20):
+        res["roofline_l2"] = {"bound": "l2", "achieved": achieved, "peak": l2_gbs,
+                              "unit": "GB/s", "frac": achieved / l2_gbs,
+                              "peak_source": "measured in this run: plain 24 MiB device "
+                                             "copy, L2-resident (read + write bytes)",
+                              "kv_cache_bytes": kv_bytes}
+    if with_e2e and len(case.blocks) == 1:
+        q, kv, ks, sink, idx, _ = case.parts[0]
+        res["e2e"] = measure_e2e(case.idx_maker, q, kv, ks, sink, idx, dev, stream, flush, K,
+                                 barrier, world, job_tokens, fp8)
+    else:
+        res["e2e"] = None
+    if with_cpu and world == 1:
+        val, n, reps, el, cores = cpu_throughput(cfg, rows=16, min_seconds=8.0, max_reps=200)
+        res["cpu_baseline"] = {
+            "value": val, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{n} query rows of '{cfg.name}' x {reps} reps ({el:.1f} s), {CPU_IMPL}"}
+    else:
+        res["cpu_baseline"] = None
+    res["_case"] = case
+    return res
+
+
+def time_allgather(case, dev, world, reps=20):
+    """The sharded op's one collective, timed alone: every rank's o rows
+    (padded to the largest share) all-gathered over NCCL."""
+    import torch.distributed as dist
+    from sparse_attn.shard import row_range
+    cfg = case.cfg
+    n_rows = cfg.b * cfg.m
+    chunk = max(row_range(n_rows, world, r)[1] - row_range(n_rows, world, r)[0]
+                for r in range(world))
+    local = torch.zeros(chunk, H, D, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(world * chunk, H, D, dtype=torch.bfloat16, device=dev)
+    st = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        dist.all_gather_into_tensor(out, local)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        dist.all_gather_into_tensor(out, local)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms, = max_over_ranks([e0.elapsed_time(e1) / reps], dev, world)
+    return {"ms": ms, "bytes_per_rank": local.numel() * 2,
+            "note": "all_gather_into_tensor of each rank's o rows (padded to the largest "
+                    "share), NCCL, outside the op's timed region"}
+
+
+def triton_reference(case, reps=10):
+    """The reference's own GPU path on this case's inputs: its unmodified
+    ``sparse_attn`` (track-01/submission.py:975), whose NVIDIA branch launches
+    the Triton universal kernel (:1003-1021).  Imported from baseline/_ref;
+    CUDA-event timed, L2 flushed before each call.  Only its times are read."""
+    if not (REF_DIR / "submission.py").exists():
+        return {"unavailable": "reference not installed under baseline/_ref (pure-Python "
+                               "repository, copied there by baseline/install_reference.sh)"}
+    try:
+        if str(REF_DIR) not in sys.path:
+            sys.path.insert(0, str(REF_DIR))
+        import importlib
+        sub = importlib.import_module("submission")
+        if not str(getattr(sub, "__file__", "")).startswith(str(REF_DIR)):
+            return {"unavailable": "another 'submission' module shadows the reference's"}
+        fn = sub.sparse_attn
+        dev = case.dev
+        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        st = torch.cuda.current_stream(dev)
+        outs = []
+        for q, kv, ks, sink, idx, o in case.parts:
+            outs.append(fn(q, kv, sink, idx, SCALE))  # compile + warm-up
+        torch.cuda.synchronize()
+        ms = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for q, kv, ks, sink, idx, o in case.parts:
+                fn(q, kv, sink, idx, SCALE)
+            e1.record(st)
+            e1.synchronize()
+            ms.append(e0.elapsed_time(e1))
+        # agreement of the two GPU paths on these inputs (max |difference|)
+        diff = max(float((a.float() - p[5].float()).abs().max()) for a, p in zip(outs, case.parts))
+        mean = sum(ms) / len(ms)
+        return {"ms_per_step": mean, "value": case.cfg.b * case.cfg.m / (mean / 1e3),
+                "unit": UNIT, "reps": reps, "max_abs_diff_vs_ours": diff,
+                "kernel": "reference Triton universal kernel (track-01/submission.py:276-347)"}
+    except Exception as e:  # noqa: BLE001 - reported, never fatal
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+
+
+def run_gather_probe(args):
+    """--op gather: random-row gather rates with no math (sa_probe_gather).
+    128 MiB of 1 KiB rows per call from a 2 GiB cache (the decode config's
+    size), L2 flushed before each call, CUDA events; the same kernel on
+    sequential rows shows what the copy machinery reaches without scatter."""
+    from sparse_attn import _lib
+    import ctypes
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L = _lib.lib()
+    cache = torch.empty(2 << 30, dtype=torch.uint8, device=dev)
+    sink = torch.zeros(4096, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    peak, kind = measured_peaks()
+    g = torch.Generator(device=dev).manual_seed(0)
+    total = 128 << 20
+    results = []
+
+    def run(row_bytes, method, ctas, depth, pattern, reps=20):
+        n_rows = total // row_bytes
+        pool = (2 << 30) // row_bytes
+        rows = (torch.randint(0, pool, (n_rows,), generator=g, device=dev, dtype=torch.int32)
+                if pattern == "random" else torch.arange(n_rows, device=dev, dtype=torch.int32))
+
+        def call():
+            _lib.check(L.sa_probe_gather(cache.data_ptr(), row_bytes, rows.data_ptr(), n_rows,
+                                         row_bytes, method, ctas, depth, sink.data_ptr(),
+                                         err.data_ptr(), ctypes.c_void_p(st.cuda_stream)))
+        for _ in range(3):
+            flush.zero_()
+            call()
+        ms = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            call()
+            e1.record(st)
+            e1.synchronize()
+            ms.append(e0.elapsed_time(e1))
+        med = statistics.median(ms)
+        gbs = total / (med / 1e3) / 1e9
+        results.append({"row_bytes": row_bytes, "method": ["cp.async16", "bulk_tma_1d",
+                                                           "ldg_nc16_regs"][method],
+                        "ctas": ctas, "depth": depth, "pattern": pattern, "us": med * 1e3,
+                        "gbs": gbs, "frac_of_hbm": gbs / peak})
+
+    for pattern in ("random", "sequential"):
+        for method in (0, 1, 2):
+            for ctas, depth in ((sms, 3), (sms, 6), (2 * sms, 3)):
+                if method == 2 and depth != 3:
+                    continue
+                run(1024, method, ctas, depth, pattern)
+    for rb in (512, 2048, 4096):
+        run(rb, 0, sms, 6, "random")
+        run(rb, 1, sms, 6, "random")
+    torch.cuda.synchronize()
+    ok = int(err.item()) == 0
+    best = max((r for r in results if r["pattern"] == "random" and r["row_bytes"] == 1024),
+               key=lambda r: r["gbs"])
+    print(json.dumps({
+        "metric": "random 1 KiB row gather GB/s (copies only)", "value": best["gbs"],
+        "unit": "GB/s", "n_gpus": 1, "higher_is_better": True, "waits_ok": ok,
+        "config": {"workload": "gather probe", "bytes_per_call": total, "cache_bytes": 2 << 30,
+                   "l2": "flushed (256 MiB write) before every call, flush untimed"},
+        "peak": {"hbm_gbs": peak, "source": kind}, "best": best, "results": results}),
+        flush=True)
+
+
+def run_reftable(args):
+    """--suite reftable: the reference's benchmark (track-01/bench.py:27-53)
+    over its own 10-workload table (track-01/workloads.py:15-26, indices drawn
+    with replacement as at :36): its torch reference (reference.py), its Triton
+    kernel (submission.py), and this library, each CUDA-event timed with L2
+    flushed before every call; speedups over the torch reference and their
+    geometric mean, as the reference reports them."""
+    import sparse_attn
+    from sparse_attn.workloads import REFERENCE_TABLE as WORKLOADS
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev)
+    have_ref = (REF_DIR / "submission.py").exists()
+    ref_fn = tri_fn = None
+    if have_ref:
+        sys.path.insert(0, str(REF_DIR))
+        import importlib
+        tri_fn = importlib.import_module("submission").sparse_attn
+        ref_fn = importlib.import_module("reference.reference").sparse_attn
+
+    def bench_fn(fn, a, reps=30):
+        for _ in range(3):
+            fn(*a)
+        torch.cuda.synchronize()
+        ms = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn(*a)
+            e1.record(st)
+            e1.synchronize()
+            ms.append(e0.elapsed_time(e1))
+        return statistics.median(ms)
+
+    rows = []
+    for label, b, m, kv_len, topk in WORKLOADS:
+        g = torch.Generator(device=dev).manual_seed(0)
+        q = torch.randn(b, m, H, D, generator=g, device=dev, dtype=torch.bfloat16)
+        kv = torch.randn(b, kv_len, D, generator=g, device=dev, dtype=torch.bfloat16)
+        sink = torch.randn(H, generator=g, device=dev, dtype=torch.float32)
+        idx = torch.randint(0, kv_len, (b, m, topk), generator=g, device=dev, dtype=torch.int32)
+        a = (q, kv, sink, idx, SCALE)
+        r = {"workload": label, "b": b, "m": m, "kv_len": kv_len, "topk": topk,
+             "ours_ms": bench_fn(sparse_attn.sparse_attn, a)}
+        if have_ref:
+            r["triton_ms"] = bench_fn(tri_fn, a)
+            try:
+                r["torch_ref_ms"] = bench_fn(ref_fn, a, reps=10)
+            except torch.cuda.OutOfMemoryError:
+                r["torch_ref_ms"] = None
+                torch.cuda.empty_cache()
+        rows.append(r)
+        del q, kv, idx
+        torch.cuda.empty_cache()
+
+    def geo(xs):
+        xs = [x for x in xs if x]
+        return math.exp(sum(math.log(x) for x in xs) / len(xs)) if xs else None
+    summary = {"geomean_ours_over_triton": geo([r.get("triton_ms", 0) / r["ours_ms"]
+                                                for r in rows if r.get("triton_ms")]),
+               "geomean_ours_over_torch_ref": geo([r["torch_ref_ms"] / r["ours_ms"]
+                                                   for r in rows if r.get("torch_ref_ms")]),
+               "geomean_triton_over_torch_ref": geo([r["torch_ref_ms"] / r["triton_ms"]
+                                                     for r in rows if r.get("torch_ref_ms")
+                                                     and r.get("triton_ms")])}
+    print(json.dumps({"suite": "reftable", "reference_available": have_ref, "rows": rows,
+                      **summary}), flush=True)
+
+
 def main():
     args = parse()
     if args.op == "indexer":
@@ -602,11 +1034,12 @@ def main():
         return run_hc_sinkhorn(args)
     if args.op == "sparse_attn_bwd":
         return run_backward(args)
+    if args.op == "gather":
+        return run_gather_probe(args)
+    if args.suite == "reftable":
+        return run_reftable(args)
     if args.impl == "reference":
         return run_reference(args)
-
-    import sparse_attn
-    from sparse_attn import sparse_attn_out
 
     rank, local_rank, world = dist_env()
     torch.cuda.set_device(local_rank)
@@ -615,136 +1048,95 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
     variant = {"auto": 0, "mma": 1, "tcgen05": 2, "ws": 3}[args.variant]
-    cfg = CONFIGS[args.config]
-    q, kv, sink, idx = device_inputs(cfg, seed=1000 + rank, device=dev)
-    o = torch.empty_like(q)
-    ws = torch.zeros(sparse_attn.workspace_bytes(cfg.b, cfg.m, cfg.topk, local_rank),
-                     dtype=torch.uint8, device=dev)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream(dev)
-    tokens = cfg.b * cfg.m
-    valid = int(((idx >= 0) & (idx < cfg.kv_len)).sum().item())
-    gathered = valid * D * 2
-
     fp8 = args.kv == "fp8"
-    if fp8:
-        # quantised once, outside every timed region, by the library's own kernel
-        kv8, kscale = sparse_attn.quantize_kv_fp8(kv)
-        del kv
-        torch.cuda.synchronize()
-        gathered = valid * (D + 4)  # e4m3 row + its fp32 scale
-
-    def op_call():
-        if fp8:
-            sparse_attn.sparse_attn_fp8_out(o, q, kv8, kscale, sink, idx, SCALE, ws,
-                                            grid=args.grid, stream=torch.cuda.current_stream(dev))
-        else:
-            sparse_attn_out(o, q, kv, sink, idx, SCALE, ws, variant=variant, grid=args.grid,
-                            stream=torch.cuda.current_stream(dev))
-
-    step = op_call
-    if args.graph:
-        # one op call (forward + combine launches, programmatic dependency kept)
-        # captured once; every step replays it on the timed stream
-        op_call()
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            op_call()
-        step = graph.replay
-
-    for _ in range(max(args.warmup, 3)):
-        flush.zero_()
-        step()
-    torch.cuda.synchronize()
-    per_call, kernel_us = (None, {}) if args.no_launch_count else profile_our_kernels(step, flush)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    K = args.steps
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    sampler = ClockSampler(local_rank)
-    barrier()
-    sampler.start()
-    for k in range(K):
-        flush.zero_()  # untimed: outside the events
-        starts[k].record(stream)
-        step()
-        ends[k].record(stream)
-    barrier()
-    clocks = sampler.stop()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = sum(step_ms)
-    t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    max_total_ms = float(t.item())
-    value = world * tokens * K / (max_total_ms / 1e3)
+    l2_gbs = l2_copy_gbs(dev)
+    cfg = CONFIGS[args.config]
+    head = measure_config(cfg, args, rank, world, dev, flush, barrier, args.steps,
+                          headline=True, fp8=fp8, variant=variant, l2_gbs=l2_gbs,
+                          with_e2e=not args.no_e2e, with_cpu=not args.no_cpu_baseline)
+    head_case = head.pop("_case")
+    allgather = time_allgather(head_case, dev, world) if world > 1 else None
+    triton = None
+    if rank == 0 and world == 1 and not args.no_triton and not fp8:
+        triton = triton_reference(head_case)
+        if "ms_per_step" in triton:
+            triton["ours_over_triton"] = triton["ms_per_step"] / head["ms_per_step"]
+    del head_case
+    torch.cuda.empty_cache()
 
-    # ---- end to end through the public op, host buffers ----
-    e2e = None
-    if not args.no_e2e:
-        e2e = measure_e2e(cfg, q, kv8 if fp8 else kv, kscale if fp8 else None, sink, idx, dev,
-                          stream, flush, K, barrier, world, tokens, fp8, seed=1000 + rank)
+    per_config = {}
+    if not args.no_per_config:
+        others = ["long", "decode", "causal", "mtp"] if world == 1 else ["mtp"]
+        for name in others:
+            if name == args.config:
+                continue
+            c = CONFIGS[name]
+            r = measure_config(c, args, rank, world, dev, flush, barrier,
+                               PER_CONFIG_STEPS.get(name, args.steps), headline=False, fp8=fp8,
+                               variant=variant, l2_gbs=l2_gbs, with_e2e=not args.no_e2e,
+                               with_cpu=not args.no_cpu_baseline)
+            case = r.pop("_case")
+            if rank == 0 and world == 1 and not args.no_triton and not fp8:
+                r["triton_reference"] = triton_reference(case)
+                if "ms_per_step" in r["triton_reference"]:
+                    r["triton_reference"]["ours_over_triton"] = (
+                        r["triton_reference"]["ms_per_step"] / r["ms_per_step"])
+            if world > 1:
+                r["allgather"] = time_allgather(case, dev, world)
+            del case
+            torch.cuda.empty_cache()
+            per_config[name] = r
 
     if rank != 0:
         if world > 1:
             torch.distributed.destroy_process_group()
         return
 
-    peak, peak_kind = measured_peaks()
-    mean_ms = total_ms / K
-    achieved = gathered / (mean_ms / 1e3) / 1e9
-    traffic = None
-    tpath = ROOT / "profiles" / "traffic.json"
-    if tpath.exists():
-        try:
-            tj = json.loads(tpath.read_text())
-            key = f"{args.config}:fp8" if fp8 else f"{args.config}:{args.variant}"
-            traffic = tj.get(key, None if fp8 else tj.get(args.config))
-        except Exception:
-            traffic = None
-
-    cpu = None
-    if world == 1 and not args.no_cpu_baseline:
-        val, n, reps, el, cores = cpu_throughput(cfg, rows=16, min_seconds=10.0, max_reps=200)
-        cpu = {"value": val, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"{n} query rows of '{cfg.name}' x {reps} reps ({el:.1f} s), "
-                         f"{CPU_IMPL}"}
-
+    launches = head["gpu_launches"]
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
-        "warmup": args.warmup, "ms_per_step": max_total_ms / K, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None,
+        "metric": METRIC, "value": head["value"], "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "e4m3 KV (fp32 per-token scale), bf16 q/o" if fp8 else "bf16",
-        "data": "synthetic (seeded; q/kv/sink randn on device, distinct indices per row)",
-        "config": {"workload": cfg.name, "b": cfg.b, "m": cfg.m, "h": H, "d": D,
-                   "kv_len": cfg.kv_len, "topk": cfg.topk, "global_batch": cfg.b * world,
-                   "parallelism": f"rows sharded by batch over {world} GPU(s), no collective",
+        "data": "synthetic (seeded; q/kv/sink randn on device, distinct indices per row "
+                "drawn on the CPU with the config's pattern)",
+        "config": {**head["config"], "global_batch": cfg.b, "seq_len": cfg.m,
+                   "parallelism": f"query rows sharded over {world} GPU(s) "
+                                  "(shard.partition_blocks), KV cache of each rank's batch "
+                                  "items resident, no collective in the timed region",
+                   "allgather": "of o, outside the timed region, timed separately"
+                                if world > 1 else "none (one GPU)",
                    "l2": "flushed (256 MiB write) before every timed step, flush untimed",
                    "variant": "fp8" if fp8 else args.variant, "grid": args.grid,
                    "kv_cache": "e4m3 + fp32 per-token scale" if fp8 else "bf16",
                    "launch": "CUDA graph replay" if args.graph else "stream launch"},
-        "gathered_kv_gbs": gathered * world * K / (max_total_ms / 1e3) / 1e9,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": traffic,
-                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)"
-                     if peak_kind == "measured" else "fallback 6650 GB/s",
-                     "algorithmic_bytes_per_step": gathered,
-                     "note": "achieved = valid gathered KV bytes (" + ("516" if fp8 else "1024")
-                             + " per slot) / mean event time of one op call (main + combine "
-                             "kernels)"},
-        "cpu_baseline": cpu,
-        "e2e": e2e,
-        "gpu_launches": None if per_call is None else per_call * K,
-        "kernel_us": kernel_us,
-        "step_ms": {"mean": mean_ms, "min": min(step_ms), "median": statistics.median(step_ms)},
-        "clocks": clocks,
+        "gathered_kv_gbs": head["gathered_kv_gbs"],
+        "roofline": head["roofline"],
+        "cpu_baseline": head["cpu_baseline"],
+        "e2e": head["e2e"],
+        "gpu_launches": launches,
+        "kernel_us": head["kernel_us"],
+        "step_ms": head["step_ms"],
+        "clocks": head["clocks"],
+        "l2_copy_gbs": l2_gbs,
     }
+    if "roofline_l2" in head:
+        line["roofline_l2"] = head["roofline_l2"]
+    if allgather is not None:
+        allgather["value_with_allgather"] = (cfg.b * cfg.m) / (
+            (head["ms_per_step"] + allgather["ms"]) / 1e3)
+        line["allgather"] = allgather
+    if triton is not None:
+        line["triton_reference"] = triton
+    if per_config:
+        line["per_config"] = per_config
     print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

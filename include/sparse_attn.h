@@ -184,6 +184,20 @@ int sa_device_status_reset(void);
 int sa_set_option(int option, int64_t value);
 int64_t sa_get_option(int option);
 
+/* Diagnostic: the random-row gather of the forward kernels on its own, with
+ * no math, to measure how fast the GPU serves scattered KV rows.  Copies
+ * rows[0..n_rows) of src (row r at src + rows[r] * row_stride bytes,
+ * row_bytes each: a power of two, 16..32768) into shared memory or registers
+ * and discards them.  method 0 = 16-byte cp.async (the forward kernels'
+ * form), 1 = one 1-D bulk copy (TMA, no multicast) per row, 2 = 16-byte
+ * ld.global.nc into registers; `ctas` CTAs of 256 threads; `depth` = ring
+ * slots of 32 KiB (2..6, methods 0 and 1).  sink: >= ctas words (a checksum
+ * keeps the loads live); *err becomes nonzero if a bounded wait gave up.
+ * Stream-ordered.  No counterpart in the reference. */
+int sa_probe_gather(const void* src, int64_t row_stride, const int32_t* rows, int64_t n_rows,
+                    int64_t row_bytes, int method, int ctas, int depth, uint32_t* sink, int* err,
+                    void* stream);
+
 /* Last cudaError_t observed by this thread inside the library (0 if none). */
 int sa_last_cuda_error(void);
 

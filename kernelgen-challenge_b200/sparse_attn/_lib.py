@@ -42,6 +42,8 @@ SIGNATURES = {
     "sa_device_status_reset": (ctypes.c_int, []),
     "sa_set_option": (ctypes.c_int, [ctypes.c_int, _I64]),
     "sa_get_option": (_I64, [ctypes.c_int]),
+    "sa_probe_gather": (ctypes.c_int, [_P, _I64, _P, _I64, _I64, ctypes.c_int, ctypes.c_int,
+                                       ctypes.c_int, _P, _P, _P]),
     "sa_index_faults": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]),
     "sa_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, ctypes.c_int]),
     "sa_fwd": (ctypes.c_int, _FWD_ARGS),

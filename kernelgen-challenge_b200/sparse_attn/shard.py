@@ -18,7 +18,7 @@ import dataclasses
 
 import torch
 
-__all__ = ["RowPiece", "partition_rows", "sparse_attn_sharded"]
+__all__ = ["RowPiece", "RowBlock", "partition_rows", "partition_blocks", "sparse_attn_sharded"]
 
 
 @dataclasses.dataclass(frozen=True)
@@ -51,6 +51,37 @@ def partition_rows(b: int, m: int, world: int, rank: int) -> list[RowPiece]:
     return pieces
 
 
+@dataclasses.dataclass(frozen=True)
+class RowBlock:
+    """Rows ``m0:m1`` of batch items ``b0:b1``: one op call over a contiguous
+    slab (``q[b0:b1, m0:m1]``).  Either whole batch items (``m0 = 0``,
+    ``m1 = m``) or a part of one batch item (``b1 = b0 + 1``)."""
+    b0: int
+    b1: int
+    m0: int
+    m1: int
+
+    @property
+    def rows(self) -> int:
+        return (self.b1 - self.b0) * (self.m1 - self.m0)
+
+
+def partition_blocks(b: int, m: int, world: int, rank: int) -> list[RowBlock]:
+    """The rows of ``rank`` (as :func:`partition_rows`) as at most three
+    slabs: a leading partial batch item, the whole batch items, a trailing
+    partial one.  At one rank that is one block covering the whole job."""
+    pieces = partition_rows(b, m, world, rank)
+    blocks: list[RowBlock] = []
+    for p in pieces:
+        full = p.m0 == 0 and p.m1 == m
+        last = blocks[-1] if blocks else None
+        if full and last is not None and last.m0 == 0 and last.m1 == m and last.b1 == p.b:
+            blocks[-1] = RowBlock(last.b0, p.b + 1, 0, m)
+        else:
+            blocks.append(RowBlock(p.b, p.b + 1, p.m0, p.m1))
+    return blocks
+
+
 def sparse_attn_sharded(q, kv, attn_sink, topk_idxs, scale, group=None, compute=None):
     """Run the rows of this rank and all-gather the full output on every rank.
 
@@ -65,10 +96,10 @@ def sparse_attn_sharded(q, kv, attn_sink, topk_idxs, scale, group=None, compute=
     rank = dist.get_rank(group)
     b, m, h, d = q.shape
     n_rows = b * m
-    pieces = partition_rows(b, m, world, rank)
-    mine = [compute(q[p.b:p.b + 1, p.m0:p.m1], kv[p.b:p.b + 1], attn_sink,
-                    topk_idxs[p.b:p.b + 1, p.m0:p.m1], scale).reshape(-1, h, d)
-            for p in pieces]
+    blocks = partition_blocks(b, m, world, rank)
+    mine = [compute(q[k.b0:k.b1, k.m0:k.m1], kv[k.b0:k.b1], attn_sink,
+                    topk_idxs[k.b0:k.b1, k.m0:k.m1], scale).reshape(-1, h, d)
+            for k in blocks]
     local = torch.cat(mine) if mine else q.new_empty(0, h, d)
     # all_gather wants equal sizes: pad every rank's rows to the largest range
     chunk = max(row_range(n_rows, world, r)[1] - row_range(n_rows, world, r)[0]

@@ -58,6 +58,23 @@ CONFIGS = {
     "mtp": Config("mtp", 128, 2, 131072, 2048, "mtp"),
 }
 
+# The reference's own benchmark table, track-01/workloads.py:15-26, as
+# (label, b, m, kv_len, topk); its inputs are randn q/kv/sink and indices drawn
+# WITH replacement from [0, kv_len) (track-01/workloads.py:29-37).  Used by the
+# parity tests and by ``bench.py --suite reftable``.
+REFERENCE_TABLE = [
+    ("prefill-64x1024-1024-128", 64, 1024, 1024, 128),
+    ("prefill-64x1024-1280-384", 64, 1024, 1280, 384),
+    ("prefill-16x4096-4096-128", 16, 4096, 4096, 128),
+    ("prefill-1x16384-16384-128", 1, 16384, 16384, 128),
+    ("prefill-1x16384-20480-640", 1, 16384, 20480, 640),
+    ("decode-64x1-128-128", 64, 1, 128, 128),
+    ("decode-64x1-400-392", 64, 1, 400, 392),
+    ("decode-64x1-640-640", 64, 1, 640, 640),
+    ("decode-16x1-1408-640", 16, 1, 1408, 640),
+    ("decode-1x1-4480-640", 1, 1, 4480, 640),
+]
+
 _CHUNK_ELEMS = 1 << 25  # bound the random-key scratch to ~128 MiB
 
 
@@ -80,15 +97,19 @@ def _shuffle_rows(x: torch.Tensor, g: torch.Generator) -> torch.Tensor:
     return torch.gather(x, 1, perm)
 
 
-def make_indices(cfg: Config, g: torch.Generator) -> torch.Tensor:
-    """int32 ``[b, m, topk]`` index tensor for ``cfg`` (CPU)."""
+def make_indices(cfg: Config, g: torch.Generator, m0: int = 0) -> torch.Tensor:
+    """int32 ``[b, m, topk]`` index tensor for ``cfg`` (CPU).
+
+    ``m0`` is the query position of the first row within its batch item (a
+    shard of rows ``m0 : m0 + cfg.m``); only the causal pattern depends on it.
+    """
     rows = cfg.b * cfg.m
     k, n = cfg.topk, cfg.kv_len
     if cfg.pattern == "uniform":
         idx = _distinct_uniform(rows, n, k, g)
     elif cfg.pattern == "causal":
         # row i (query position i within its batch) may attend [0, i]
-        pos = torch.arange(cfg.m).repeat(cfg.b)                    # [rows]
+        pos = torch.arange(m0, m0 + cfg.m).repeat(cfg.b)          # [rows]
         idx = torch.empty(rows, k, dtype=torch.int64)
         step = max(1, _CHUNK_ELEMS // max(n, 1))
         ar = torch.arange(n)

@@ -1,9 +1,9 @@
 """Generate the golden vectors in this directory from the LIVE reference.
 
-Run in a container that has the reference checkout (read-only) at
-``$SPARSE_ATTN_REFERENCE`` (default ``/root/reference``):
+Run where the reference checkout is available, with its path in
+``$SPARSE_ATTN_REFERENCE`` (required):
 
-    python tests/golden/make_golden.py
+    SPARSE_ATTN_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 Each case's inputs come from a seeded CPU generator (``make_case``), so only
 the outputs and a SHA-256 of the input bytes are stored; the tests rebuild the
@@ -123,8 +123,15 @@ def input_digest_hc(mixes, hc_scale, hc_base) -> str:
     return h.hexdigest()
 
 
+def _reference_root() -> pathlib.Path:
+    root = os.environ.get("SPARSE_ATTN_REFERENCE")
+    if not root:
+        raise RuntimeError("set SPARSE_ATTN_REFERENCE to the reference checkout")
+    return pathlib.Path(root)
+
+
 def _load_hc_reference():
-    root = pathlib.Path(os.environ.get("SPARSE_ATTN_REFERENCE", "/root/reference"))
+    root = _reference_root()
     path = root / "track-02" / "reference" / "reference.py"
     spec = importlib.util.spec_from_file_location("kernelgen_track02_reference", path)
     mod = importlib.util.module_from_spec(spec)
@@ -148,8 +155,8 @@ def input_digest(q, kv, sink, idx, scale) -> str:
     return h.hexdigest()
 
 
-def _load_reference():
-    root = pathlib.Path(os.environ.get("SPARSE_ATTN_REFERENCE", "/root/reference"))
+def _load_reference(root=None):
+    root = pathlib.Path(root) if root is not None else _reference_root()
     path = root / "track-01" / "reference" / "reference.py"
     spec = importlib.util.spec_from_file_location("kernelgen_track01_reference", path)
     mod = importlib.util.module_from_spec(spec)

@@ -10,7 +10,10 @@ import make_golden
 from helpers import load_golden
 from oracle.sparse_attn_oracle import sparse_attn_oracle
 
-REF_ROOT = pathlib.Path(os.environ.get("SPARSE_ATTN_REFERENCE", "/root/reference"))
+# The live reference: $SPARSE_ATTN_REFERENCE (a checkout), else the copy that
+# baseline/install_reference.sh makes under baseline/_ref; skipped if neither.
+REF_ROOT = pathlib.Path(os.environ.get("SPARSE_ATTN_REFERENCE") or
+                        pathlib.Path(__file__).resolve().parent.parent / "baseline" / "_ref")
 HAVE_REF = (REF_ROOT / "track-01" / "reference" / "reference.py").exists()
 
 
@@ -39,7 +42,7 @@ def assert_within_one_ulp(a, b):
 
 @pytest.mark.skipif(not HAVE_REF, reason="reference checkout not present")
 def test_oracle_matches_live_reference_unmasked():
-    ref = make_golden._load_reference()
+    ref = make_golden._load_reference(REF_ROOT)
     q, kv, sink, idx, scale = make_golden.make_case("replacement")
     assert torch.equal(ref(q, kv, sink, idx, scale), sparse_attn_oracle(q, kv, sink, idx, scale))
 
