@@ -8,11 +8,16 @@
 // CTAs; sa_fwd_noalloc instead uses one file-scope device array of fixed size
 // that every GPU loading this library holds until the process exits.
 //
-// The array holds the partials of at most SA_NOALLOC_MAX_CTAS CTAs.  Nothing
-// in it has to start at zero: every partial is written before the combine
-// kernel reads it.  All calls on a device share the array, so calls that can
-// overlap on that GPU (different streams without ordering between them) race
-// and must be serialised by the caller.
+// The array holds the partials of at most SA_NOALLOC_MAX_CTAS CTAs.  Its
+// first bytes are the per-CTA ticket words of the in-kernel merge of split
+// rows (prefill-shaped calls without room for the row schedule), which must
+// be zero when a call starts: they rely on the zero initialisation of
+// __device__ storage when the module loads, and every call leaves them zero
+// again (each CTA that takes a ticket still does so when a bounded wait gave
+// up, and the last one resets the word).  Everything else in it is written
+// before it is read.  All calls on a device share the array, so calls that
+// can overlap on that GPU (different streams without ordering between them)
+// race and must be serialised by the caller.
 #include <mutex>
 
 #include "sa_common.cuh"

@@ -1,10 +1,10 @@
-"""Row-sharded run over NCCL on 2 GPUs equals the single-GPU result (GPU).
+"""Row-sharded run over NCCL on 2 GPUs against the CPU oracle (GPU).
 
 Skipped unless at least two GPUs are visible.  Each rank computes its row
 range of a reduced long-context problem with the B200 op and the ranks
-all-gather the output; the single-GPU op on the same inputs is the check,
-within the parity tolerance (a rank's smaller problem splits rows across
-CTAs differently, so partial sums merge in a different order).
+all-gather the output; the CPU oracle on the same inputs checks every row,
+within the parity tolerance (atol = rtol = 2e-2).  NVLS is off
+(NCCL_NVLS_ENABLE=0): the test needs only a plain all-gather.
 """
 import os
 import socket
@@ -47,11 +47,12 @@ def _worker(rank, world, port, path):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sharded_nccl_two_gpus_equals_single_gpu(tmp_path):
-    from sparse_attn import sparse_attn
+def test_sharded_nccl_two_gpus_matches_oracle(tmp_path):
+    from oracle.sparse_attn_oracle import sparse_attn_oracle
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
     path = str(tmp_path / "o.pt")
     mp.spawn(_worker, args=(2, _free_port(), path), nprocs=2, join=True)
     q, kv, sink, idx, scale = _inputs()
-    ref = sparse_attn(q.cuda(), kv.cuda(), sink.cuda(), idx.cuda(), scale).cpu()
+    ref = sparse_attn_oracle(q, kv, sink, idx, scale)
     from helpers import assert_close
-    assert_close(torch.load(path), ref, what="2-GPU sharded vs 1 GPU")
+    assert_close(torch.load(path), ref, what="2-GPU sharded vs oracle")
