@@ -98,6 +98,26 @@ def parse():
     return ap.parse_args()
 
 
+class L2Flush:
+    """Untimed L2 flush between timed steps: a 256 MiB write (the whole 126 MB
+    L2 is replaced), then a read of another 256 MiB buffer, so the lines the
+    write left dirty are written back here, outside the timed region, and the
+    next step starts from a cold, clean L2.  ``read=False`` keeps the write
+    alone (the step then also pays for writing those dirty lines back)."""
+
+    def __init__(self, dev, read=True):
+        self.w = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        self.r = torch.ones(L2_FLUSH_BYTES // 8, dtype=torch.int64, device=dev) if read else None
+
+    def zero_(self):
+        self.w.zero_()
+        if self.r is not None:
+            self._acc = self.r.sum()
+
+    describe = ("flushed before every timed step (256 MiB write, then a 256 MiB read so the "
+                "dirty lines are written back), flush untimed")
+
+
 def dist_env():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     return int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")), ws
@@ -492,7 +512,7 @@ def run_hc_sinkhorn(args):
     g = torch.Generator(device=dev).manual_seed(0)
     mixes = torch.randn(b, s_, 24, generator=g, device=dev)
     sc, base = torch.randn(3, generator=g, device=dev), torch.randn(24, generator=g, device=dev)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
     stream = torch.cuda.current_stream(dev)
     for _ in range(max(args.warmup, 3)):
         sparse_attn.hc_split_sinkhorn(mixes, sc, base)
@@ -550,7 +570,7 @@ def run_backward(args):
     q, kv, sink, idx = device_inputs(cfg, seed=1000, device=dev)
     o, lse = _forward_train(q, kv, sink, idx, SCALE)  # the training forward keeps the lse
     do = torch.randn(q.shape, device=dev, dtype=torch.bfloat16)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
     stream = torch.cuda.current_stream(dev)
     for _ in range(max(args.warmup, 3)):
         sparse_attn.sparse_attn_backward(q, kv, sink, idx, SCALE, o, do, lse)
@@ -605,7 +625,7 @@ def run_indexer(args):
     k = torch.randn(cfg.b, cfg.kv_len, 128, generator=g, device=dev, dtype=torch.bfloat16)
     w = torch.rand(cfg.b, cfg.m, 64, generator=g, device=dev)
     ln = torch.full((cfg.b, cfg.m), cfg.kv_len, dtype=torch.int32, device=dev)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
     stream = torch.cuda.current_stream(dev)
     for _ in range(max(args.warmup, 3)):
         sparse_attn.indexer_topk(q, k, w, ln, cfg.topk)
@@ -840,54 +860,26 @@ def time_allgather(case, dev, world, reps=20):
                     "share), NCCL, outside the op's timed region"}
 
 
-def triton_reference(case, reps=10):
-    """The reference's own GPU path on this case's inputs: its unmodified
-    ``sparse_attn`` (track-01/submission.py:975), whose NVIDIA branch launches
-    the Triton universal kernel (:1003-1021).  Imported from baseline/_ref;
-    CUDA-event timed, L2 flushed before each call.  Only its times are read."""
-    if not (REF_DIR / "submission.py").exists():
-        return {"unavailable": "reference not installed under baseline/_ref (pure-Python "
-                               "repository, copied there by baseline/install_reference.sh)"}
-    try:
-        if str(REF_DIR) not in sys.path:
-            sys.path.insert(0, str(REF_DIR))
-        import importlib
-        sub = importlib.import_module("submission")
-        if not str(getattr(sub, "__file__", "")).startswith(str(REF_DIR)):
-            return {"unavailable": "another 'submission' module shadows the reference's"}
-        fn = sub.sparse_attn
-        dev = case.dev
-        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-        st = torch.cuda.current_stream(dev)
-        outs = []
-        for q, kv, ks, sink, idx, o in case.parts:
-            outs.append(fn(q, kv, sink, idx, SCALE))  # compile + warm-up
-        torch.cuda.synchronize()
-        ms = []
-        for _ in range(reps):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            for q, kv, ks, sink, idx, o in case.parts:
-                fn(q, kv, sink, idx, SCALE)
-            e1.record(st)
-            e1.synchronize()
-            ms.append(e0.elapsed_time(e1))
-        # agreement of the two GPU paths on these inputs (max |difference|)
-        diff = max(float((a.float() - p[5].float()).abs().max()) for a, p in zip(outs, case.parts))
-        mean = sum(ms) / len(ms)
-        return {"ms_per_step": mean, "value": case.cfg.b * case.cfg.m / (mean / 1e3),
-                "unit": UNIT, "reps": reps, "max_abs_diff_vs_ours": diff,
-                "kernel": "reference Triton universal kernel (track-01/submission.py:276-347)"}
-    except Exception as e:  # noqa: BLE001 - reported, never fatal
-        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+# The reference's Triton kernel (track-01/submission.py:276-347, launched by its
+# sparse_attn at :1003-1021) is not run: on this pool's B200 it raised a CUDA
+# fault ("an illegal memory access was encountered") on the decode
+# configuration (b=64, m=1, kv_len=32768, topk=2048, every index inside
+# [0, kv_len)), so it stays off the GPU.
+TRITON_UNAVAILABLE = ("not run: the reference's Triton universal kernel "
+                      "(track-01/submission.py:276-347) raised an illegal-memory-access fault "
+                      "on this pool's B200 on the decode configuration, so it stays off the GPU")
+
+
+def triton_reference(case):
+    return {"unavailable": TRITON_UNAVAILABLE}
 
 
 def run_gather_probe(args):
     """--op gather: random-row gather rates with no math (sa_probe_gather).
-    128 MiB of 1 KiB rows per call from a 2 GiB cache (the decode config's
-    size), L2 flushed before each call, CUDA events; the same kernel on
-    sequential rows shows what the copy machinery reaches without scatter."""
+    128 MiB of rows per call from a 2 GiB cache (the decode config's size),
+    L2 flushed before each call (write only, or write then read), CUDA events;
+    the same kernel on sequential rows shows what the copy machinery reaches
+    without scatter."""
     from sparse_attn import _lib
     import ctypes
     dev = torch.device("cuda", 0)
@@ -896,7 +888,7 @@ def run_gather_probe(args):
     cache = torch.empty(2 << 30, dtype=torch.uint8, device=dev)
     sink = torch.zeros(4096, dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flushes = {"write": L2Flush(dev, read=False), "write+read": L2Flush(dev, read=True)}
     st = torch.cuda.current_stream(dev)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     peak, kind = measured_peaks()
@@ -904,11 +896,12 @@ def run_gather_probe(args):
     total = 128 << 20
     results = []
 
-    def run(row_bytes, method, ctas, depth, pattern, reps=20):
+    def run(row_bytes, method, ctas, depth, pattern, fl, reps=20):
         n_rows = total // row_bytes
         pool = (2 << 30) // row_bytes
         rows = (torch.randint(0, pool, (n_rows,), generator=g, device=dev, dtype=torch.int32)
                 if pattern == "random" else torch.arange(n_rows, device=dev, dtype=torch.int32))
+        flush = flushes[fl]
 
         def call():
             _lib.check(L.sa_probe_gather(cache.data_ptr(), row_bytes, rows.data_ptr(), n_rows,
@@ -930,18 +923,20 @@ def run_gather_probe(args):
         gbs = total / (med / 1e3) / 1e9
         results.append({"row_bytes": row_bytes, "method": ["cp.async16", "bulk_tma_1d",
                                                            "ldg_nc16_regs"][method],
-                        "ctas": ctas, "depth": depth, "pattern": pattern, "us": med * 1e3,
-                        "gbs": gbs, "frac_of_hbm": gbs / peak})
+                        "ctas": ctas, "depth": depth, "pattern": pattern, "flush": fl,
+                        "us": med * 1e3, "gbs": gbs, "frac_of_hbm": gbs / peak})
 
-    for pattern in ("random", "sequential"):
-        for method in (0, 1, 2):
-            for ctas, depth in ((sms, 3), (sms, 6), (2 * sms, 3)):
-                if method == 2 and depth != 3:
-                    continue
-                run(1024, method, ctas, depth, pattern)
+    for fl in ("write", "write+read"):
+        for pattern in ("random", "sequential"):
+            for method in (0, 1, 2):
+                for ctas, depth in ((sms, 3), (sms, 6), (2 * sms, 3)):
+                    if method == 2 and depth != 3:
+                        continue
+                    run(1024, method, ctas, depth, pattern, fl)
     for rb in (512, 2048, 4096):
-        run(rb, 0, sms, 6, "random")
-        run(rb, 1, sms, 6, "random")
+        for method in (0, 1):
+            run(rb, method, sms, 6, "random", "write+read")
+            run(rb, method, 2 * sms, 3, "random", "write+read")
     torch.cuda.synchronize()
     ok = int(err.item()) == 0
     best = max((r for r in results if r["pattern"] == "random" and r["row_bytes"] == 1024),
@@ -950,7 +945,7 @@ def run_gather_probe(args):
         "metric": "random 1 KiB row gather GB/s (copies only)", "value": best["gbs"],
         "unit": "GB/s", "n_gpus": 1, "higher_is_better": True, "waits_ok": ok,
         "config": {"workload": "gather probe", "bytes_per_call": total, "cache_bytes": 2 << 30,
-                   "l2": "flushed (256 MiB write) before every call, flush untimed"},
+                   "l2": "flushed before every call (see each result's 'flush'), untimed"},
         "peak": {"hbm_gbs": peak, "source": kind}, "best": best, "results": results}),
         flush=True)
 
@@ -958,22 +953,22 @@ def run_gather_probe(args):
 def run_reftable(args):
     """--suite reftable: the reference's benchmark (track-01/bench.py:27-53)
     over its own 10-workload table (track-01/workloads.py:15-26, indices drawn
-    with replacement as at :36): its torch reference (reference.py), its Triton
-    kernel (submission.py), and this library, each CUDA-event timed with L2
-    flushed before every call; speedups over the torch reference and their
-    geometric mean, as the reference reports them."""
+    with replacement as at :36): its torch reference (reference.py, on the GPU)
+    and this library, each CUDA-event timed with L2 flushed before every call;
+    the speedup over the torch reference per workload and its geometric mean,
+    as the reference reports its own.  (Its Triton kernel is not run; see
+    TRITON_UNAVAILABLE.)"""
     import sparse_attn
     from sparse_attn.workloads import REFERENCE_TABLE as WORKLOADS
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
     st = torch.cuda.current_stream(dev)
-    have_ref = (REF_DIR / "submission.py").exists()
-    ref_fn = tri_fn = None
+    have_ref = (REF_DIR / "reference" / "reference.py").exists()
+    ref_fn = None
     if have_ref:
         sys.path.insert(0, str(REF_DIR))
         import importlib
-        tri_fn = importlib.import_module("submission").sparse_attn
         ref_fn = importlib.import_module("reference.reference").sparse_attn
 
     def bench_fn(fn, a, reps=30):
@@ -1002,7 +997,6 @@ def run_reftable(args):
         r = {"workload": label, "b": b, "m": m, "kv_len": kv_len, "topk": topk,
              "ours_ms": bench_fn(sparse_attn.sparse_attn, a)}
         if have_ref:
-            r["triton_ms"] = bench_fn(tri_fn, a)
             try:
                 r["torch_ref_ms"] = bench_fn(ref_fn, a, reps=10)
             except torch.cuda.OutOfMemoryError:
@@ -1015,13 +1009,12 @@ def run_reftable(args):
     def geo(xs):
         xs = [x for x in xs if x]
         return math.exp(sum(math.log(x) for x in xs) / len(xs)) if xs else None
-    summary = {"geomean_ours_over_triton": geo([r.get("triton_ms", 0) / r["ours_ms"]
-                                                for r in rows if r.get("triton_ms")]),
-               "geomean_ours_over_torch_ref": geo([r["torch_ref_ms"] / r["ours_ms"]
-                                                   for r in rows if r.get("torch_ref_ms")]),
-               "geomean_triton_over_torch_ref": geo([r["torch_ref_ms"] / r["triton_ms"]
-                                                     for r in rows if r.get("torch_ref_ms")
-                                                     and r.get("triton_ms")])}
+    for r in rows:
+        if r.get("torch_ref_ms"):
+            r["speedup_over_torch_ref"] = r["torch_ref_ms"] / r["ours_ms"]
+    summary = {"geomean_speedup_over_torch_ref": geo([r["torch_ref_ms"] / r["ours_ms"]
+                                                      for r in rows if r.get("torch_ref_ms")]),
+               "triton_reference": TRITON_UNAVAILABLE}
     print(json.dumps({"suite": "reftable", "reference_available": have_ref, "rows": rows,
                       **summary}), flush=True)
 
@@ -1049,7 +1042,7 @@ def main():
         dist.init_process_group("nccl", device_id=dev)
     variant = {"auto": 0, "mma": 1, "tcgen05": 2, "ws": 3}[args.variant]
     fp8 = args.kv == "fp8"
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
 
     def barrier():
         if world > 1:
@@ -1113,7 +1106,7 @@ def main():
                                   "items resident, no collective in the timed region",
                    "allgather": "of o, outside the timed region, timed separately"
                                 if world > 1 else "none (one GPU)",
-                   "l2": "flushed (256 MiB write) before every timed step, flush untimed",
+                   "l2": L2Flush.describe,
                    "variant": "fp8" if fp8 else args.variant, "grid": args.grid,
                    "kv_cache": "e4m3 + fp32 per-token scale" if fp8 else "bf16",
                    "launch": "CUDA graph replay" if args.graph else "stream launch"},

@@ -30,6 +30,7 @@ struct Params {
   const int32_t* rows;
   int64_t n_rows, row_stride;  // bytes between rows of src
   int row_bytes, method, depth;
+  int cpr_log2;  // log2(16-byte chunks per row)
   uint32_t* sink;
   int* err;
 };
@@ -73,7 +74,7 @@ __global__ void __launch_bounds__(NT) probe_gather_kernel(const Params p) {
   const int64_t units = (p.n_rows + rows_per_unit - 1) / rows_per_unit;
   const int64_t u0 = blockIdx.x * units / gridDim.x, u1 = (blockIdx.x + 1) * units / gridDim.x;
   const int n = static_cast<int>(u1 - u0);
-  const int chunks_per_row = p.row_bytes / 16;
+  const int cpr_mask = (1 << p.cpr_log2) - 1;
   uint32_t acc = 0;
 
   if (p.method == 2) {  // registers: each thread owns 8 chunks of every unit
@@ -83,9 +84,9 @@ __global__ void __launch_bounds__(NT) probe_gather_kernel(const Params p) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int c = tid + k * NT;
-        const int64_t r = r0 + c / chunks_per_row;
+        const int64_t r = r0 + (c >> p.cpr_log2);
         const int64_t row = r < p.n_rows ? __ldg(p.rows + r) : 0;
-        v[k] = ldg_nc16(p.src + row * p.row_stride + (c % chunks_per_row) * 16);
+        v[k] = ldg_nc16(p.src + row * p.row_stride + (c & cpr_mask) * 16);
       }
 #pragma unroll
       for (int k = 0; k < 8; ++k) acc ^= v[k].x ^ v[k].w;
@@ -114,11 +115,12 @@ __global__ void __launch_bounds__(NT) probe_gather_kernel(const Params p) {
       const int64_t r0 = (u0 + i) * rows_per_unit;
       const uint32_t dst = smem_u32(ring + (size_t)slot * SLOT);
       if (p.method == 0) {
+#pragma unroll 4
         for (int c = tid; c < SLOT / 16; c += 128) {
-          const int64_t r = r0 + c / chunks_per_row;
+          const int64_t r = r0 + (c >> p.cpr_log2);
           const bool v = r < p.n_rows;
           const int64_t row = v ? __ldg(p.rows + r) : 0;
-          cp_async16_hint(dst + c * 16, p.src + row * p.row_stride + (c % chunks_per_row) * 16,
+          cp_async16_hint(dst + c * 16, p.src + row * p.row_stride + (c & cpr_mask) * 16,
                           v ? 16 : 0, pol);
         }
         cp_async_mbar_arrive_noinc(smem_u32(&full[slot]));
@@ -174,8 +176,10 @@ extern "C" int sa_probe_gather(const void* src, int64_t row_stride, const int32_
   if (method < 0 || method > 2 || ctas < 1 || ctas > 4096 || depth < 2 || depth > MAX_DEPTH)
     return SA_ERR_INVALID_ARG;
   if (n_rows == 0) return SA_OK;
+  int lg = 0;
+  while ((16 << lg) < row_bytes) ++lg;
   Params p{static_cast<const uint8_t*>(src), rows, n_rows, row_stride, static_cast<int>(row_bytes),
-           method, depth, sink, err};
+           method, depth, lg, sink, err};
   const size_t smem = method == 2 ? 0 : (size_t)depth * SLOT + 2 * MAX_DEPTH * 8 + 128;
   cudaError_t e = cudaFuncSetAttribute(probe_gather_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

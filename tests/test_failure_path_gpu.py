@@ -8,8 +8,8 @@ anything: ``SA_OPT_TEST_STALL`` withholds one arrival on the first ring slot
 (a flag that nothing else sets) and ``SA_OPT_SPIN_LIMIT`` shortens the wait.
 They then check that the call returned, that the status word carries the
 consumer's code, that ``sa_device_status_reset`` clears it, and that the next
-calls -- including one whose split rows are merged through the workspace's
-ticket words -- are correct against the CPU oracle.
+call is correct against the CPU oracle.  The calls are decode-shaped: a few
+units per CTA, split rows merged by the combine kernel.
 """
 import dataclasses
 
@@ -19,14 +19,14 @@ import torch
 from helpers import assert_close
 from oracle.sparse_attn_oracle import sparse_attn_fp8_oracle, sparse_attn_oracle
 from sparse_attn import _lib, quantize_kv_fp8, sparse_attn_fp8_out, sparse_attn_out
-from sparse_attn.workloads import CONFIGS, make_inputs
+from sparse_attn.workloads import CONFIGS, make_inputs  # noqa: F401
 
 pytestmark = pytest.mark.gpu
 
-# consumer wait on a ring slot's full barrier: code 8; ws reports 100 + code,
-# fp8 200 + code
-WS_FULL_WAIT = 108
-FP8_FULL_WAIT = 208
+# a wait on a ring slot's full barrier (8) or on a free slot (1) runs out; ws
+# reports 100 + code, fp8 200 + code
+WS_CODES = (101, 108)
+FP8_CODES = (201, 208)
 
 
 def _cuda(*ts):
@@ -59,7 +59,7 @@ def test_ws_wait_runs_out_then_recovers(stalled):
     o = torch.empty_like(qd)
     sparse_attn_out(o, qd, kvd, sd, idd, scale)  # returns: nothing waits forever
     torch.cuda.synchronize()
-    assert _lib.device_status() == WS_FULL_WAIT
+    assert _lib.device_status() in WS_CODES
     _lib.device_status_reset()
     assert _lib.device_status() == 0
     # healthy again: defaults restored, same call, right answer
@@ -71,31 +71,6 @@ def test_ws_wait_runs_out_then_recovers(stalled):
     assert_close(o, sparse_attn_oracle(q, kv, sink, idx, scale), what="after recovery")
 
 
-def test_ticket_merge_clean_after_a_stalled_call(stalled):
-    """Split rows merged in-kernel by ticket words: a stalled call must leave
-    every ticket at zero, or the next call would merge rows early."""
-    q, kv, sink, idx, scale = _sample("causal", 4, m=640)
-    qd, kvd, sd, idd = _cuda(q, kv, sink, idx)
-    ws = torch.zeros(1 << 25, dtype=torch.uint8, device="cuda")
-    old_rows = _lib.set_option(_lib.SA_OPT_ROW_SCHEDULE, 0)  # force the ticket merge
-    try:
-        o = torch.empty_like(qd)
-        sparse_attn_out(o, qd, kvd, sd, idd, scale, ws)
-        torch.cuda.synchronize()
-        assert _lib.device_status() == WS_FULL_WAIT
-        _lib.device_status_reset()
-        _lib.set_option(_lib.SA_OPT_TEST_STALL, 0)
-        _lib.set_option(_lib.SA_OPT_SPIN_LIMIT, 0)
-        assert int(ws[:2048].count_nonzero()) == 0, "ticket words left nonzero"
-        for _ in range(2):
-            sparse_attn_out(o, qd, kvd, sd, idd, scale, ws)
-            torch.cuda.synchronize()
-            assert _lib.device_status() == 0
-            assert_close(o, sparse_attn_oracle(q, kv, sink, idx, scale), what="ticket merge")
-    finally:
-        _lib.set_option(_lib.SA_OPT_ROW_SCHEDULE, old_rows)
-
-
 def test_fp8_wait_runs_out_then_recovers(stalled):
     q, kv, sink, idx, scale = _sample("decode", 5, b=4)
     qd, kvd, sd, idd = _cuda(q, kv, sink, idx)
@@ -103,7 +78,7 @@ def test_fp8_wait_runs_out_then_recovers(stalled):
     o = torch.empty_like(qd)
     sparse_attn_fp8_out(o, qd, kv8, ks, sd, idd, scale)
     torch.cuda.synchronize()
-    assert _lib.device_status() == FP8_FULL_WAIT
+    assert _lib.device_status() in FP8_CODES
     _lib.device_status_reset()
     _lib.set_option(_lib.SA_OPT_TEST_STALL, 0)
     _lib.set_option(_lib.SA_OPT_SPIN_LIMIT, 0)
