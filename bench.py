@@ -724,25 +724,32 @@ def max_over_ranks(vals, dev, world):
     return [float(x) for x in t.tolist()]
 
 
-def l2_copy_gbs(dev, reps=50):
+def l2_copy_gbs(dev, reps=20):
     """Measured L2 bandwidth denominator: a plain device copy of a 24 MiB
-    buffer into another (48 MiB, L2-resident after the first pass), read +
-    write bytes over the best CUDA-event time of ``reps`` back-to-back copies."""
+    buffer into another (48 MiB in all, L2-resident after the first pass),
+    20 copies back to back in one CUDA graph (no launch gaps), read + write
+    bytes over the best CUDA-event time of ``reps`` graph replays."""
     n = 24 << 20
     a = torch.empty(n, dtype=torch.uint8, device=dev).fill_(1)
     b = torch.empty_like(a)
-    st = torch.cuda.current_stream(dev)
-    for _ in range(5):
+    inner = 20
+    for _ in range(3):
         b.copy_(a)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(inner):
+            b.copy_(a)
+    st = torch.cuda.current_stream(dev)
+    graph.replay()
     best = None
     for _ in range(reps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
-        for _ in range(10):
-            b.copy_(a)
+        graph.replay()
         e1.record(st)
         e1.synchronize()
-        ms = e0.elapsed_time(e1) / 10
+        ms = e0.elapsed_time(e1) / inner
         best = ms if best is None else min(best, ms)
     return 2 * n / (best / 1e3) / 1e9
 
@@ -813,7 +820,8 @@ def measure_config(cfg, args, rank, world, dev, flush, barrier, K, *, headline, 
         res["roofline_l2"] = {"bound": "l2", "achieved": achieved, "peak": l2_gbs,
                               "unit": "GB/s", "frac": achieved / l2_gbs,
                               "peak_source": "measured in this run: plain 24 MiB device "
-                                             "copy, L2-resident (read + write bytes)",
+                                             "copy, L2-resident, 20 per CUDA graph "
+                                             "(read + write bytes)",
                               "kv_cache_bytes": kv_bytes}
     if with_e2e and len(case.blocks) == 1:
         q, kv, ks, sink, idx, _ = case.parts[0]
@@ -898,9 +906,12 @@ def run_gather_probe(args):
 
     def run(row_bytes, method, ctas, depth, pattern, fl, reps=20):
         n_rows = total // row_bytes
-        pool = (2 << 30) // row_bytes
+        # "random-l2": rows of a 4 MiB region (the causal config's KV cache), so
+        # after the first touches every row comes from L2
+        pool = ((4 << 20) if pattern == "random-l2" else (2 << 30)) // row_bytes
         rows = (torch.randint(0, pool, (n_rows,), generator=g, device=dev, dtype=torch.int32)
-                if pattern == "random" else torch.arange(n_rows, device=dev, dtype=torch.int32))
+                if pattern.startswith("random")
+                else torch.arange(n_rows, device=dev, dtype=torch.int32))
         flush = flushes[fl]
 
         def call():
@@ -937,6 +948,9 @@ def run_gather_probe(args):
         for method in (0, 1):
             run(rb, method, sms, 6, "random", "write+read")
             run(rb, method, 2 * sms, 3, "random", "write+read")
+    for method in (0, 1, 2):
+        run(1024, method, sms, 3, "random-l2", "write+read")
+        run(1024, method, 2 * sms, 3, "random-l2", "write+read")
     torch.cuda.synchronize()
     ok = int(err.item()) == 0
     best = max((r for r in results if r["pattern"] == "random" and r["row_bytes"] == 1024),

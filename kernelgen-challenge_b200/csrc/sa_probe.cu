@@ -31,6 +31,7 @@ struct Params {
   int64_t n_rows, row_stride;  // bytes between rows of src
   int row_bytes, method, depth;
   int cpr_log2;  // log2(16-byte chunks per row)
+  int ids_offset;  // byte offset of the staged row indices in dynamic shared memory
   uint32_t* sink;
   int* err;
 };
@@ -76,6 +77,13 @@ __global__ void __launch_bounds__(NT) probe_gather_kernel(const Params p) {
   const int n = static_cast<int>(u1 - u0);
   const int cpr_mask = (1 << p.cpr_log2) - 1;
   uint32_t acc = 0;
+  // The CTA's row indices, staged in shared memory up front (one round trip),
+  // so that no copy waits on an index load: the time is the gather alone.
+  int32_t* ids = reinterpret_cast<int32_t*>(smem_raw + p.ids_offset);
+  const int64_t r_begin = u0 * rows_per_unit;
+  const int n_ids = static_cast<int>(min((int64_t)n * rows_per_unit, p.n_rows - r_begin));
+  for (int k = tid; k < n_ids; k += NT) ids[k] = __ldg(p.rows + r_begin + k);
+  __syncthreads();
 
   if (p.method == 2) {  // registers: each thread owns 8 chunks of every unit
     for (int i = 0; i < n; ++i) {
@@ -85,7 +93,7 @@ __global__ void __launch_bounds__(NT) probe_gather_kernel(const Params p) {
       for (int k = 0; k < 8; ++k) {
         const int c = tid + k * NT;
         const int64_t r = r0 + (c >> p.cpr_log2);
-        const int64_t row = r < p.n_rows ? __ldg(p.rows + r) : 0;
+        const int64_t row = r < p.n_rows ? ids[r - r_begin] : 0;
         v[k] = ldg_nc16(p.src + row * p.row_stride + (c & cpr_mask) * 16);
       }
 #pragma unroll
@@ -119,7 +127,7 @@ __global__ void __launch_bounds__(NT) probe_gather_kernel(const Params p) {
         for (int c = tid; c < SLOT / 16; c += 128) {
           const int64_t r = r0 + (c >> p.cpr_log2);
           const bool v = r < p.n_rows;
-          const int64_t row = v ? __ldg(p.rows + r) : 0;
+          const int64_t row = v ? ids[r - r_begin] : 0;
           cp_async16_hint(dst + c * 16, p.src + row * p.row_stride + (c & cpr_mask) * 16,
                           v ? 16 : 0, pol);
         }
@@ -130,7 +138,7 @@ __global__ void __launch_bounds__(NT) probe_gather_kernel(const Params p) {
         __syncwarp();
         for (int k = lane; k < rows_per_unit; k += 32) {
           const int64_t r = r0 + k;
-          const int64_t row = r < p.n_rows ? __ldg(p.rows + r) : __ldg(p.rows);
+          const int64_t row = r < p.n_rows ? ids[r - r_begin] : ids[0];
           bulk_g2s(dst + k * p.row_bytes, p.src + row * p.row_stride, p.row_bytes, bar);
         }
       }
@@ -179,8 +187,15 @@ extern "C" int sa_probe_gather(const void* src, int64_t row_stride, const int32_
   int lg = 0;
   while ((16 << lg) < row_bytes) ++lg;
   Params p{static_cast<const uint8_t*>(src), rows, n_rows, row_stride, static_cast<int>(row_bytes),
-           method, depth, lg, sink, err};
-  const size_t smem = method == 2 ? 0 : (size_t)depth * SLOT + 2 * MAX_DEPTH * 8 + 128;
+           method, depth, lg, 0, sink, err};
+  // per CTA: its share of the units, rounded up, in indices (4 B each)
+  const int64_t rpu = SLOT / row_bytes;
+  const int64_t units = (n_rows + rpu - 1) / rpu;
+  const int64_t ids_bytes = ((units + ctas - 1) / ctas) * rpu * 4;
+  const size_t ring = method == 2 ? 0 : (size_t)depth * SLOT + 2 * MAX_DEPTH * 8 + 128;
+  p.ids_offset = static_cast<int>(ring);
+  const size_t smem = ring + (size_t)ids_bytes;
+  if (smem > 227 * 1024) return SA_ERR_INVALID_ARG;
   cudaError_t e = cudaFuncSetAttribute(probe_gather_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return SA_ERR_CUDA;
