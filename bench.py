@@ -91,6 +91,9 @@ def parse():
                     help="reftable: the reference's 10-workload table "
                          "(track-01/workloads.py:15-26) through the reference's torch "
                          "oracle, its Triton kernel and this library")
+    ap.add_argument("--kv-policy", type=int, default=-1, choices=[-1, 0, 1, 2],
+                    help="L2 policy of the KV gathers (library option SA_OPT_KV_POLICY): -1 "
+                         "by the call's reuse, 0 evict_first, 1 evict_normal, 2 evict_last")
     ap.add_argument("--graph", action="store_true",
                     help="capture one op call in a CUDA graph and time its replays")
     ap.add_argument("--no-launch-count", action="store_true",
@@ -904,7 +907,7 @@ def run_gather_probe(args):
     total = 128 << 20
     results = []
 
-    def run(row_bytes, method, ctas, depth, pattern, fl, reps=20):
+    def run(row_bytes, method, ctas, depth, pattern, fl, reps=20, total=total):
         n_rows = total // row_bytes
         # "random-l2": rows of a 4 MiB region (the causal config's KV cache), so
         # after the first touches every row comes from L2
@@ -930,9 +933,9 @@ def run_gather_probe(args):
             e1.record(st)
             e1.synchronize()
             ms.append(e0.elapsed_time(e1))
-        med = statistics.median(ms)
+        med = statistics.mean(ms)  # (CUDA events tick in ~2 us steps here: the mean)
         gbs = total / (med / 1e3) / 1e9
-        results.append({"row_bytes": row_bytes, "method": ["cp.async16", "bulk_tma_1d",
+        results.append({"bytes": total, "row_bytes": row_bytes, "method": ["cp.async16", "bulk_tma_1d",
                                                            "ldg_nc16_regs"][method],
                         "ctas": ctas, "depth": depth, "pattern": pattern, "flush": fl,
                         "us": med * 1e3, "gbs": gbs, "frac_of_hbm": gbs / peak})
@@ -951,6 +954,12 @@ def run_gather_probe(args):
     for method in (0, 1, 2):
         run(1024, method, sms, 3, "random-l2", "write+read")
         run(1024, method, 2 * sms, 3, "random-l2", "write+read")
+    # the read ceiling on a long kernel: 1 GiB per call (ramp-up and tail are
+    # then a small share), sequential and random rows, all three forms
+    for pattern in ("sequential", "random"):
+        for method, ctas, depth in ((2, 2 * sms, 3), (2, 4 * sms, 3), (0, 2 * sms, 3),
+                                    (1, 2 * sms, 3)):
+            run(1024, method, ctas, depth, pattern, "write+read", reps=5, total=1 << 30)
     torch.cuda.synchronize()
     ok = int(err.item()) == 0
     best = max((r for r in results if r["pattern"] == "random" and r["row_bytes"] == 1024),
@@ -1054,6 +1063,9 @@ def main():
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
+    if args.kv_policy != -1:
+        from sparse_attn import _lib
+        _lib.set_option(_lib.SA_OPT_KV_POLICY, args.kv_policy)
     variant = {"auto": 0, "mma": 1, "tcgen05": 2, "ws": 3}[args.variant]
     fp8 = args.kv == "fp8"
     flush = L2Flush(dev)
@@ -1123,7 +1135,10 @@ def main():
                    "l2": L2Flush.describe,
                    "variant": "fp8" if fp8 else args.variant, "grid": args.grid,
                    "kv_cache": "e4m3 + fp32 per-token scale" if fp8 else "bf16",
-                   "launch": "CUDA graph replay" if args.graph else "stream launch"},
+                   "launch": "CUDA graph replay" if args.graph else "stream launch",
+                   "kv_l2_policy": "by reuse (evict_first if m*topk < kv_len, else evict_last)"
+                                   if args.kv_policy == -1 else
+                                   ["evict_first", "evict_normal", "evict_last"][args.kv_policy]},
         "gathered_kv_gbs": head["gathered_kv_gbs"],
         "roofline": head["roofline"],
         "cpu_baseline": head["cpu_baseline"],

@@ -175,12 +175,18 @@ int sa_device_status_reset(void);
  *                        the kernel then records its error code, issues no
  *                        more copies, waits for those in flight and returns.
  *                        For testing the failure path; 0 (default) = off.
+ *   SA_OPT_KV_POLICY     L2 policy of the KV row gathers of sa_fwd and
+ *                        sa_fwd_fp8: -1 (default) by the call's reuse
+ *                        (evict_first when m * topk < kv_len, else
+ *                        evict_last), 0 evict_first, 1 evict_normal,
+ *                        2 evict_last.
  * Options are read when a call is made; returns SA_ERR_INVALID_ARG for an
  * unknown option or value.  No counterpart in the reference. */
 #define SA_OPT_ROW_SCHEDULE 1
 #define SA_OPT_INDEXER_TC 2
 #define SA_OPT_SPIN_LIMIT 3
 #define SA_OPT_TEST_STALL 4
+#define SA_OPT_KV_POLICY 5
 int sa_set_option(int option, int64_t value);
 int64_t sa_get_option(int option);
 

@@ -95,6 +95,16 @@ std::atomic<int> g_opt_row_schedule{1};
 std::atomic<int> g_opt_indexer_tc{1};
 std::atomic<uint32_t> g_opt_spin{0};
 std::atomic<int> g_opt_test_stall{0};
+std::atomic<int> g_opt_kv_policy{-1};
+
+// L2 policy of the KV gathers: when the call's rows read each cache row
+// about once (decode, MTP: m * topk < kv_len) the rows are evicted first;
+// when many query rows share the cache (prefill) they are kept (evict_last).
+int kv_policy_for(int64_t m, int64_t topk, int64_t kv_len) {
+  const int o = g_opt_kv_policy.load(std::memory_order_relaxed);
+  if (o >= 0) return o;
+  return m * topk >= kv_len ? 2 : 0;
+}
 
 }  // namespace
 
@@ -103,6 +113,7 @@ bool opt_row_schedule() { return g_opt_row_schedule.load(std::memory_order_relax
 bool opt_indexer_tc() { return g_opt_indexer_tc.load(std::memory_order_relaxed) != 0; }
 uint32_t opt_spin_limit() { return g_opt_spin.load(std::memory_order_relaxed); }
 int opt_test_stall() { return g_opt_test_stall.load(std::memory_order_relaxed); }
+int opt_kv_policy() { return g_opt_kv_policy.load(std::memory_order_relaxed); }
 int reset_ws_error();
 int reset_tc_error();
 int reset_fp8_error();
@@ -129,6 +140,10 @@ int sa_set_option(int option, int64_t value) {
       if (value != 0 && value != 1) return SA_ERR_INVALID_ARG;
       g_opt_test_stall.store(static_cast<int>(value));
       return SA_OK;
+    case SA_OPT_KV_POLICY:
+      if (value < -1 || value > 2) return SA_ERR_INVALID_ARG;
+      g_opt_kv_policy.store(static_cast<int>(value));
+      return SA_OK;
     default:
       return SA_ERR_INVALID_ARG;
   }
@@ -144,6 +159,8 @@ int64_t sa_get_option(int option) {
       return g_opt_spin.load();
     case SA_OPT_TEST_STALL:
       return g_opt_test_stall.load();
+    case SA_OPT_KV_POLICY:
+      return g_opt_kv_policy.load();
     default:
       return -1;
   }
@@ -287,6 +304,7 @@ static int fwd_group(const void* q, const void* kv, const float* sink, const int
   p.scale_log2 = scale * sa::kLog2e;
   p.spin = sa::opt_spin_limit();
   p.test_stall = sa::opt_test_stall();
+  p.kv_policy = kv_policy_for(m, topk, kv_len);
 
   // variant: the tensor-core path whenever its TMA maps can describe the
   // inputs, the warp-MMA path otherwise
@@ -409,6 +427,7 @@ static int fp8_group(const void* q, const void* kv8, const float* kv_scale, cons
   p.scale_log2 = scale * sa::kLog2e;
   p.spin = sa::opt_spin_limit();
   p.test_stall = sa::opt_test_stall();
+  p.kv_policy = kv_policy_for(m, topk, kv_len);
   if (!sa::tc_supports(p)) return SA_ERR_UNSUPPORTED;
   p.upt = ceil_div(topk > 0 ? topk : 1, sa::fp8_unit_keys());
   p.units = b * m * p.upt;

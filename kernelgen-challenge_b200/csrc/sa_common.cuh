@@ -75,6 +75,9 @@ struct Params {
   // wait runs out (the failure-path test, SA_OPT_TEST_STALL).
   uint32_t spin;
   int test_stall;
+  // L2 policy of the KV row gathers: 0 evict_first, 1 evict_normal,
+  // 2 evict_last (l2_policy_kv)
+  int kv_policy;
 };
 
 // Process-wide options (sa_set_option, sa_abi.cu).
@@ -82,6 +85,7 @@ bool opt_row_schedule();
 bool opt_indexer_tc();
 uint32_t opt_spin_limit();
 int opt_test_stall();
+int opt_kv_policy();  // -1: by the call's reuse (sa_abi.cu)
 
 // log2 of the full denominator for a running max m and sum l (relative to m),
 // with the sink as the extra logit; all in the log2 domain.
@@ -228,6 +232,21 @@ __device__ __forceinline__ void cp_async_wait() {
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+  return p;
+}
+
+// L2 policy of the KV row gathers (Params::kv_policy): rows that no other
+// query row of the call will read are best evicted first; rows that many
+// query rows share (prefill: m * topk >= kv_len) are kept.
+__device__ __forceinline__ uint64_t l2_policy_kv(int kv_policy) {
+  uint64_t p;
+  if (kv_policy == 2) {
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(p));
+  } else if (kv_policy == 1) {
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;\n" : "=l"(p));
+  } else {
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+  }
   return p;
 }
 

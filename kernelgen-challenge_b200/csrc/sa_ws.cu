@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(NT, 1)
     // of one row.  The rows land in the 128-byte-swizzled slab layout.  (With
     // half as many issuing threads the gather rate drops by a quarter: issue,
     // not memory, would then bound it.)
-    const uint64_t pol = l2_policy_evict_first();
+    const uint64_t pol = l2_policy_kv(p.kv_policy);
     const int c = tid & 63, par = tid >> 6, j = c >> 3, cc = c & 7;
     int64_t t = t_first, kb = kb_first;
     int64_t tb = t / p.m, tm = t - tb * p.m;
