@@ -1,5 +1,5 @@
 // sa_fp8.cu — sparse_attn over an fp8 (e4m3) KV cache with one fp32 scale per
-// token, for sm_100a.  Same warp-specialized pipeline as sa_ws.cu; every
+// token, for sm_100a.  Same warp-specialized pipeline as sa_ws.cu, but every
 // gathered row is 512 B instead of 1 KiB.
 //
 // Semantics: the bf16 op applied to the dequantised cache
@@ -8,47 +8,45 @@
 // track-01/submission.py:313-322; sink in the denominator only).  The
 // reference has no fp8 cache.  This is the fp8 KV-cache layout variant.
 //
-// Where the work goes: the producer warps gather a unit's 64 e4m3 rows into
-// the upper half of a 64 KiB ring slot, then widen them in place to f16
-// (cvt.f16x2.e4m3x2, exact) in the slab layout of the bf16 kernel, so the
-// consumer warps run the bf16 kernel's MMA loop unchanged except for the
-// operand type.  Widening once per unit in the producers (which otherwise
-// only wait on copies) replaces widening twice per unit in the consumers (K
-// for S, V for P.V), which bounded the earlier form of this kernel.
-//
 // Arithmetic: both products are f16 warp MMAs (mma.sync m16n8k16, fp32
-// accumulate).
-//   Q:   the bf16 Q fragments, scaled per head by a power of two that puts the
-//        head's amax in [2^14, 2^15) and rounded to f16: exact, since f16 has
-//        more mantissa bits than bf16 (values below amax * 2^-28 would lose
-//        bits).
+// accumulate).  The e4m3 K and V values are widened to f16 in registers
+// (cvt.f16x2.e4m3x2, exact) right before each MMA, so shared memory and HBM
+// only ever hold the 1-byte values.  The e4m3 MMA (m16n8k32) was measured
+// here at the same FLOP rate as m16n8k16 (about twice the cycles for twice
+// the work), and it would need Q and P in e4m3.  The f16 path keeps them at
+// full precision for the same tensor time.
+//   Q:   bf16 -> f16 after scaling each head by a power of two that puts its
+//        amax in [2^14, 2^15): exact, since f16 has more mantissa bits than
+//        bf16 (values below amax * 2^-28 would lose bits).
 //   S:   (Q.K8) * 2^-e_h * kscale[key] * scale, fp32.
 //   P:   f16 (11 significant bits).  For V the weights are
 //        Pv = P * kscale[key] / R, where R is a running maximum of the row's
 //        token scales, so Pv <= P <= 2^8.  O is kept in units of R and
 //        rescaled when R grows.
-//   l:   the fp32 sum of P (before rounding), without the token scales: each
-//        thread sums its own keys, reduced over the row at the segment's end.
+//   l:   P . 1 on the same f16 P, without the token scales.
 //
-// Per 64-key unit (32 KiB of gathered rows + 64 scales):
-//   producers  cp.async of the 64 rows (one warp-wide instruction per 512-byte
-//              row) into the slot's upper 32 KiB, rows' 16-byte chunks
-//              XOR-swizzled by (row & 1) * 4; warp 0 writes the validity mask
-//              and the token scales.  One unit later: wait for those copies,
-//              read all 32 KiB into registers (128 threads x 256 B), then write
-//              the f16 rows over the whole slot as 8 slabs of [64 keys x 64
-//              cols] in the 128-byte swizzle; arrive on the slot's full barrier.
-//   consumer c S for keys 16c..16c+15 (64 MMAs), online softmax on the
-//              fragments, Pv to shared memory, O for columns 128c..128c+127
-//              (64 MMAs); row sums in fp32 registers.
+// Per 64-key unit (32 KiB of gathered rows + 64 scales), consumer warp c:
+//   S for keys 16c..16c+15: 2 n-tiles x 32 k16-steps = 64 MMAs.  An ldmatrix
+//     of the e4m3 rows gives each lane columns 4q..4q+3 of one key per 16-column
+//     step.  Widened, they are the lane's two B registers if the k index is
+//     permuted within the step (k 2q,2q+1 <-> columns 4q,4q+1 and k 2q+8,2q+9
+//     <-> 4q+2,4q+3).  Q is stored in shared memory with the same column
+//     permutation, so its ldmatrix A-fragments match.
+//   O for columns 128c..128c+127: 4 k16-steps x 16 n-tiles = 64 MMAs.  The B
+//     fragment of V needs two keys of one column per register; the rows hold
+//     one key's columns.  A lane reads 32-bit words (4 columns) of its keys
+//     2q, 2q+1, 2q+8, 2q+9, pairs the keys bytewise (prmt) and widens each
+//     pair.  So output n-tile j of column group G holds columns 32G + 4n + j,
+//     not 32G + 8j + n: a fixed column permutation, undone at the store.
 //
-// Warp roles (256 threads, one CTA per SM):
-//   warps 0..3   producers (gather, widen)
+// Warp roles (256 threads, one CTA per SM), as in sa_ws.cu:
+//   warps 0..3   producer: cp.async of 64 rows x 512 B per unit (each warp-wide
+//                instruction reads one row) into a 5-deep ring; warp 0 also
+//                writes the unit's validity mask, token scales and their max
 //   warps 4..7   consumers; consumer thread 0 refills the bf16 Q tile by TMA
 //
 // Every mbarrier wait is bounded; on a timeout the CTA records an error code
-// in sa_fp8_error (readable through sa_device_status), issues no more copies,
-// waits for those in flight and returns.
+// in sa_fp8_error (readable through sa_device_status) and stops issuing work.
 #include <type_traits>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -64,32 +62,31 @@ namespace fp8_path {
 using namespace tc;
 
 constexpr int UK = 64;                      // keys per unit
-constexpr int NSLOT = 3;                    // ring depth (units)
+constexpr int NSLOT = 5;                    // ring depth (units)
 constexpr int ROW_BYTES = kDim;             // one e4m3 row
-constexpr int SLOT_BYTES = UK * kDim * 2;   // 64 KiB: the unit's rows widened to f16
-constexpr int STAGE_OFF = SLOT_BYTES / 2;   // e4m3 rows land in the slot's upper half
-constexpr int SLAB_BYTES = UK * 128;        // [64 keys x 64 cols] f16 = 8 KiB
-constexpr int Q_BYTES = kHeads * kDim * 2;  // 16 KiB bf16 TMA tile
+constexpr int SLOT_BYTES = UK * ROW_BYTES;  // 32 KiB
+constexpr int Q_BYTES = kHeads * kDim * 2;  // 16 KiB (bf16 TMA tile, f16 MMA tile)
+constexpr int QH_ROW = kDim * 2;            // f16 Q row: 1 KiB
 constexpr int PT_BYTES = kHeads * UK * 2;   // 2 KiB f16 P tile [head][key]
 constexpr int NCW = 4;                      // consumer warps
 constexpr int NCT = NCW * 32;
 constexpr int NT = 4 * 32 + NCT;            // 256
 constexpr float kRescaleThreshold = 8.0f;   // log2 domain: P <= 2^8
 constexpr float kE4m3Max = 448.0f;
+constexpr uint32_t kOnesF16 = 0x3C003C00u;  // f16 pair (1, 1)
 
 struct __align__(1024) Smem {
-  uint8_t ring[NSLOT][SLOT_BYTES];  // f16 slabs (e4m3 staging in the upper half until widened)
+  uint8_t ring[NSLOT][SLOT_BYTES];  // rows of 512 B, 16-byte chunks swizzled by row
   uint8_t q[Q_BYTES];               // bf16 Q: 8 TMA boxes [16 heads][64 cols], 128-byte swizzle
+  uint8_t qh[Q_BYTES];              // f16 Q [16][512], columns permuted per 16, rows swizzled
+  uint8_t pl[PT_BYTES];             // f16 P for the row sums
   uint8_t pv[PT_BYTES];             // f16 P * kscale / R for P.V
   float kscale[NSLOT][UK];          // token scales of the unit (0 for masked slots)
   float kmax[NSLOT];                // their maximum
   uint32_t mask[NSLOT][2];          // validity: [0] keys 2l, [1] keys 2l+1 (bit l)
   float red_max[NCW][kHeads];
-  float red_sum[NCW][kHeads];  // per-warp row sums at a segment's end
-  float qscale[NCW][kHeads];   // per warp: 2^-e_h * scale * log2(e) of this row's heads
-  float rscale[NCW][2];        // per warp: R and 1 / R (running max of the token scales)
-  // full: the unit is widened (128 producer arrivals); empty: the four
-  // consumer warps finished the unit; q_full: next row's Q
+  // full: rows landed (128 cp.async arrivals + warp 0's release arrival);
+  // empty: the four consumer warps finished the unit; q_full: next row's Q
   uint64_t full[NSLOT], empty[NSLOT], q_full;
   int err;
   uint32_t spin;  // polls before a wait gives up
@@ -117,17 +114,19 @@ __device__ __forceinline__ bool wait_or_err(Smem& S, uint64_t& bar, uint32_t par
   return false;
 }
 
-// e4m3 staging: 16-byte chunk ch (0..31) of row r, XOR-swizzled by (r & 1) * 4
-// so that the widening reads (two rows x four chunks per quarter-warp) hit
-// eight different bank groups.
-__device__ __forceinline__ uint32_t stage_chunk(int r, int ch) {
-  return STAGE_OFF + r * ROW_BYTES + ((ch ^ ((r & 1) << 2)) << 4);
+// Byte offset of 16-byte chunk `ch` (0..31) of gathered row `r` in a slot:
+// chunks XOR-swizzled by r & 7, so ldmatrix of 8 consecutive rows at one chunk
+// and the V reads of rows 2i + d (i = 0..3) at one chunk pair are both
+// conflict-free.
+__device__ __forceinline__ uint32_t row_chunk(int r, int ch) {
+  return r * ROW_BYTES + ((ch ^ (r & 7)) << 4);
 }
 
-// f16 slab layout (as the bf16 kernel's): columns 64s..64s+63 of key r in slab
-// s, 16-byte chunk j (columns 64s + 8j..+7) at j ^ (r & 7).
-__device__ __forceinline__ uint32_t slab_chunk(int r, int s, int j) {
-  return s * SLAB_BYTES + r * 128 + ((j ^ (r & 7)) << 4);
+// f16 Q tile: row h (1 KiB), 16-byte chunk ch (0..63) swizzled by h & 7.
+// Chunk 2j holds columns 16j + 4i + {0,1} and chunk 2j+1 columns
+// 16j + 4i + {2,3} (i = 0..3, two f16 each).
+__device__ __forceinline__ uint32_t qh_chunk(int h, int ch) {
+  return h * QH_ROW + ((ch ^ (h & 7)) << 4);
 }
 
 // f16 P tile: row h (128 B), chunk ch = keys 8ch..8ch+7, swizzled by h & 7.
@@ -165,43 +164,29 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// bf16 pair -> f16 pair after scaling both by s (a power of two).
-__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w, float s) {
-  const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
-  return pack_f16x2(f.x * s, f.y * s);
-}
-
-__device__ __forceinline__ float2 lds64f(uint32_t addr) {
-  float2 v;
-  asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];\n" : "=f"(v.x), "=f"(v.y) : "r"(addr));
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];\n" : "=r"(v) : "r"(addr));
   return v;
 }
 
-__device__ __forceinline__ uint4 lds128(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr));
-  return v;
+__device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(addr), "r"(v));
 }
 
-__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
-                                       uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c),
-               "r"(d)
-               : "memory");
+// Four bf16 of the TMA Q tile: head h, columns col..col+3 (col % 4 == 0).
+__device__ __forceinline__ float4 q_four(uint32_t qbase, int h, int col) {
+  const int box = col >> 6, cb = col & 63;
+  const uint32_t addr = qbase + box * 2048 + h * 128 + (((cb >> 3) ^ (h & 7)) << 4) + (cb & 7) * 2;
+  uint32_t w0, w1;
+  asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];\n" : "=r"(w0), "=r"(w1) : "r"(addr));
+  const float2 a = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w0));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w1));
+  return make_float4(a.x, a.y, b.x, b.y);
 }
 
 // 2^e as a float for e in [-126, 127].
 __device__ __forceinline__ float exp2i(int e) { return __int_as_float((127 + e) << 23); }
-
-// e such that amax * 2^e lies in [2^14, 2^15) (amax = f * 2^E, f in [0.5, 1):
-// e = 15 - E), clamped to the normal range; 0 for amax == 0.
-__device__ __forceinline__ int head_exp(float a) {
-  const int E = ((__float_as_int(a) >> 23) & 0xff) - 126;
-  const int e = a > 0.f ? 15 - E : 0;
-  return e < -126 ? -126 : (e > 126 ? 126 : e);
-}
 
 struct Cursor {
   int64_t kb, tb, tm;
@@ -215,46 +200,6 @@ struct Cursor {
     }
   }
 };
-
-// Widening of one unit by the 128 producer threads, after its copies landed.
-// Half h (e4m3 chunks 16h..16h+15, f16 slabs 4h..4h+3) in steps k = 0..7:
-// row pair rp = 4k + warp (rows 2rp, 2rp + 1); lane l takes row
-// 2rp + ((l & 7) >> 2) and chunk 16h + 4(l >> 3) + (l & 3).  Each quarter-warp
-// then reads two rows x four chunks and writes two rows x four chunk pairs,
-// both without bank conflicts.  The f16 slabs of half 0 lie below the staging
-// area, so half 0 is widened straight through; half 1's slabs overwrite the
-// staging rows, so all of half 1 is read (barrier) before its first write.
-__device__ __forceinline__ void widen_half(uint32_t slot_base, int warp, int lane, int h,
-                                           bool in_place) {
-  uint4 v[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int r = 2 * (4 * k + warp) + ((lane & 7) >> 2);
-    const int ch = 16 * h + 4 * (lane >> 3) + (lane & 3);
-    v[k] = lds128(slot_base + stage_chunk(r, ch));
-  }
-  if (in_place) named_bar(7, 128);
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int r = 2 * (4 * k + warp) + ((lane & 7) >> 2);
-    const int ch = 16 * h + 4 * (lane >> 3) + (lane & 3);
-    // e4m3 columns 16ch..16ch+15 -> f16 columns of slab ch >> 2, chunks
-    // 2(ch & 3) and 2(ch & 3) + 1
-    uint32_t f[8];
-    widen4(v[k].x, f[0], f[1]);
-    widen4(v[k].y, f[2], f[3]);
-    widen4(v[k].z, f[4], f[5]);
-    widen4(v[k].w, f[6], f[7]);
-    const int sl = ch >> 2, j = 2 * (ch & 3);
-    sts128(slot_base + slab_chunk(r, sl, j), f[0], f[1], f[2], f[3]);
-    sts128(slot_base + slab_chunk(r, sl, j + 1), f[4], f[5], f[6], f[7]);
-  }
-}
-
-__device__ __forceinline__ void widen_unit(uint32_t slot_base, int warp, int lane) {
-  widen_half(slot_base, warp, lane, 0, false);
-  widen_half(slot_base, warp, lane, 1, true);
-}
 
 // kRows: the row schedule of sa_common.cuh (whole rows in snake order, each
 // up to its last valid slot) instead of contiguous unit ranges.
@@ -285,7 +230,7 @@ __global__ void __launch_bounds__(NT, 1)
 
   if (tid == 0) {
     for (int s = 0; s < NSLOT; ++s) {
-      mbar_init(smem_u32(&S.full[s]), 128);
+      mbar_init(smem_u32(&S.full[s]), 128 + 1);
       mbar_init(smem_u32(&S.empty[s]), NCW);
     }
     mbar_init(smem_u32(&S.q_full), 1);
@@ -297,7 +242,7 @@ __global__ void __launch_bounds__(NT, 1)
   }
   if (warp == 4 && lane == 0) tma_prefetch_desc(&q_map);
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  if constexpr (kRows) {
+  if constexpr (kRows) {  // units of this CTA, all row counts loaded at once
     __syncthreads();      // (S.n_units initialised)
     int part = 0;
     for (int64_t k = tid;; k += NT) {
@@ -313,12 +258,11 @@ __global__ void __launch_bounds__(NT, 1)
   if constexpr (kRows) n = S.n_units;
 
   if (warp < 4) {
-    // ------------------------------------------------------------ producers
+    // ------------------------------------------------------------ producer
     // Warp w copies rows w, w+4, ..., w+60 of each unit; lane = 16-byte chunk,
     // so one warp-wide cp.async reads one 512-byte row.  Indices run two
     // units ahead and warp 0's token scales one unit ahead, so neither
-    // dependent global load stalls the copy issue.  Unit i's copies form
-    // cp.async group i; unit i - 1 is widened right after group i is issued.
+    // dependent global load stalls the copy issue.
     const uint64_t pol = l2_policy_kv(p.kv_policy);
     const uint8_t* kv8 = reinterpret_cast<const uint8_t*>(p.kv);
     auto load_ids = [&](const auto& cu, int32_t& a, int32_t& b) {
@@ -346,20 +290,6 @@ __global__ void __launch_bounds__(NT, 1)
         cu.advance(upt, p.m);
       }
     };
-    // widen unit j (its copies are group j; at most `pending` younger groups)
-    // and release it to the consumers
-    auto finish_unit = [&](int j, bool newest) {
-      if (newest) {
-        cp_async_wait<0>();
-      } else {
-        cp_async_wait<1>();
-      }
-      named_bar(6, 128);  // every producer's copies of unit j have landed
-      widen_unit(smem_u32(S.ring[j % NSLOT]), warp, lane);
-      // (failure-path test: one arrival of the first unit is withheld, so the
-      // consumers' wait on it runs out)
-      if (!(p.test_stall && j == 0 && tid == 0)) mbar_arrive(smem_u32(&S.full[j % NSLOT]));
-    };
     int32_t xa0, xb0, xa1 = -1, xb1 = -1;  // indices of units i and i+1
     int64_t tb0 = cu.tb, tb1 = cu.tb;
     float sa0 = 0.f, sb0 = 0.f;           // scales of unit i (warp 0)
@@ -386,53 +316,56 @@ __global__ void __launch_bounds__(NT, 1)
 
       const int slot = i % NSLOT;
       const bool ok = i < NSLOT || wait_or_err(S, S.empty[slot], ((i / NSLOT) - 1) & 1, 1);
-      // one decision for all four producer warps: they widen together
-      if (!named_bar_or(8, 128, !ok)) {
-        const uint8_t* kvb = kv8 + cur_tb * p.kv_sb + lane * 16;
-        const uint32_t dst0 = smem_u32(S.ring[slot]);
-        const int32_t mine = (warp & 1) ? ib : ia;  // rows of this warp have parity warp & 1
+      if (!__all_sync(0xffffffffu, ok)) continue;
+      const uint8_t* kvb = kv8 + cur_tb * p.kv_sb + lane * 16;
+      const uint32_t dst0 = smem_u32(S.ring[slot]);
+      const int32_t mine = (warp & 1) ? ib : ia;  // rows of this warp have parity warp & 1
 #pragma unroll 8
-        for (int k = 0; k < UK / 4; ++k) {
-          const int r = warp + 4 * k;
-          const int32_t id = __shfl_sync(0xffffffffu, mine, r >> 1);
-          const bool v = valid(id);
-          cp_async16_hint(dst0 + stage_chunk(r, lane), kvb + (v ? (int64_t)id : 0) * p.kv_sn,
-                          v ? 16 : 0, pol);
-        }
-        if (warp == 0) {
-          const uint32_t ma = __ballot_sync(0xffffffffu, valid(ia));
-          const uint32_t mb = __ballot_sync(0xffffffffu, valid(ib));
-          const uint32_t fa = __ballot_sync(0xffffffffu, index_fault(ia, p.kv_len));
-          const uint32_t fb = __ballot_sync(0xffffffffu, index_fault(ib, p.kv_len));
-          *reinterpret_cast<float2*>(&S.kscale[slot][2 * lane]) = make_float2(fsa, fsb);
-          float km = fmaxf(fsa, fsb);
-#pragma unroll
-          for (int off = 16; off >= 1; off >>= 1)
-            km = fmaxf(km, __shfl_xor_sync(0xffffffffu, km, off));
-          if (lane == 0) {
-            S.mask[slot][0] = ma;
-            S.mask[slot][1] = mb;
-            S.kmax[slot] = km;
-            count_index_faults(&sa_fp8_index_faults, __popc(fa) + __popc(fb));
-          }
-        }
+      for (int k = 0; k < UK / 4; ++k) {
+        const int r = warp + 4 * k;
+        const int32_t id = __shfl_sync(0xffffffffu, mine, r >> 1);
+        const bool v = valid(id);
+        cp_async16_hint(dst0 + row_chunk(r, lane), kvb + (v ? (int64_t)id : 0) * p.kv_sn,
+                        v ? 16 : 0, pol);
       }
-      cp_async_commit();  // group i (empty after an error)
-      if (i > 0) finish_unit(i - 1, false);
+      cp_async_mbar_arrive_noinc(smem_u32(&S.full[slot]));
+      if (warp == 0) {
+        const uint32_t ma = __ballot_sync(0xffffffffu, valid(ia));
+        const uint32_t mb = __ballot_sync(0xffffffffu, valid(ib));
+        const uint32_t fa = __ballot_sync(0xffffffffu, index_fault(ia, p.kv_len));
+        const uint32_t fb = __ballot_sync(0xffffffffu, index_fault(ib, p.kv_len));
+        *reinterpret_cast<float2*>(&S.kscale[slot][2 * lane]) = make_float2(fsa, fsb);
+        float km = fmaxf(fsa, fsb);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) km = fmaxf(km, __shfl_xor_sync(0xffffffffu, km, off));
+        if (lane == 0) {
+          S.mask[slot][0] = ma;
+          S.mask[slot][1] = mb;
+          S.kmax[slot] = km;
+          count_index_faults(&sa_fp8_index_faults, __popc(fa) + __popc(fb));
+        }
+        __syncwarp();
+        // release: the slot's full barrier also counts this arrival, made
+        // after every lane's scale and mask writes
+        // (failure-path test: the first slot's release is withheld, so the
+        // consumers' wait on it runs out)
+        if (lane == 0 && !(p.test_stall && i == 0)) mbar_arrive(smem_u32(&S.full[slot]));
+      }
     }
-    if (n > 0) finish_unit(n - 1, true);
     cp_async_wait<0>();
   } else {
     // ------------------------------------------------------------ consumers
     const int c = warp - 4;                   // 0..3
     const int tt = tid - 128;                 // consumer thread 0..127
     const int g8 = lane >> 2, q4 = lane & 3;  // mma fragment coordinates
-    const uint32_t qbase = smem_u32(S.q);
-    const uint32_t pvbase = smem_u32(S.pv);
+    const int mtx = lane >> 3;                // ldmatrix: matrix whose row address this lane gives
+    const uint32_t qbase = smem_u32(S.q), qhbase = smem_u32(S.qh);
+    const uint32_t plbase = smem_u32(S.pl), pvbase = smem_u32(S.pv);
+    float qs_lo = 0.f, qs_hi = 0.f;  // 2^-e * scale * log2(e), heads g8 / g8+8
     float m_lo = -INFINITY, m_hi = -INFINITY;  // running max (log2 domain)
-    uint32_t qf[32][4];              // f16 Q A-fragments, 32 k-steps of 16 columns
-    float o[16][4];  // O / R: heads g8, g8+8, columns 128c + 8nt + 2q4 + {0,1}
-    float l_lo = 0.f, l_hi = 0.f;  // this thread's share of the row sums, heads g8 / g8+8
+    float R = 0.f, invR = 0.f;       // running max of the token scales seen
+    float o[16][4];  // O / R; n-tile 4G+j: heads g8, g8+8, columns 128c+32G+8q4+{j, 4+j}
+    float lacc[4];   // running row sums: [0] head g8, [2] head g8+8
     // Q loads issued by consumer thread 0; after an error none is issued, and
     // the one possibly in flight is waited for before the CTA exits.
     int q_issued = 0;
@@ -460,108 +393,138 @@ __global__ void __launch_bounds__(NT, 1)
       const bool seg_end = (i == n - 1) || kb == nu_t - 1;
       if (seg_first) {
         m_lo = m_hi = -INFINITY;
-        if (lane == 0) S.rscale[c][0] = S.rscale[c][1] = 0.f;  // R, 1 / R: in shared
-        // memory, read back per unit (registers are short in the main loop)
+        R = invR = 0.f;
         seg_kb0 = kb;
         wait_or_err(S, S.q_full, seg & 1, 7);
-        // This row's Q fragments (bf16, as the bf16 kernel loads them); the
-        // four lanes of a fragment row hold all 512 columns of heads g8 and
-        // g8 + 8 between them, so the per-head amax is a two-step shuffle.
-        {
-          const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
-#pragma unroll
-          for (int ks = 0; ks < 32; ++ks) {
-            const int ch = (ks & 3) * 2 + (lane >> 4);
-            ldmatrix_x4(qf[ks], qbase + (ks >> 2) * 2048 + row * 128 + ((ch ^ (row & 7)) << 4));
-          }
-        }
-        named_bar(4, NCT);  // every consumer holds the fragments: the tile is free
-        if constexpr (kRows) {
-          const int64_t tn = snake_row(sk + 1, g, G, nrows);
-          if (tt == 0 && tn >= 0) issue_q(tn);
-        } else if (tt == 0 && t < t_last) {
-          issue_q(t + 1);
-        }
+        // This row's Q as f16: warp c converts columns 128c..128c+127 (lane:
+        // columns 16j + 4q4..+3 of heads g8, g8+8), after a per-head amax over
+        // all four warps' columns.  Once per row: loops kept rolled.
         float a_lo = 0.f, a_hi = 0.f;
-#pragma unroll
-        for (int ks = 0; ks < 32; ++ks) {
-          // a[0], a[2]: head g8; a[1], a[3]: head g8 + 8 (bf16 pairs)
-          const uint32_t m0 = (qf[ks][0] & 0x7fff7fffu), m2 = (qf[ks][2] & 0x7fff7fffu);
-          const uint32_t m1 = (qf[ks][1] & 0x7fff7fffu), m3 = (qf[ks][3] & 0x7fff7fffu);
-          a_lo = fmaxf(a_lo, fmaxf(fmaxf(__uint_as_float(m0 << 16), __uint_as_float(m0 & 0xffff0000u)),
-                                   fmaxf(__uint_as_float(m2 << 16), __uint_as_float(m2 & 0xffff0000u))));
-          a_hi = fmaxf(a_hi, fmaxf(fmaxf(__uint_as_float(m1 << 16), __uint_as_float(m1 & 0xffff0000u)),
-                                   fmaxf(__uint_as_float(m3 << 16), __uint_as_float(m3 & 0xffff0000u))));
+#pragma unroll 1
+        for (int j = 8 * c; j < 8 * c + 8; ++j) {
+          const float4 u = q_four(qbase, g8, 16 * j + 4 * q4);
+          const float4 v = q_four(qbase, g8 + 8, 16 * j + 4 * q4);
+          a_lo = fmaxf(a_lo, fmaxf(fmaxf(fabsf(u.x), fabsf(u.y)), fmaxf(fabsf(u.z), fabsf(u.w))));
+          a_hi = fmaxf(a_hi, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
         }
 #pragma unroll
         for (int off = 1; off <= 2; off <<= 1) {
           a_lo = fmaxf(a_lo, __shfl_xor_sync(0xffffffffu, a_lo, off));
           a_hi = fmaxf(a_hi, __shfl_xor_sync(0xffffffffu, a_hi, off));
         }
+        if (q4 == 0) {
+          S.red_max[c][g8] = a_lo;
+          S.red_max[c][g8 + 8] = a_hi;
+        }
+        named_bar(5, NCT);
+#pragma unroll
+        for (int w = 0; w < NCW; ++w) {
+          a_lo = fmaxf(a_lo, S.red_max[w][g8]);
+          a_hi = fmaxf(a_hi, S.red_max[w][g8 + 8]);
+        }
+        // e: amax * 2^e in [2^14, 2^15) (amax = f * 2^E, f in [0.5, 1): e = 15 - E)
+        auto head_exp = [](float a) {
+          const int E = ((__float_as_int(a) >> 23) & 0xff) - 126;
+          const int e = a > 0.f ? 15 - E : 0;
+          return e < -126 ? -126 : (e > 126 ? 126 : e);
+        };
         const int e_lo = head_exp(a_lo), e_hi = head_exp(a_hi);
         const float s_lo = exp2i(e_lo), s_hi = exp2i(e_hi);
-        if (q4 == 0) {  // read back per unit (registers are short in the main loop)
-          S.qscale[c][g8] = exp2i(-e_lo) * p.scale_log2;
-          S.qscale[c][g8 + 8] = exp2i(-e_hi) * p.scale_log2;
+        qs_lo = exp2i(-e_lo) * p.scale_log2;
+        qs_hi = exp2i(-e_hi) * p.scale_log2;
+#pragma unroll 1
+        for (int j = 8 * c; j < 8 * c + 8; ++j) {
+          const float4 u = q_four(qbase, g8, 16 * j + 4 * q4);
+          const float4 v = q_four(qbase, g8 + 8, 16 * j + 4 * q4);
+          sts32(qhbase + qh_chunk(g8, 2 * j) + 4 * q4, pack_f16x2(u.x * s_lo, u.y * s_lo));
+          sts32(qhbase + qh_chunk(g8, 2 * j + 1) + 4 * q4, pack_f16x2(u.z * s_lo, u.w * s_lo));
+          sts32(qhbase + qh_chunk(g8 + 8, 2 * j) + 4 * q4, pack_f16x2(v.x * s_hi, v.y * s_hi));
+          sts32(qhbase + qh_chunk(g8 + 8, 2 * j + 1) + 4 * q4, pack_f16x2(v.z * s_hi, v.w * s_hi));
         }
-        __syncwarp();
-#pragma unroll
-        for (int ks = 0; ks < 32; ++ks) {
-          qf[ks][0] = bf16x2_to_f16x2(qf[ks][0], s_lo);
-          qf[ks][1] = bf16x2_to_f16x2(qf[ks][1], s_hi);
-          qf[ks][2] = bf16x2_to_f16x2(qf[ks][2], s_lo);
-          qf[ks][3] = bf16x2_to_f16x2(qf[ks][3], s_hi);
+        // the f16 tile is complete and the bf16 tile free for the next row.
+        // (The previous row's f16 tile reads all came before the previous
+        // unit's vote barrier; its red_max reads before its P barrier.)
+        named_bar(4, NCT);
+        if constexpr (kRows) {
+          const int64_t tn = snake_row(sk + 1, g, G, nrows);
+          if (tt == 0 && tn >= 0) issue_q(tn);
+        } else if (tt == 0 && t < t_last) {
+          issue_q(t + 1);
         }
 #pragma unroll
         for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
-        l_lo = l_hi = 0.f;
+        lacc[0] = lacc[1] = lacc[2] = lacc[3] = 0.f;
       }
       const int slot = i % NSLOT;
       wait_or_err(S, S.full[slot], (i / NSLOT) & 1, 8);
       const uint32_t sb = smem_u32(S.ring[slot]);
 
-      // ---- S for keys 16c + 8nt + {0..7}: 2 n-tiles x 32 k-steps, 2-way split
+      // ---- S for keys 16c + 8nt + {0..7}: [nt][0] even k-steps, [nt][1] odd
       float sa[2][2][4];
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int z = 0; z < 2; ++z) sa[nt][z][0] = sa[nt][z][1] = sa[nt][z][2] = sa[nt][z][3] = 0.f;
+      {
+        // K: rows 16c + 8nt + (lane & 7), chunk 4J + mtx gives k16-step 4J + mtx.
+        // (4J + mtx) ^ (lane & 7) = 8 (J >> 1) + ((4 (J & 1) + mtx) ^ (lane & 7)).
+        uint32_t koff[2][2];
 #pragma unroll
-      for (int kp = 0; kp < 16; ++kp) {  // k-steps 2kp, 2kp+1: columns 32kp..32kp+31
-        const int slab = kp >> 1, c0 = (kp & 1) * 4;
+        for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const int key = 16 * c + 8 * nt + (lane & 7);
-          uint32_t kf[4];
-          ldmatrix_x4(kf, sb + slab * SLAB_BYTES + key * 128 + (((c0 + (lane >> 3)) ^ (key & 7)) << 4));
-          mma_f16(sa[nt][0], qf[2 * kp], kf[0], kf[1]);
-          mma_f16(sa[nt][1], qf[2 * kp + 1], kf[2], kf[3]);
-        }
+          for (int jo = 0; jo < 2; ++jo)
+            koff[nt][jo] = sb + (16 * c + 8 * nt + (lane & 7)) * ROW_BYTES +
+                           (((4 * jo + mtx) ^ (lane & 7)) << 4);
+        // Q: row (lane & 7) + 8 (mtx & 1), chunk 2ks + (mtx >> 1); for ks = 4J + kk
+        // the chunk is 8J + (2kk + (mtx >> 1)) and only the low part is swizzled.
+        uint32_t qoff[4];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          qoff[kk] = qhbase + ((lane & 7) + 8 * (mtx & 1)) * QH_ROW +
+                     (((2 * kk + (mtx >> 1)) ^ (lane & 7)) << 4);
+#pragma unroll
+        for (int J2 = 0; J2 < 4; ++J2)
+#pragma unroll
+          for (int jo = 0; jo < 2; ++jo) {  // J = 2 J2 + jo: k16-steps 4J..4J+3
+            uint32_t kf[2][4];
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) ldmatrix_x4(kf[nt], koff[nt][jo] + (J2 << 7));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              uint32_t qa[4];
+              ldmatrix_x4(qa, qoff[kk] + (J2 << 8) + (jo << 7));
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt) {
+                uint32_t b0, b1;
+                widen4(kf[nt][kk], b0, b1);
+                mma_f16(sa[nt][kk & 1], qa, b0, b1);
+              }
+            }
+          }
       }
       // ---- softmax on the fragments: x[nt][0,1] head g8, x[nt][2,3] head g8+8,
       //      keys 16c + 8nt + 2q4 + {0,1}
       const uint32_t mw0 = S.mask[slot][0], mw1 = S.mask[slot][1];
-      const float qs_lo = S.qscale[c][g8], qs_hi = S.qscale[c][g8 + 8];
+      float2 ks[2];
       float x[2][4];
       bool over = false;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
         const int key = 16 * c + 8 * nt + 2 * q4;
-        const int l = key >> 1;  // producer lane that loaded this key pair
-        const float2 ks = lds64f(smem_u32(&S.kscale[slot][key]));
+        const int l = key >> 1;  // mask bit of this key pair
+        ks[nt] = *reinterpret_cast<const float2*>(&S.kscale[slot][key]);
         const bool v0 = (mw0 >> l) & 1u, v1 = (mw1 >> l) & 1u;
-        x[nt][0] = v0 ? (sa[nt][0][0] + sa[nt][1][0]) * qs_lo * ks.x : -INFINITY;
-        x[nt][1] = v1 ? (sa[nt][0][1] + sa[nt][1][1]) * qs_lo * ks.y : -INFINITY;
-        x[nt][2] = v0 ? (sa[nt][0][2] + sa[nt][1][2]) * qs_hi * ks.x : -INFINITY;
-        x[nt][3] = v1 ? (sa[nt][0][3] + sa[nt][1][3]) * qs_hi * ks.y : -INFINITY;
+        x[nt][0] = v0 ? (sa[nt][0][0] + sa[nt][1][0]) * qs_lo * ks[nt].x : -INFINITY;
+        x[nt][1] = v1 ? (sa[nt][0][1] + sa[nt][1][1]) * qs_lo * ks[nt].y : -INFINITY;
+        x[nt][2] = v0 ? (sa[nt][0][2] + sa[nt][1][2]) * qs_hi * ks[nt].x : -INFINITY;
+        x[nt][3] = v1 ? (sa[nt][0][3] + sa[nt][1][3]) * qs_hi * ks[nt].y : -INFINITY;
         over |= fmaxf(x[nt][0], x[nt][1]) > m_lo + kRescaleThreshold;
         over |= fmaxf(x[nt][2], x[nt][3]) > m_hi + kRescaleThreshold;
       }
+      const float kmax = S.kmax[slot];  // the same in every thread
       // The vote barrier also orders this unit's P writes after every warp's
       // P.V of the previous unit (single pair of P tiles).
       const bool vote = named_bar_or(1, NCT, over);
-      const float kmax = S.kmax[slot];  // the same in every thread
-      float R = S.rscale[c][0], invR = S.rscale[c][1];
       if (vote || kmax > R) {
         float b_lo = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
         float b_hi = fmaxf(fmaxf(x[0][2], x[0][3]), fmaxf(x[1][2], x[1][3]));
@@ -589,11 +552,6 @@ __global__ void __launch_bounds__(NT, 1)
         const float fr = Rn > 0.f ? R / Rn : 0.f;  // O is kept in units of R
         R = Rn;
         invR = R > 0.f ? 1.f / R : 0.f;
-        __syncwarp();
-        if (lane == 0) {
-          S.rscale[c][0] = R;
-          S.rscale[c][1] = invR;
-        }
         const float o_lo = c_lo * fr, o_hi = c_hi * fr;
 #pragma unroll
         for (int nt = 0; nt < 16; ++nt) {
@@ -602,8 +560,10 @@ __global__ void __launch_bounds__(NT, 1)
           o[nt][2] *= o_hi;
           o[nt][3] *= o_hi;
         }
-        l_lo *= c_lo;
-        l_hi *= c_hi;
+        lacc[0] *= c_lo;
+        lacc[1] *= c_lo;
+        lacc[2] *= c_hi;
+        lacc[3] *= c_hi;
       }
       {
         const float base_lo = (m_lo == -INFINITY) ? 0.f : m_lo;
@@ -612,87 +572,101 @@ __global__ void __launch_bounds__(NT, 1)
         for (int nt = 0; nt < 2; ++nt) {
           const float p0 = exp2f(x[nt][0] - base_lo), p1 = exp2f(x[nt][1] - base_lo);
           const float p2 = exp2f(x[nt][2] - base_hi), p3 = exp2f(x[nt][3] - base_hi);
-          // the token scales again, from shared memory (not held across the vote)
-          const float2 ks = lds64f(smem_u32(&S.kscale[slot][16 * c + 8 * nt + 2 * q4]));
-          const float w0 = ks.x * invR, w1 = ks.y * invR;
+          const float w0 = ks[nt].x * invR, w1 = ks[nt].y * invR;
           const uint32_t off_lo = p_chunk(g8, 2 * c + nt) + 4 * q4;
           const uint32_t off_hi = p_chunk(g8 + 8, 2 * c + nt) + 4 * q4;
-          l_lo += p0 + p1;
-          l_hi += p2 + p3;
-          *reinterpret_cast<uint32_t*>(S.pv + off_lo) = pack_f16x2(p0 * w0, p1 * w1);
-          *reinterpret_cast<uint32_t*>(S.pv + off_hi) = pack_f16x2(p2 * w0, p3 * w1);
+          sts32(plbase + off_lo, pack_f16x2(p0, p1));
+          sts32(plbase + off_hi, pack_f16x2(p2, p3));
+          sts32(pvbase + off_lo, pack_f16x2(p0 * w0, p1 * w1));
+          sts32(pvbase + off_hi, pack_f16x2(p2 * w0, p3 * w1));
         }
       }
       named_bar(3, NCT);  // P of all 64 keys written
 
-      // ---- O[16 x 128 cols of this warp] += Pv[16 x 64] . V[64 x 128]
+      // ---- O[16 x 128 cols of this warp] += Pv[16 x 64] . V[64 x 128]; l += Pl . 1
+      // V words: rows r = 16s + 2q4 + d (d in {0, 1, 8, 9}), chunk
+      // ch = 8c + 2Gp + (g8 >> 2), byte 4 (g8 & 3).  With r & 7 = 2q4 + (d & 1)
+      // the physical chunk is 8c + 2 (Gp ^ q4) + ((g8 >> 2) ^ (d & 1)): one base
+      // register per (d & 1, Gp), the row offset an immediate.
+      uint32_t vb[2][4];
 #pragma unroll
-      for (int kst = 0; kst < 4; ++kst) {
-        uint32_t pa[4];
-        {
-          const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
-          ldmatrix_x4(pa, pvbase + p_chunk(row, 2 * kst + (lane >> 4)));
-        }
-        const int kr = kst * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      for (int d1 = 0; d1 < 2; ++d1)
 #pragma unroll
-        for (int np = 0; np < 8; ++np) {
-          const int slab = 2 * c + (np >> 2);
-          const int ch = ((np & 3) << 1) + (lane >> 4);
-          uint32_t vb[4];
-          ldmatrix_x4_trans(vb, sb + slab * SLAB_BYTES + kr * 128 + ((ch ^ (kr & 7)) << 4));
-          mma_f16(o[2 * np], pa, vb[0], vb[1]);
-          mma_f16(o[2 * np + 1], pa, vb[2], vb[3]);
+        for (int Gp = 0; Gp < 4; ++Gp)
+          vb[d1][Gp] = sb + 2 * q4 * ROW_BYTES +
+                       ((8 * c + 2 * (Gp ^ q4) + ((g8 >> 2) ^ d1)) << 4) + 4 * (g8 & 3);
+#pragma unroll 1
+      for (int s = 0; s < 4; ++s) {  // keys 16s..16s+15 (rolled: bounded loads in flight)
+        uint32_t pa[4], pl[4];
+        // A-fragments of P for keys 16s..16s+15: chunk 2s + (mtx >> 1)
+        const uint32_t pch = p_chunk((lane & 7) + 8 * (mtx & 1), 2 * s + (mtx >> 1));
+        ldmatrix_x4(pl, plbase + pch);
+        ldmatrix_x4(pa, pvbase + pch);
+        mma_f16(lacc, pl, kOnesF16, kOnesF16);
+#pragma unroll
+        for (int Gp = 0; Gp < 4; ++Gp) {  // columns 128c + 32Gp .. +31
+          const uint32_t rs = (uint32_t)(16 * s) * ROW_BYTES;
+          const uint32_t wa = lds32(vb[0][Gp] + rs);
+          const uint32_t wb = lds32(vb[1][Gp] + rs + ROW_BYTES);
+          const uint32_t wc = lds32(vb[0][Gp] + rs + 8 * ROW_BYTES);
+          const uint32_t wd = lds32(vb[1][Gp] + rs + 9 * ROW_BYTES);
+          uint32_t b0[4], b1[4];  // n-tile j: keys (2q4, 2q4+1) / (2q4+8, 2q4+9), column 4g8 + j
+          widen4(__byte_perm(wa, wb, 0x5140), b0[0], b0[1]);
+          widen4(__byte_perm(wa, wb, 0x7362), b0[2], b0[3]);
+          widen4(__byte_perm(wc, wd, 0x5140), b1[0], b1[1]);
+          widen4(__byte_perm(wc, wd, 0x7362), b1[2], b1[3]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) mma_f16(o[4 * Gp + j], pa, b0[j], b1[j]);
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&S.empty[slot]));  // slot free for the producers
+      if (lane == 0) mbar_arrive(smem_u32(&S.empty[slot]));  // slot free for the producer
 
       if (seg_end) {
         // ---------------- epilogue of the segment ending at unit i ----------
         const int64_t tb = t / p.m, tm = t - tb * p.m;
-        // the row sums: over the four lanes of a fragment row, then the warps
-        float s_lo = l_lo, s_hi = l_hi;
-#pragma unroll
-        for (int off = 1; off <= 2; off <<= 1) {
-          s_lo += __shfl_xor_sync(0xffffffffu, s_lo, off);
-          s_hi += __shfl_xor_sync(0xffffffffu, s_hi, off);
-        }
-        if (q4 == 0) {
-          S.red_sum[c][g8] = s_lo;
-          S.red_sum[c][g8 + 8] = s_hi;
-        }
-        named_bar(9, NCT);
-        s_lo = S.red_sum[0][g8] + S.red_sum[1][g8] + S.red_sum[2][g8] + S.red_sum[3][g8];
-        s_hi = S.red_sum[0][g8 + 8] + S.red_sum[1][g8 + 8] + S.red_sum[2][g8 + 8] +
-               S.red_sum[3][g8 + 8];
+        const float l_lo = lacc[0], l_hi = lacc[2];
         if (kRows || (seg_kb0 == 0 && kb == upt - 1)) {
-          const float f_lo = sink_factor(m_lo, s_lo, __ldg(p.sink + g8) * kLog2e) * R;
-          const float f_hi = sink_factor(m_hi, s_hi, __ldg(p.sink + g8 + 8) * kLog2e) * R;
+          const float f_lo = sink_factor(m_lo, l_lo, __ldg(p.sink + g8) * kLog2e) * R;
+          const float f_hi = sink_factor(m_hi, l_hi, __ldg(p.sink + g8 + 8) * kLog2e) * R;
           __nv_bfloat16* ob = p.o + tb * p.o_sb + tm * p.o_sm;
 #pragma unroll
-          for (int nt = 0; nt < 16; ++nt) {
-            const int d = 128 * c + 8 * nt + 2 * q4;
-            *reinterpret_cast<uint32_t*>(ob + g8 * p.o_sh + d) =
-                pack_bf16x2(o[nt][0] * f_lo, o[nt][1] * f_lo);
-            *reinterpret_cast<uint32_t*>(ob + (g8 + 8) * p.o_sh + d) =
-                pack_bf16x2(o[nt][2] * f_hi, o[nt][3] * f_hi);
+          for (int Gp = 0; Gp < 4; ++Gp) {
+            const int d = 128 * c + 32 * Gp + 8 * q4;
+            uint4 lo4, hi4;
+            lo4.x = pack_bf16x2(o[4 * Gp + 0][0] * f_lo, o[4 * Gp + 1][0] * f_lo);
+            lo4.y = pack_bf16x2(o[4 * Gp + 2][0] * f_lo, o[4 * Gp + 3][0] * f_lo);
+            lo4.z = pack_bf16x2(o[4 * Gp + 0][1] * f_lo, o[4 * Gp + 1][1] * f_lo);
+            lo4.w = pack_bf16x2(o[4 * Gp + 2][1] * f_lo, o[4 * Gp + 3][1] * f_lo);
+            hi4.x = pack_bf16x2(o[4 * Gp + 0][2] * f_hi, o[4 * Gp + 1][2] * f_hi);
+            hi4.y = pack_bf16x2(o[4 * Gp + 2][2] * f_hi, o[4 * Gp + 3][2] * f_hi);
+            hi4.z = pack_bf16x2(o[4 * Gp + 0][3] * f_hi, o[4 * Gp + 1][3] * f_hi);
+            hi4.w = pack_bf16x2(o[4 * Gp + 2][3] * f_hi, o[4 * Gp + 3][3] * f_hi);
+            *reinterpret_cast<uint4*>(ob + g8 * p.o_sh + d) = lo4;
+            *reinterpret_cast<uint4*>(ob + (g8 + 8) * p.o_sh + d) = hi4;
           }
         } else {
           const int64_t pslot = 2 * g + (t == t_first ? 0 : 1);
           float* pacc = p.part_acc + pslot * kPartAccFloats;
 #pragma unroll
-          for (int nt = 0; nt < 16; ++nt) {
-            const int d = 128 * c + 8 * nt + 2 * q4;
-            *reinterpret_cast<float2*>(pacc + g8 * kDim + d) =
-                make_float2(o[nt][0] * R, o[nt][1] * R);
-            *reinterpret_cast<float2*>(pacc + (g8 + 8) * kDim + d) =
-                make_float2(o[nt][2] * R, o[nt][3] * R);
+          for (int Gp = 0; Gp < 4; ++Gp) {
+            const int d = 128 * c + 32 * Gp + 8 * q4;
+            float4* lo4 = reinterpret_cast<float4*>(pacc + g8 * kDim + d);
+            float4* hi4 = reinterpret_cast<float4*>(pacc + (g8 + 8) * kDim + d);
+            lo4[0] = make_float4(o[4 * Gp + 0][0] * R, o[4 * Gp + 1][0] * R,
+                                 o[4 * Gp + 2][0] * R, o[4 * Gp + 3][0] * R);
+            lo4[1] = make_float4(o[4 * Gp + 0][1] * R, o[4 * Gp + 1][1] * R,
+                                 o[4 * Gp + 2][1] * R, o[4 * Gp + 3][1] * R);
+            hi4[0] = make_float4(o[4 * Gp + 0][2] * R, o[4 * Gp + 1][2] * R,
+                                 o[4 * Gp + 2][2] * R, o[4 * Gp + 3][2] * R);
+            hi4[1] = make_float4(o[4 * Gp + 0][3] * R, o[4 * Gp + 1][3] * R,
+                                 o[4 * Gp + 2][3] * R, o[4 * Gp + 3][3] * R);
           }
           if (c == 0 && q4 == 0) {
             p.part_ml[pslot * kPartMlFloats + g8] = m_lo;
             p.part_ml[pslot * kPartMlFloats + g8 + 8] = m_hi;
-            p.part_ml[pslot * kPartMlFloats + kHeads + g8] = s_lo;
-            p.part_ml[pslot * kPartMlFloats + kHeads + g8 + 8] = s_hi;
+            p.part_ml[pslot * kPartMlFloats + kHeads + g8] = l_lo;
+            p.part_ml[pslot * kPartMlFloats + kHeads + g8 + 8] = l_hi;
           }
           if (p.merge_in_kernel) {  // ticket of the split row, as in sa_ws.cu
             const int64_t ts = t * upt;
@@ -750,7 +724,6 @@ __global__ void __launch_bounds__(NT, 1)
 }
 
 }  // namespace fp8_path
-
 
 // ---------------------------------------------------------------------------
 // Quantiser: bf16 cache rows -> e4m3 rows + one fp32 scale per row.
