@@ -94,10 +94,6 @@ def parse():
     ap.add_argument("--kv-policy", type=int, default=-1, choices=[-1, 0, 1, 2],
                     help="L2 policy of the KV gathers (library option SA_OPT_KV_POLICY): -1 "
                          "by the call's reuse, 0 evict_first, 1 evict_normal, 2 evict_last")
-    ap.add_argument("--flush-smem-tail", action="store_true",
-                    help="experiment: end the untimed L2 flush with a tiny kernel that uses "
-                         "192 KiB of shared memory, so the op starts without an L1/shared "
-                         "memory reconfiguration")
     ap.add_argument("--graph", action="store_true",
                     help="capture one op call in a CUDA graph and time its replays")
     ap.add_argument("--no-launch-count", action="store_true",
@@ -112,28 +108,14 @@ class L2Flush:
     next step starts from a cold, clean L2.  ``read=False`` keeps the write
     alone (the step then also pays for writing those dirty lines back)."""
 
-    def __init__(self, dev, read=True, smem_tail=False):
+    def __init__(self, dev, read=True):
         self.w = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
         self.r = torch.ones(L2_FLUSH_BYTES // 8, dtype=torch.int64, device=dev) if read else None
-        self.tail = None
-        if smem_tail:  # experiment: leave the SMs in a large-shared-memory configuration
-            import ctypes
-            from sparse_attn import _lib
-            rows = torch.zeros(1, dtype=torch.int32, device=dev)
-            sink = torch.zeros(4, dtype=torch.int32, device=dev)
-            err = torch.zeros(1, dtype=torch.int32, device=dev)
-            st = torch.cuda.current_stream(dev)
-            self._keep = (rows, sink, err)
-            self.tail = lambda: _lib.check(_lib.lib().sa_probe_gather(
-                self.w.data_ptr(), 1024, rows.data_ptr(), 1, 1024, 0, 1, 6, sink.data_ptr(),
-                err.data_ptr(), ctypes.c_void_p(st.cuda_stream)))
 
     def zero_(self):
         self.w.zero_()
         if self.r is not None:
             self._acc = self.r.sum()
-        if self.tail is not None:
-            self.tail()
 
     describe = ("flushed before every timed step (256 MiB write, then a 256 MiB read so the "
                 "dirty lines are written back), flush untimed")
@@ -1086,7 +1068,7 @@ def main():
         _lib.set_option(_lib.SA_OPT_KV_POLICY, args.kv_policy)
     variant = {"auto": 0, "mma": 1, "tcgen05": 2, "ws": 3}[args.variant]
     fp8 = args.kv == "fp8"
-    flush = L2Flush(dev, smem_tail=args.flush_smem_tail)
+    flush = L2Flush(dev)
 
     def barrier():
         if world > 1:
