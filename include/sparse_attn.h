@@ -195,7 +195,7 @@ int64_t sa_get_option(int option);
  * rows[0..n_rows) of src (row r at src + rows[r] * row_stride bytes,
  * row_bytes each: a power of two, 16..32768) into shared memory or registers
  * and discards them.  method 0 = 16-byte cp.async (the forward kernels'
- * form), 1 = one 1-D bulk copy (TMA, no multicast) per row, 2 = 16-byte
+ * form), 1 = one 1-D bulk copy (1-D TMA, one CTA) per row, 2 = 16-byte
  * ld.global.nc into registers; `ctas` CTAs of 256 threads; `depth` = ring
  * slots of 32 KiB (2..6, methods 0 and 1).  sink: >= ctas words (a checksum
  * keeps the loads live); *err becomes nonzero if a bounded wait gave up.

@@ -8,7 +8,7 @@
 // checksum, so the time is the gather alone.  Three copy forms:
 //   0  cp.async 16 B per thread (the forward kernels' form): 128 producer
 //      threads, L2 evict_first hint, completion by cp.async.mbarrier.arrive;
-//   1  cp.async.bulk (1-D TMA, no multicast), one bulk copy per row, issued by
+//   1  cp.async.bulk (1-D TMA, one CTA), one bulk copy per row, issued by
 //      the 32 lanes of one warp, completion by the mbarrier's byte count;
 //   2  ld.global.nc 16 B into registers, 256 threads, 8 loads in flight each.
 // Forms 0 and 1 use a ring of `depth` slots with one consumer warp that waits
