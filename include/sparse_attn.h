@@ -180,6 +180,10 @@ int sa_device_status_reset(void);
  *                        (evict_first when m * topk < kv_len, else
  *                        evict_last), 0 evict_first, 1 evict_normal,
  *                        2 evict_last.
+ *   SA_OPT_GATHER_ONLY   diagnostic: 1 makes the default sa_fwd kernel
+ *                        gather its rows and discard them, writing no
+ *                        output (the gather's share of the kernel's time);
+ *                        0 (default) = off.
  * Options are read when a call is made; returns SA_ERR_INVALID_ARG for an
  * unknown option or value.  No counterpart in the reference. */
 #define SA_OPT_ROW_SCHEDULE 1
@@ -187,6 +191,7 @@ int sa_device_status_reset(void);
 #define SA_OPT_SPIN_LIMIT 3
 #define SA_OPT_TEST_STALL 4
 #define SA_OPT_KV_POLICY 5
+#define SA_OPT_GATHER_ONLY 6
 int sa_set_option(int option, int64_t value);
 int64_t sa_get_option(int option);
 

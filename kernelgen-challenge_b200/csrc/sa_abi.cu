@@ -96,6 +96,7 @@ std::atomic<int> g_opt_indexer_tc{1};
 std::atomic<uint32_t> g_opt_spin{0};
 std::atomic<int> g_opt_test_stall{0};
 std::atomic<int> g_opt_kv_policy{-1};
+std::atomic<int> g_opt_gather_only{0};
 
 // L2 policy of the KV gathers: when the call's rows read each cache row
 // about once (decode, MTP: m * topk < kv_len) the rows are evicted first;
@@ -114,6 +115,7 @@ bool opt_indexer_tc() { return g_opt_indexer_tc.load(std::memory_order_relaxed) 
 uint32_t opt_spin_limit() { return g_opt_spin.load(std::memory_order_relaxed); }
 int opt_test_stall() { return g_opt_test_stall.load(std::memory_order_relaxed); }
 int opt_kv_policy() { return g_opt_kv_policy.load(std::memory_order_relaxed); }
+bool opt_gather_only() { return g_opt_gather_only.load(std::memory_order_relaxed) != 0; }
 int reset_ws_error();
 int reset_tc_error();
 int reset_fp8_error();
@@ -144,6 +146,10 @@ int sa_set_option(int option, int64_t value) {
       if (value < -1 || value > 2) return SA_ERR_INVALID_ARG;
       g_opt_kv_policy.store(static_cast<int>(value));
       return SA_OK;
+    case SA_OPT_GATHER_ONLY:
+      if (value != 0 && value != 1) return SA_ERR_INVALID_ARG;
+      g_opt_gather_only.store(static_cast<int>(value));
+      return SA_OK;
     default:
       return SA_ERR_INVALID_ARG;
   }
@@ -161,6 +167,8 @@ int64_t sa_get_option(int option) {
       return g_opt_test_stall.load();
     case SA_OPT_KV_POLICY:
       return g_opt_kv_policy.load();
+    case SA_OPT_GATHER_ONLY:
+      return g_opt_gather_only.load();
     default:
       return -1;
   }

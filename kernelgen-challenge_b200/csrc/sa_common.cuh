@@ -86,6 +86,7 @@ bool opt_indexer_tc();
 uint32_t opt_spin_limit();
 int opt_test_stall();
 int opt_kv_policy();  // -1: by the call's reuse (sa_abi.cu)
+bool opt_gather_only();
 
 // log2 of the full denominator for a running max m and sum l (relative to m),
 // with the sink as the extra logit; all in the log2 domain.

@@ -155,7 +155,10 @@ __global__ void __launch_bounds__(256) sa_row_units_kernel(const Params p, int* 
 // kLse: also write the row log-sum-exp (training forward); a separate
 // instance, so the inference kernel carries no trace of it.  kRows: the row
 // schedule above instead of contiguous unit ranges (no split rows).
-template <bool kLse, bool kRows>
+// kGatherOnly (diagnostic, SA_OPT_GATHER_ONLY): the same pipeline, but the
+// consumers release each unit as soon as it lands and compute nothing; the
+// output is left unwritten.  Its time is the gather's share of the kernel.
+template <bool kLse, bool kRows, bool kGatherOnly = false>
 __global__ void __launch_bounds__(NT, 1)
     sa_ws_fwd_kernel(const Params p, const __grid_constant__ CUtensorMap q_map) {
   extern __shared__ uint8_t smem_raw[];
@@ -356,6 +359,10 @@ __global__ void __launch_bounds__(NT, 1)
       }
       const int slot = i % NSLOT;
       wait_or_err(S, S.full[slot], (i / NSLOT) & 1, 8);
+      if constexpr (kGatherOnly) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&S.empty[slot]));
+      } else {
       const uint32_t sb = smem_u32(S.ring[slot]);
 
       // ---- S for keys 16c + 8nt + {0..7}: 2 n-tiles x 32 k-steps, 2-way split
@@ -520,6 +527,7 @@ __global__ void __launch_bounds__(NT, 1)
           }
         }
       }
+      }
       if (seg_end) ++seg;
       seg_first = seg_end;
       if (++kb == nu_t) {
@@ -608,7 +616,8 @@ cudaError_t launch_ws(const Params& p, cudaStream_t st) {
   static PerDeviceOnce attr_once;
   e = once_per_device(attr_once, [] {
     for (auto* k : {sa_ws_fwd_kernel<false, false>, sa_ws_fwd_kernel<true, false>,
-                    sa_ws_fwd_kernel<false, true>, sa_ws_fwd_kernel<true, true>}) {
+                    sa_ws_fwd_kernel<false, true>, sa_ws_fwd_kernel<true, true>,
+                    sa_ws_fwd_kernel<false, false, true>, sa_ws_fwd_kernel<false, true, true>}) {
       const cudaError_t e1 =
           cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
       if (e1 != cudaSuccess) return e1;
@@ -633,6 +642,8 @@ cudaError_t launch_ws(const Params& p, cudaStream_t st) {
   cfg.numAttrs = 1;
   auto* kern = p.lse != nullptr ? (rows ? sa_ws_fwd_kernel<true, true> : sa_ws_fwd_kernel<true, false>)
                                 : (rows ? sa_ws_fwd_kernel<false, true> : sa_ws_fwd_kernel<false, false>);
+  if (opt_gather_only() && p.lse == nullptr)
+    kern = rows ? sa_ws_fwd_kernel<false, true, true> : sa_ws_fwd_kernel<false, false, true>;
   e = cudaLaunchKernelEx(&cfg, kern, p, q_map);
   if (e != cudaSuccess || p.merge_in_kernel || rows) return e;
   return launch_combine(p, st);
