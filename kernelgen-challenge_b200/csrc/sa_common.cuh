@@ -162,6 +162,41 @@ struct RangeOrder {
     if (i < n2) return u_fe + i;
     return u0 + (i - n2);
   }
+  // true when position i starts a new piece of the order (a jump in units)
+  __device__ __forceinline__ bool jumps_at(int64_t i) const {
+    return i == u1 - u_ls || i == (u1 - u_ls) + (u_ls - u_fe);
+  }
+};
+
+// Position in a RangeOrder: row t (batch tb, row tm within it), unit kb of
+// the row.  Steps by increments inside a piece and by division only at the
+// (at most two) jumps between pieces.
+struct RangeCursor {
+  RangeOrder ord;
+  int64_t t, kb, tb, tm;
+  __device__ __forceinline__ void set(int64_t u, int64_t upt, int64_t m) {
+    t = u / upt;
+    kb = u - t * upt;
+    tb = t / m;
+    tm = t - tb * m;
+  }
+  __device__ __forceinline__ void init(int64_t u0, int64_t u1, int64_t upt, int64_t m) {
+    ord.init(u0, u1, upt);
+    set(ord.at(0), upt, m);
+  }
+  // move from position i to i + 1
+  __device__ __forceinline__ void next(int64_t i, int64_t upt, int64_t m) {
+    if (ord.jumps_at(i + 1)) {
+      set(ord.at(i + 1), upt, m);
+    } else if (++kb == upt) {
+      kb = 0;
+      ++t;
+      if (++tm == m) {
+        tm = 0;
+        ++tb;
+      }
+    }
+  }
 };
 
 // Row schedule (many rows, p.row_units set): CTA g runs whole rows, the

@@ -320,13 +320,12 @@ __global__ void __launch_bounds__(NT, 1)
     // not memory, would then bound it.)
     const uint64_t pol = l2_policy_kv(p.kv_policy);
     const int c = tid & 63, par = tid >> 6, j = c >> 3, cc = c & 7;
-    RangeOrder ord;  // (unit ranges: the order of sa_common.cuh)
-    ord.init(u0, u1, upt);
+    RangeCursor rc;  // (unit ranges: the order of sa_common.cuh)
     int64_t t = t_first, kb = kb_first;
     if constexpr (!kRows) {
-      const int64_t u = ord.at(0);
-      t = u / upt;
-      kb = u - t * upt;
+      rc.init(u0, u1, upt, p.m);
+      t = rc.t;
+      kb = rc.kb;
     }
     int64_t tb = t / p.m, tm = t - tb * p.m;
     // row schedule: this row's units, the next row's (loaded a row ahead)
@@ -357,11 +356,11 @@ __global__ void __launch_bounds__(NT, 1)
           nu_n = units_of_row(p, snake_row(sk + 1, g, G, R));
         }
       } else if (i + 1 < n) {
-        const int64_t u = ord.at(i + 1);
-        t = u / upt;
-        kb = u - t * upt;
-        tb = t / p.m;
-        tm = t - tb * p.m;
+        rc.next(i, upt, p.m);
+        t = rc.t;
+        kb = rc.kb;
+        tb = rc.tb;
+        tm = rc.tm;
       }
       if (i + 1 < n) load_ids(kb, tb, tm, na, nb);
 
@@ -423,15 +422,14 @@ __global__ void __launch_bounds__(NT, 1)
         tma_load_4d(qbase + j * 2048, &q_map, 64 * j, 0, (int32_t)qm, (int32_t)qb,
                     smem_u32(&S.q_full));
     };
-    if (tt == 0) issue_q(t_first);
-    RangeOrder ord;  // (unit ranges: the order of sa_common.cuh, as the producer's)
-    ord.init(u0, u1, upt);
+    RangeCursor rc;  // (unit ranges: the order of sa_common.cuh, as the producer's)
     int64_t t = t_first, kb = kb_first, seg_kb0 = kb_first;
     if constexpr (!kRows) {
-      const int64_t u = ord.at(0);
-      t = u / upt;
-      kb = u - t * upt;
+      rc.init(u0, u1, upt, p.m);
+      t = rc.t;
+      kb = rc.kb;
     }
+    if (tt == 0) issue_q(t);  // the first row in this CTA's order
     int64_t sk = 0, nu_t = upt, nu_n = 0;  // as in the producer
     if constexpr (kRows) {
       nu_t = units_of_row(p, t);
@@ -443,11 +441,8 @@ __global__ void __launch_bounds__(NT, 1)
     // it merges after the loop, from its registers (see below)
     bool owner_pending = false;
     for (int i = 0; i < n; ++i) {
-      int64_t t_nx = -1;  // row of the next unit (unit ranges)
-      if constexpr (!kRows) {
-        if (i + 1 < n) t_nx = ord.at(i + 1) / upt;
-      }
-      const bool seg_end = kRows ? ((i == n - 1) || kb == nu_t - 1) : ((i == n - 1) || t_nx != t);
+      // (unit ranges: a segment ends at its row's last unit or at a jump)
+      const bool seg_end = (i == n - 1) || kb == nu_t - 1 || (!kRows && rc.ord.jumps_at(i + 1));
       if (seg_first) {
         m_lo = m_hi = -INFINITY;
 #pragma unroll
@@ -472,7 +467,7 @@ __global__ void __launch_bounds__(NT, 1)
         } else {
           // the next segment's row, in this CTA's order
           const int64_t seg_len = min(u1, (t + 1) * upt) - max(u0, t * upt);
-          if (tt == 0 && i + seg_len < n) issue_q(ord.at(i + seg_len) / upt);
+          if (tt == 0 && i + seg_len < n) issue_q(rc.ord.at(i + seg_len) / upt);
         }
       }
       const int slot = i % NSLOT;
@@ -665,9 +660,9 @@ __global__ void __launch_bounds__(NT, 1)
           nu_n = units_of_row(p, snake_row(sk + 1, g, G, R));
         }
       } else if (i + 1 < n) {
-        const int64_t u = ord.at(i + 1);
-        t = u / upt;
-        kb = u - t * upt;
+        rc.next(i, upt, p.m);
+        t = rc.t;
+        kb = rc.kb;
       }
     }
     if constexpr (!kRows && !kLse && !kGatherOnly) {
