@@ -68,7 +68,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="long")
-    ap.add_argument("--variant", choices=["auto", "mma", "tcgen05", "ws"], default="auto")
+    ap.add_argument("--variant", choices=["auto", "mma", "tcgen05", "ws", "wt"], default="auto")
     ap.add_argument("--grid", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the CPU baseline legs (profiling runs)")
@@ -1075,7 +1075,7 @@ def main():
         _lib.set_option(_lib.SA_OPT_KV_POLICY, args.kv_policy)
         _lib.set_option(_lib.SA_OPT_GATHER_ONLY, int(args.gather_only))
         _lib.set_option(_lib.SA_OPT_MERGE_ORDERED, int(args.merge == "ordered"))
-    variant = {"auto": 0, "mma": 1, "tcgen05": 2, "ws": 3}[args.variant]
+    variant = {"auto": 0, "mma": 1, "tcgen05": 2, "ws": 3, "wt": 4}[args.variant]
     fp8 = args.kv == "fp8"
     flush = L2Flush(dev)
 

@@ -45,12 +45,13 @@ extern "C" {
 #define SA_ERR_CUDA (-3)        /* CUDA runtime error (see last_cuda_error) */
 #define SA_ERR_UNSUPPORTED (-4) /* h % 16 != 0, d != 512, or no sm_100 device */
 
-/* Kernel variants for sa_fwd_ex (SA_VARIANT_AUTO picks the fastest, WS). */
+/* Kernel variants for sa_fwd_ex (SA_VARIANT_AUTO picks the default, WS). */
 #define SA_VARIANT_AUTO 0
 #define SA_VARIANT_MMA 1     /* all-warp mma.sync, cp.async ring, __syncthreads     */
 #define SA_VARIANT_TCGEN05 2 /* S^T by tcgen05 (TMEM), P.V warp MMAs, mbarrier pipe */
 #define SA_VARIANT_WS 3      /* warp-specialized: cp.async + TMA(Q) producers,      */
                              /* mma.sync consumers with Q in registers (default)    */
+#define SA_VARIANT_WT 4      /* as WS, with P.V on tcgen05.mma and O in TMEM        */
 
 /* Library ABI version (major * 10000 + minor * 100 + patch). */
 int sa_version(void);
@@ -142,7 +143,7 @@ int sa_quantize_kv_fp8(const void* kv, void* kv8, float* kv_scale, int64_t b, in
 /* Debug/health query, synchronous: copies into *flags the error word that the
  * pipelined kernels (SA_VARIANT_TCGEN05, SA_VARIANT_WS; the latter reported
  * as 100 + code, sa_fwd_fp8 as 200 + code, the tensor-core scorer of
- * sa_indexer_topk as 300 + code) set on the current device when one of their
+ * sa_indexer_topk as 300 + code, SA_VARIANT_WT as 400 + code) set on the current device when one of their
  * bounded pipeline waits gave up (0 = never).  Intended for tests and health checks,
  * not the hot path.  No counterpart in the reference. */
 int sa_device_status(int* flags);

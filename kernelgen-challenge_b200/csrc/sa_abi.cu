@@ -23,6 +23,10 @@ bool tc_supports(const Params& p);
 int read_tc_error(int* flags);
 cudaError_t launch_ws(const Params& p, cudaStream_t st);
 int ws_unit_keys();
+cudaError_t launch_wt(const Params& p, cudaStream_t st);
+int wt_unit_keys();
+int read_wt_error(int* flags);
+int read_wt_index_faults(unsigned long long* out, bool reset);
 int read_ws_error(int* flags);
 int read_ws_index_faults(unsigned long long* out, bool reset);
 int read_tc_index_faults(unsigned long long* out, bool reset);
@@ -122,6 +126,7 @@ int reset_ws_error();
 int reset_tc_error();
 int reset_fp8_error();
 int reset_indexer_error();
+int reset_wt_error();
 }  // namespace sa
 
 extern "C" {
@@ -187,6 +192,7 @@ int sa_device_status_reset(void) {
   if (e == 0) e = sa::reset_ws_error();
   if (e == 0) e = sa::reset_fp8_error();
   if (e == 0) e = sa::reset_indexer_error();
+  if (e == 0) e = sa::reset_wt_error();
   if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
   return SA_OK;
 }
@@ -214,13 +220,19 @@ int sa_last_cuda_error(void) { return t_last_cuda_error; }
 
 int sa_device_status(int* flags) {
   if (flags == nullptr) return SA_ERR_INVALID_ARG;
-  int a = 0, b = 0, f = 0, x = 0;
+  int a = 0, b = 0, f = 0, x = 0, w = 0;
   int e = sa::read_tc_error(&a);
   if (e == 0) e = sa::read_ws_error(&b);
   if (e == 0) e = sa::read_fp8_error(&f);
   if (e == 0) e = sa::read_indexer_error(&x);
+  if (e == 0) e = sa::read_wt_error(&w);
   if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
-  *flags = a != 0 ? a : (b != 0 ? 100 + b : (f != 0 ? 200 + f : (x != 0 ? 300 + x : 0)));
+  *flags = a != 0    ? a
+           : b != 0 ? 100 + b
+           : f != 0 ? 200 + f
+           : x != 0 ? 300 + x
+           : w != 0 ? 400 + w
+                    : 0;
   return SA_OK;
 }
 
@@ -231,6 +243,7 @@ int sa_index_faults(uint64_t* count, int reset) {
   if (e == 0) e = sa::read_tc_index_faults(&total, reset != 0);
   if (e == 0) e = sa::read_mma_index_faults(&total, reset != 0);
   if (e == 0) e = sa::read_fp8_index_faults(&total, reset != 0);
+  if (e == 0) e = sa::read_wt_index_faults(&total, reset != 0);
   if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
   *count = total;
   return SA_OK;
@@ -243,6 +256,7 @@ int sa_variant_available(int variant) {
       return 1;
     case SA_VARIANT_TCGEN05:
     case SA_VARIANT_WS:
+    case SA_VARIANT_WT:
       return sa::tc_available() ? 1 : 0;
     default:
       return 0;
@@ -338,11 +352,15 @@ static int fwd_group(const void* q, const void* kv, const float* sink, const int
     if (!sa::tc_supports(p)) return SA_ERR_UNSUPPORTED;
     unit_keys = sa::ws_unit_keys();
     ctas_per_sm = 1;
+  } else if (variant == SA_VARIANT_WT) {
+    if (!sa::tc_available() || !sa::tc_supports(p)) return SA_ERR_UNSUPPORTED;
+    unit_keys = sa::wt_unit_keys();
+    ctas_per_sm = 1;
   } else {
     return SA_ERR_INVALID_ARG;
   }
-  if (lse != nullptr) {  // only the warp-specialized kernel writes it
-    if (variant != SA_VARIANT_WS) return SA_ERR_UNSUPPORTED;
+  if (lse != nullptr) {  // only the warp-specialized kernels write it
+    if (variant != SA_VARIANT_WS && variant != SA_VARIANT_WT) return SA_ERR_UNSUPPORTED;
     if ((reinterpret_cast<uintptr_t>(lse) & 3u) != 0) return SA_ERR_INVALID_ARG;
   }
   p.lse = lse;
@@ -366,7 +384,8 @@ static int fwd_group(const void* q, const void* kv, const float* sink, const int
   // (prefill), the ws kernel merges them itself (the last CTA of each row,
   // at its end); with fewer units per CTA (decode) nearly every CTA would end
   // in merges, and the combine kernel spreads them over the whole GPU instead.
-  p.merge_in_kernel = (variant == SA_VARIANT_WS && p.units >= 2 * p.upt * p.grid) ? 1 : 0;
+  const bool ws_like = variant == SA_VARIANT_WS || variant == SA_VARIANT_WT;
+  p.merge_in_kernel = (ws_like && p.units >= 2 * p.upt * p.grid) ? 1 : 0;
   // With that many rows and room in the workspace for one int per row, the
   // ws kernel runs whole rows instead (no split rows), each only up to its
   // last valid slot (sa_ws.cu: row schedule).
@@ -379,7 +398,7 @@ static int fwd_group(const void* q, const void* kv, const float* sink, const int
   // row's last part merges the row itself (cooperative launch, so every CTA
   // is resident: the grid must fit one CTA per SM); otherwise the combine
   // kernel merges after the grid.
-  p.merge_ordered = (variant == SA_VARIANT_WS && !p.merge_in_kernel && p.row_units == nullptr &&
+  p.merge_ordered = (ws_like && !p.merge_in_kernel && p.row_units == nullptr &&
                      lse == nullptr && p.grid <= di->sms && sa::opt_merge_ordered() &&
                      !sa::opt_gather_only())
                         ? 1
@@ -388,6 +407,7 @@ static int fwd_group(const void* q, const void* kv, const float* sink, const int
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   e = (variant == SA_VARIANT_MMA)       ? sa::launch_mma(p, st)
       : (variant == SA_VARIANT_TCGEN05) ? sa::launch_tc(p, st)
+      : (variant == SA_VARIANT_WT)      ? sa::launch_wt(p, st)
                                         : sa::launch_ws(p, st);
   if (e != cudaSuccess) return fail_cuda(e);
   return SA_OK;

@@ -168,37 +168,6 @@ struct RangeOrder {
   }
 };
 
-// Position in a RangeOrder: row t (batch tb, row tm within it), unit kb of
-// the row.  Steps by increments inside a piece and by division only at the
-// (at most two) jumps between pieces.
-struct RangeCursor {
-  RangeOrder ord;
-  int64_t t, kb, tb, tm;
-  __device__ __forceinline__ void set(int64_t u, int64_t upt, int64_t m) {
-    t = u / upt;
-    kb = u - t * upt;
-    tb = t / m;
-    tm = t - tb * m;
-  }
-  __device__ __forceinline__ void init(int64_t u0, int64_t u1, int64_t upt, int64_t m) {
-    ord.init(u0, u1, upt);
-    set(ord.at(0), upt, m);
-  }
-  // move from position i to i + 1
-  __device__ __forceinline__ void next(int64_t i, int64_t upt, int64_t m) {
-    if (ord.jumps_at(i + 1)) {
-      set(ord.at(i + 1), upt, m);
-    } else if (++kb == upt) {
-      kb = 0;
-      ++t;
-      if (++tm == m) {
-        tm = 0;
-        ++tb;
-      }
-    }
-  }
-};
-
 // Row schedule (many rows, p.row_units set): CTA g runs whole rows, the
 // positions g, 2G-1-g, 2G+g, 4G-1-g, ... of the rows taken in descending
 // index order (snake rounds of G).  Every thread derives the same sequence.

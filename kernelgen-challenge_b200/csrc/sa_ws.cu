@@ -75,6 +75,7 @@ struct __align__(1024) Smem {
   int n_merge;
   int64_t merge_row[2];
   int n_units;  // row schedule: units of this CTA
+  int64_t ord[4];  // unit ranges: u0, u1, u_fe, u_ls of this CTA's RangeOrder
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + manual 1 KiB alignment
 
@@ -288,6 +289,14 @@ __global__ void __launch_bounds__(NT, 1)
     S.spin = p.spin != 0u ? p.spin : kSpinLimit;
     S.n_merge = 0;
     S.n_units = 0;
+    if constexpr (!kRows) {
+      RangeOrder o;
+      o.init(u0, u1, upt);
+      S.ord[0] = o.u0;
+      S.ord[1] = o.u1;
+      S.ord[2] = o.u_fe;
+      S.ord[3] = o.u_ls;
+    }
     fence_mbar_init();
   }
   if (warp == 4 && lane == 0) tma_prefetch_desc(&q_map);
@@ -320,12 +329,15 @@ __global__ void __launch_bounds__(NT, 1)
     // not memory, would then bound it.)
     const uint64_t pol = l2_policy_kv(p.kv_policy);
     const int c = tid & 63, par = tid >> 6, j = c >> 3, cc = c & 7;
-    RangeCursor rc;  // (unit ranges: the order of sa_common.cuh)
+    // unit ranges: the order of sa_common.cuh (RangeOrder, kept in S.ord):
+    // positions j1 and j2 jump to the next piece
+    int j1 = 0, j2 = 0;
     int64_t t = t_first, kb = kb_first;
     if constexpr (!kRows) {
-      rc.init(u0, u1, upt, p.m);
-      t = rc.t;
-      kb = rc.kb;
+      j1 = static_cast<int>(S.ord[1] - S.ord[3]);
+      j2 = j1 + static_cast<int>(S.ord[3] - S.ord[2]);
+      t = S.ord[3] / upt;
+      kb = S.ord[3] - t * upt;
     }
     int64_t tb = t / p.m, tm = t - tb * p.m;
     // row schedule: this row's units, the next row's (loaded a row ahead)
@@ -356,11 +368,20 @@ __global__ void __launch_bounds__(NT, 1)
           nu_n = units_of_row(p, snake_row(sk + 1, g, G, R));
         }
       } else if (i + 1 < n) {
-        rc.next(i, upt, p.m);
-        t = rc.t;
-        kb = rc.kb;
-        tb = rc.tb;
-        tm = rc.tm;
+        if (i + 1 == j1 || i + 1 == j2) {  // the next piece of the order
+          const int64_t u = (i + 1 == j2) ? S.ord[0] : S.ord[2];
+          t = u / upt;
+          kb = u - t * upt;
+          tb = t / p.m;
+          tm = t - tb * p.m;
+        } else if (++kb == upt) {
+          kb = 0;
+          ++t;
+          if (++tm == p.m) {
+            tm = 0;
+            ++tb;
+          }
+        }
       }
       if (i + 1 < n) load_ids(kb, tb, tm, na, nb);
 
@@ -422,12 +443,13 @@ __global__ void __launch_bounds__(NT, 1)
         tma_load_4d(qbase + j * 2048, &q_map, 64 * j, 0, (int32_t)qm, (int32_t)qb,
                     smem_u32(&S.q_full));
     };
-    RangeCursor rc;  // (unit ranges: the order of sa_common.cuh, as the producer's)
+    int j1 = 0, j2 = 0;  // (unit ranges: as the producer's)
     int64_t t = t_first, kb = kb_first, seg_kb0 = kb_first;
     if constexpr (!kRows) {
-      rc.init(u0, u1, upt, p.m);
-      t = rc.t;
-      kb = rc.kb;
+      j1 = static_cast<int>(S.ord[1] - S.ord[3]);
+      j2 = j1 + static_cast<int>(S.ord[3] - S.ord[2]);
+      t = S.ord[3] / upt;
+      kb = S.ord[3] - t * upt;
     }
     if (tt == 0) issue_q(t);  // the first row in this CTA's order
     int64_t sk = 0, nu_t = upt, nu_n = 0;  // as in the producer
@@ -442,7 +464,7 @@ __global__ void __launch_bounds__(NT, 1)
     bool owner_pending = false;
     for (int i = 0; i < n; ++i) {
       // (unit ranges: a segment ends at its row's last unit or at a jump)
-      const bool seg_end = (i == n - 1) || kb == nu_t - 1 || (!kRows && rc.ord.jumps_at(i + 1));
+      const bool seg_end = (i == n - 1) || kb == nu_t - 1 || (!kRows && (i + 1 == j1 || i + 1 == j2));
       if (seg_first) {
         m_lo = m_hi = -INFINITY;
 #pragma unroll
@@ -466,8 +488,9 @@ __global__ void __launch_bounds__(NT, 1)
           if (tt == 0 && tn >= 0) issue_q(tn);
         } else {
           // the next segment's row, in this CTA's order
-          const int64_t seg_len = min(u1, (t + 1) * upt) - max(u0, t * upt);
-          if (tt == 0 && i + seg_len < n) issue_q(rc.ord.at(i + seg_len) / upt);
+          const RangeOrder o{S.ord[0], S.ord[1], S.ord[2], S.ord[3]};
+          const int64_t seg_len = min(o.u1, (t + 1) * upt) - max(o.u0, t * upt);
+          if (tt == 0 && i + seg_len < n) issue_q(o.at(i + seg_len) / upt);
         }
       }
       const int slot = i % NSLOT;
@@ -660,9 +683,14 @@ __global__ void __launch_bounds__(NT, 1)
           nu_n = units_of_row(p, snake_row(sk + 1, g, G, R));
         }
       } else if (i + 1 < n) {
-        rc.next(i, upt, p.m);
-        t = rc.t;
-        kb = rc.kb;
+        if (i + 1 == j1 || i + 1 == j2) {
+          const int64_t u = (i + 1 == j2) ? S.ord[0] : S.ord[2];
+          t = u / upt;
+          kb = u - t * upt;
+        } else if (++kb == upt) {
+          kb = 0;
+          ++t;
+        }
       }
     }
     if constexpr (!kRows && !kLse && !kGatherOnly) {

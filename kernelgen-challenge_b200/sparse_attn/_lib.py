@@ -21,6 +21,7 @@ SA_VARIANT_AUTO = 0
 SA_VARIANT_MMA = 1
 SA_VARIANT_TCGEN05 = 2
 SA_VARIANT_WS = 3
+SA_VARIANT_WT = 4
 
 SA_OPT_ROW_SCHEDULE = 1
 SA_OPT_INDEXER_TC = 2

@@ -88,7 +88,10 @@ def test_training_forward_more_heads_lse():
     scale = 512 ** -0.5
     o, lse = _forward_train(q, kv, sink, idx, scale)
     assert lse.shape == (b, m, h)
-    assert torch.equal(o, sparse_attn(q, kv, sink, idx, scale))
+    # (the inference call may merge split rows in another order: equal within
+    # the parity tolerance, not bit for bit)
+    from helpers import assert_close
+    assert_close(o, sparse_attn(q, kv, sink, idx, scale), what="training vs inference forward")
     one = sparse_attn_backward(q, kv, sink, idx, scale, o, do, lse)
     two = sparse_attn_backward(q, kv, sink, idx, scale, o, do)
     for a, e, what in zip(one, two, ("dq", "dkv", "dsink")):
@@ -140,7 +143,8 @@ def test_training_forward_lse_and_one_pass_backward(name):
     qc, kvc, sc, ic = q.cuda(), kv.cuda(), sink.cuda(), idx.cuda()
     o_t, lse = _forward_train(qc, kvc, sc, ic, scale)
     o = sparse_attn(qc, kvc, sc, ic, scale)
-    assert torch.equal(o_t, o)
+    from helpers import assert_close
+    assert_close(o_t, o, what="training vs inference forward")
     ref = _ref_lse2(q, kv, sink, idx, scale).float()
     assert torch.allclose(lse.cpu(), ref, atol=2e-3, rtol=1e-4), (lse.cpu() - ref).abs().max()
     do = torch.randn(q.shape, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).cuda()

@@ -12,17 +12,17 @@ import torch
 import make_golden
 from helpers import assert_close, load_golden
 from oracle.sparse_attn_oracle import sparse_attn_oracle
-from sparse_attn import (SA_VARIANT_MMA, SA_VARIANT_TCGEN05, SA_VARIANT_WS, sparse_attn,
-                         sparse_attn_out)
+from sparse_attn import (SA_VARIANT_MMA, SA_VARIANT_TCGEN05, SA_VARIANT_WS, SA_VARIANT_WT,
+                         sparse_attn, sparse_attn_out)
 from sparse_attn import lib as _salib
 from sparse_attn.workloads import CONFIGS, make_inputs
 
 pytestmark = pytest.mark.gpu
 
-VARIANTS = [v for v in (SA_VARIANT_MMA, SA_VARIANT_TCGEN05, SA_VARIANT_WS)
+VARIANTS = [v for v in (SA_VARIANT_MMA, SA_VARIANT_TCGEN05, SA_VARIANT_WS, SA_VARIANT_WT)
             if _salib().sa_variant_available(v)]
-VARIANT_IDS = [{SA_VARIANT_MMA: "mma", SA_VARIANT_TCGEN05: "tcgen05", SA_VARIANT_WS: "ws"}[v]
-               for v in VARIANTS]
+VARIANT_IDS = [{SA_VARIANT_MMA: "mma", SA_VARIANT_TCGEN05: "tcgen05", SA_VARIANT_WS: "ws",
+                SA_VARIANT_WT: "wt"}[v] for v in VARIANTS]
 
 
 def _cuda(*ts):
