@@ -97,10 +97,6 @@ def parse():
     ap.add_argument("--gather-only", action="store_true",
                     help="diagnostic: the forward kernel gathers and discards its rows "
                          "(library option SA_OPT_GATHER_ONLY); no valid output")
-    ap.add_argument("--merge", choices=["ordered", "combine"], default="ordered",
-                    help="how decode-shaped calls merge split rows (library option "
-                         "SA_OPT_MERGE_ORDERED): in the kernel, by the CTA holding the row's "
-                         "last part (default), or by a separate combine kernel")
     ap.add_argument("--graph", action="store_true",
                     help="capture one op call in a CUDA graph and time its replays")
     ap.add_argument("--no-launch-count", action="store_true",
@@ -1070,11 +1066,10 @@ def main():
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
-    if args.kv_policy != -1 or args.gather_only or args.merge != "ordered":
+    if args.kv_policy != -1 or args.gather_only:
         from sparse_attn import _lib
         _lib.set_option(_lib.SA_OPT_KV_POLICY, args.kv_policy)
         _lib.set_option(_lib.SA_OPT_GATHER_ONLY, int(args.gather_only))
-        _lib.set_option(_lib.SA_OPT_MERGE_ORDERED, int(args.merge == "ordered"))
     variant = {"auto": 0, "mma": 1, "tcgen05": 2, "ws": 3, "wt": 4}[args.variant]
     fp8 = args.kv == "fp8"
     flush = L2Flush(dev)
@@ -1146,7 +1141,6 @@ def main():
                    "kv_cache": "e4m3 + fp32 per-token scale" if fp8 else "bf16",
                    "launch": "CUDA graph replay" if args.graph else "stream launch",
                    "gather_only": bool(args.gather_only),
-                   "split_row_merge": args.merge,
                    "kv_l2_policy": "by reuse (evict_first if m*topk < kv_len, else evict_last)"
                                    if args.kv_policy == -1 else
                                    ["evict_first", "evict_normal", "evict_last"][args.kv_policy]},

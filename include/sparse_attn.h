@@ -185,9 +185,6 @@ int sa_device_status_reset(void);
  *                        gather its rows and discard them, writing no
  *                        output (the gather's share of the kernel's time);
  *                        0 (default) = off.
- *   SA_OPT_MERGE_ORDERED 1 (default): in decode-shaped sa_fwd calls the CTA
- *                        holding a split row's last part merges the row
- *                        (cooperative launch); 0: a separate combine kernel.
  * Options are read when a call is made; returns SA_ERR_INVALID_ARG for an
  * unknown option or value.  No counterpart in the reference. */
 #define SA_OPT_ROW_SCHEDULE 1
@@ -196,7 +193,6 @@ int sa_device_status_reset(void);
 #define SA_OPT_TEST_STALL 4
 #define SA_OPT_KV_POLICY 5
 #define SA_OPT_GATHER_ONLY 6
-#define SA_OPT_MERGE_ORDERED 7
 int sa_set_option(int option, int64_t value);
 int64_t sa_get_option(int option);
 

@@ -101,7 +101,6 @@ std::atomic<uint32_t> g_opt_spin{0};
 std::atomic<int> g_opt_test_stall{0};
 std::atomic<int> g_opt_kv_policy{-1};
 std::atomic<int> g_opt_gather_only{0};
-std::atomic<int> g_opt_merge_ordered{1};
 
 // L2 policy of the KV gathers: when the call's rows read each cache row
 // about once (decode, MTP: m * topk < kv_len) the rows are evicted first;
@@ -121,7 +120,6 @@ uint32_t opt_spin_limit() { return g_opt_spin.load(std::memory_order_relaxed); }
 int opt_test_stall() { return g_opt_test_stall.load(std::memory_order_relaxed); }
 int opt_kv_policy() { return g_opt_kv_policy.load(std::memory_order_relaxed); }
 bool opt_gather_only() { return g_opt_gather_only.load(std::memory_order_relaxed) != 0; }
-bool opt_merge_ordered() { return g_opt_merge_ordered.load(std::memory_order_relaxed) != 0; }
 int reset_ws_error();
 int reset_tc_error();
 int reset_fp8_error();
@@ -157,10 +155,6 @@ int sa_set_option(int option, int64_t value) {
       if (value != 0 && value != 1) return SA_ERR_INVALID_ARG;
       g_opt_gather_only.store(static_cast<int>(value));
       return SA_OK;
-    case SA_OPT_MERGE_ORDERED:
-      if (value != 0 && value != 1) return SA_ERR_INVALID_ARG;
-      g_opt_merge_ordered.store(static_cast<int>(value));
-      return SA_OK;
     default:
       return SA_ERR_INVALID_ARG;
   }
@@ -180,8 +174,6 @@ int64_t sa_get_option(int option) {
       return g_opt_kv_policy.load();
     case SA_OPT_GATHER_ONLY:
       return g_opt_gather_only.load();
-    case SA_OPT_MERGE_ORDERED:
-      return g_opt_merge_ordered.load();
     default:
       return -1;
   }
@@ -394,16 +386,6 @@ static int fwd_group(const void* q, const void* kv, const float* sink, const int
     p.merge_in_kernel = 0;
     p.row_units = reinterpret_cast<const int*>(ws + need);
   }
-  // Decode-shaped calls of the default kernel: the CTA that holds a split
-  // row's last part merges the row itself (cooperative launch, so every CTA
-  // is resident: the grid must fit one CTA per SM); otherwise the combine
-  // kernel merges after the grid.
-  p.merge_ordered = (ws_like && !p.merge_in_kernel && p.row_units == nullptr &&
-                     lse == nullptr && p.grid <= di->sms && sa::opt_merge_ordered() &&
-                     !sa::opt_gather_only())
-                        ? 1
-                        : 0;
-
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   e = (variant == SA_VARIANT_MMA)       ? sa::launch_mma(p, st)
       : (variant == SA_VARIANT_TCGEN05) ? sa::launch_tc(p, st)

@@ -61,10 +61,6 @@ struct Params {
   // last one merges the row and zeroes the word again (sa_ws.cu).
   int* tickets;
   int merge_in_kernel;  // sa_ws only: merge split rows by ticket instead of the combine kernel
-  // sa_ws only (unit ranges, no lse): the CTA holding a split row's last
-  // part waits for the other parts (ticket count) and merges the row itself,
-  // right after its own part; no combine kernel.  Launched cooperatively.
-  int merge_ordered;
   // Optional (sa_fwd_train, ws kernel): lse[row][h] = log2 of the row's full
   // softmax denominator, the sink included, in the log2 domain of the scores
   // (p_t = 2^(s_t * scale * log2(e) - lse)); the backward pass reads it.
@@ -91,7 +87,6 @@ uint32_t opt_spin_limit();
 int opt_test_stall();
 int opt_kv_policy();  // -1: by the call's reuse (sa_abi.cu)
 bool opt_gather_only();
-bool opt_merge_ordered();
 
 // log2 of the full denominator for a running max m and sum l (relative to m),
 // with the sink as the extra logit; all in the log2 domain.
@@ -133,40 +128,6 @@ __host__ __device__ inline int64_t unit_begin(int64_t g, int64_t units, int64_t 
 __host__ __device__ inline int64_t cta_of_unit(int64_t u, int64_t units, int64_t grid) {
   return ((u + 1) * grid - 1) / units;
 }
-
-// The order in which a CTA runs its unit range [u0, u1): the last segment
-// first, then the whole rows between, then the first segment:
-// [u_ls, u1), [u_fe, u_ls), [u0, u_fe).  A row split across CTAs f..l then
-// has every part but l's ready early (f's part is f's last segment, run
-// first; the middle CTAs' single segments take their whole range), and l's
-// part (l's first segment) comes last, so l can merge the row right after
-// it (Params::merge_ordered, sa_ws.cu).
-struct RangeOrder {
-  int64_t u0, u1, u_fe, u_ls;
-  __device__ __forceinline__ void init(int64_t a, int64_t b, int64_t upt) {
-    u0 = a;
-    u1 = b;
-    const int64_t tf = a / upt, tl = (b - 1) / upt;
-    if (tf == tl) {  // one segment: the plain order
-      u_fe = u_ls = a;
-    } else {
-      u_fe = (tf + 1) * upt;
-      u_ls = tl * upt;
-    }
-  }
-  __device__ __forceinline__ int64_t at(int64_t i) const {
-    const int64_t n1 = u1 - u_ls;
-    if (i < n1) return u_ls + i;
-    i -= n1;
-    const int64_t n2 = u_ls - u_fe;
-    if (i < n2) return u_fe + i;
-    return u0 + (i - n2);
-  }
-  // true when position i starts a new piece of the order (a jump in units)
-  __device__ __forceinline__ bool jumps_at(int64_t i) const {
-    return i == u1 - u_ls || i == (u1 - u_ls) + (u_ls - u_fe);
-  }
-};
 
 // Row schedule (many rows, p.row_units set): CTA g runs whole rows, the
 // positions g, 2G-1-g, 2G+g, 4G-1-g, ... of the rows taken in descending

@@ -75,7 +75,6 @@ struct __align__(1024) Smem {
   int n_merge;
   int64_t merge_row[2];
   int n_units;  // row schedule: units of this CTA
-  int64_t ord[4];  // unit ranges: u0, u1, u_fe, u_ls of this CTA's RangeOrder
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + manual 1 KiB alignment
 
@@ -95,102 +94,6 @@ __device__ __forceinline__ bool wait_or_err(Smem& S, uint64_t& bar, uint32_t par
   }
   set_err(S, code);
   return false;
-}
-
-// Ordered merge of split rows (Params::merge_ordered).  The CTA that ran row
-// t's last part (its own first segment, which its order puts last) calls this
-// after its loop, with that part still in registers: it waits until the row's
-// other parts are stored (their count in the ticket word of the row's first
-// CTA), then merges them with its own and writes the row's o.  Those parts
-// were run early by their CTAs (RangeOrder), so the wait is short.  The wait
-// depends only on other CTAs of this cooperative launch finishing loops that
-// are themselves bounded; it is bounded too (code 9 in sa_ws_error, the row
-// left unwritten).  Consumer thread (c, g8, q4) holds heads g8 and g8 + 8,
-// columns 128c + 8nt + 2q4 + {0, 1} of the part.
-__device__ __forceinline__ void merge_owned_row(const Params& p, Smem& S, int64_t t, int64_t g,
-                                                float (&o)[16][4], float m_lo, float m_hi,
-                                                float l_lo, float l_hi, int c, int g8, int q4,
-                                                int tt) {
-  const int64_t upt = p.upt, ts = t * upt, G = p.grid;
-  const int64_t f = cta_of_unit(ts, p.units, G);
-  const int np = static_cast<int>(g - f);  // parts held by CTAs f .. g-1
-  const bool f_mid = unit_begin(f, p.units, G) < ts;
-  if (tt == 0) {
-    bool ok = false;
-    for (uint32_t k = 0; k < kSpinLimit; ++k) {
-      int v;
-      asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(p.tickets + f) : "memory");
-      if (v >= np) {
-        ok = true;
-        break;
-      }
-      __nanosleep(64);
-    }
-    if (ok) {
-      p.tickets[f] = 0;  // every part counted: zero for the next call
-    } else {
-      set_err(S, 9);
-    }
-  }
-  named_bar(5, NCT);
-  if (*reinterpret_cast<volatile int*>(&S.err) == 9) return;
-  __threadfence();
-  // slot of part k (CTA f + k): f's last segment when the row starts inside
-  // f's range, else that CTA's first segment (as merge_split_row)
-  auto slot_of = [&](int k) -> int64_t { return (k == 0 && f_mid) ? 2 * f + 1 : 2 * (f + k); };
-  const float sk_lo = __ldg(p.sink + g8) * kLog2e, sk_hi = __ldg(p.sink + g8 + 8) * kLog2e;
-  float M_lo = fmaxf(sk_lo, m_lo), M_hi = fmaxf(sk_hi, m_hi);
-  for (int k = 0; k < np; ++k) {
-    const float* ml = p.part_ml + slot_of(k) * kPartMlFloats;
-    M_lo = fmaxf(M_lo, __ldcg(ml + g8));
-    M_hi = fmaxf(M_hi, __ldcg(ml + g8 + 8));
-  }
-  float w_lo = exp2f(m_lo - M_lo), w_hi = exp2f(m_hi - M_hi);  // 0 for an empty part
-  float den_lo = l_lo * w_lo + exp2f(sk_lo - M_lo);
-  float den_hi = l_hi * w_hi + exp2f(sk_hi - M_hi);
-#pragma unroll
-  for (int nt = 0; nt < 16; ++nt) {
-    o[nt][0] *= w_lo;
-    o[nt][1] *= w_lo;
-    o[nt][2] *= w_hi;
-    o[nt][3] *= w_hi;
-  }
-  for (int k = 0; k < np; ++k) {
-    const int64_t sl = slot_of(k);
-    const float* ml = p.part_ml + sl * kPartMlFloats;
-    const float* acc = p.part_acc + sl * kPartAccFloats;
-    const float a_lo = exp2f(__ldcg(ml + g8) - M_lo), a_hi = exp2f(__ldcg(ml + g8 + 8) - M_hi);
-    den_lo += __ldcg(ml + kHeads + g8) * a_lo;
-    den_hi += __ldcg(ml + kHeads + g8 + 8) * a_hi;
-#pragma unroll
-    for (int h8 = 0; h8 < 2; ++h8) {  // 8 column pairs at a time: their loads in flight together
-      float2 lo[8], hi[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int d = 128 * c + 8 * (8 * h8 + e) + 2 * q4;
-        lo[e] = __ldcg(reinterpret_cast<const float2*>(acc + g8 * kDim + d));
-        hi[e] = __ldcg(reinterpret_cast<const float2*>(acc + (g8 + 8) * kDim + d));
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int nt = 8 * h8 + e;
-        o[nt][0] += lo[e].x * a_lo;
-        o[nt][1] += lo[e].y * a_lo;
-        o[nt][2] += hi[e].x * a_hi;
-        o[nt][3] += hi[e].y * a_hi;
-      }
-    }
-  }
-  const float i_lo = 1.f / den_lo, i_hi = 1.f / den_hi;
-  const int64_t tb = t / p.m, tm = t - tb * p.m;
-  __nv_bfloat16* ob = p.o + tb * p.o_sb + tm * p.o_sm;
-#pragma unroll
-  for (int nt = 0; nt < 16; ++nt) {
-    const int d = 128 * c + 8 * nt + 2 * q4;
-    *reinterpret_cast<uint32_t*>(ob + g8 * p.o_sh + d) = pack_bf16x2(o[nt][0] * i_lo, o[nt][1] * i_lo);
-    *reinterpret_cast<uint32_t*>(ob + (g8 + 8) * p.o_sh + d) =
-        pack_bf16x2(o[nt][2] * i_hi, o[nt][3] * i_hi);
-  }
 }
 
 // Byte offset of the 16-byte chunk `ch` (keys 8ch..8ch+7) of P row `h`:
@@ -275,6 +178,7 @@ __global__ void __launch_bounds__(NT, 1)
   int n = static_cast<int>(u1 - u0);  // units of this CTA (row schedule: below)
   const int64_t upt = p.upt;
   const int64_t t_first = kRows ? snake_row(0, g, G, R) : u0 / upt;
+  const int64_t t_last = (u1 - 1) / upt;  // (unit ranges only)
   const int64_t kb_first = kRows ? 0 : u0 - t_first * upt;
   // the combine kernel of split rows may launch now; it waits for this grid
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -289,14 +193,6 @@ __global__ void __launch_bounds__(NT, 1)
     S.spin = p.spin != 0u ? p.spin : kSpinLimit;
     S.n_merge = 0;
     S.n_units = 0;
-    if constexpr (!kRows) {
-      RangeOrder o;
-      o.init(u0, u1, upt);
-      S.ord[0] = o.u0;
-      S.ord[1] = o.u1;
-      S.ord[2] = o.u_fe;
-      S.ord[3] = o.u_ls;
-    }
     fence_mbar_init();
   }
   if (warp == 4 && lane == 0) tma_prefetch_desc(&q_map);
@@ -329,16 +225,7 @@ __global__ void __launch_bounds__(NT, 1)
     // not memory, would then bound it.)
     const uint64_t pol = l2_policy_kv(p.kv_policy);
     const int c = tid & 63, par = tid >> 6, j = c >> 3, cc = c & 7;
-    // unit ranges: the order of sa_common.cuh (RangeOrder, kept in S.ord):
-    // positions j1 and j2 jump to the next piece
-    int j1 = 0, j2 = 0;
     int64_t t = t_first, kb = kb_first;
-    if constexpr (!kRows) {
-      j1 = static_cast<int>(S.ord[1] - S.ord[3]);
-      j2 = j1 + static_cast<int>(S.ord[3] - S.ord[2]);
-      t = S.ord[3] / upt;
-      kb = S.ord[3] - t * upt;
-    }
     int64_t tb = t / p.m, tm = t - tb * p.m;
     // row schedule: this row's units, the next row's (loaded a row ahead)
     int64_t sk = 0, nu_t = upt, nu_n = 0;
@@ -358,24 +245,15 @@ __global__ void __launch_bounds__(NT, 1)
       const int32_t ia = na, ib = nb;
       const int64_t cur_tb = tb;
       // advance the cursor and prefetch the next unit's indices
-      if constexpr (kRows) {
-        if (++kb == nu_t) {
-          kb = 0;
+      if (++kb == nu_t) {
+        kb = 0;
+        if constexpr (kRows) {
           t = snake_row(++sk, g, G, R);
           tb = t / p.m;
           tm = t - tb * p.m;
           nu_t = nu_n;
           nu_n = units_of_row(p, snake_row(sk + 1, g, G, R));
-        }
-      } else if (i + 1 < n) {
-        if (i + 1 == j1 || i + 1 == j2) {  // the next piece of the order
-          const int64_t u = (i + 1 == j2) ? S.ord[0] : S.ord[2];
-          t = u / upt;
-          kb = u - t * upt;
-          tb = t / p.m;
-          tm = t - tb * p.m;
-        } else if (++kb == upt) {
-          kb = 0;
+        } else {
           ++t;
           if (++tm == p.m) {
             tm = 0;
@@ -443,15 +321,8 @@ __global__ void __launch_bounds__(NT, 1)
         tma_load_4d(qbase + j * 2048, &q_map, 64 * j, 0, (int32_t)qm, (int32_t)qb,
                     smem_u32(&S.q_full));
     };
-    int j1 = 0, j2 = 0;  // (unit ranges: as the producer's)
+    if (tt == 0) issue_q(t_first);
     int64_t t = t_first, kb = kb_first, seg_kb0 = kb_first;
-    if constexpr (!kRows) {
-      j1 = static_cast<int>(S.ord[1] - S.ord[3]);
-      j2 = j1 + static_cast<int>(S.ord[3] - S.ord[2]);
-      t = S.ord[3] / upt;
-      kb = S.ord[3] - t * upt;
-    }
-    if (tt == 0) issue_q(t);  // the first row in this CTA's order
     int64_t sk = 0, nu_t = upt, nu_n = 0;  // as in the producer
     if constexpr (kRows) {
       nu_t = units_of_row(p, t);
@@ -459,12 +330,8 @@ __global__ void __launch_bounds__(NT, 1)
     }
     int seg = 0;
     bool seg_first = true;
-    // ordered merge: this CTA's last segment is a split row whose other parts
-    // it merges after the loop, from its registers (see below)
-    bool owner_pending = false;
     for (int i = 0; i < n; ++i) {
-      // (unit ranges: a segment ends at its row's last unit or at a jump)
-      const bool seg_end = (i == n - 1) || kb == nu_t - 1 || (!kRows && (i + 1 == j1 || i + 1 == j2));
+      const bool seg_end = (i == n - 1) || kb == nu_t - 1;
       if (seg_first) {
         m_lo = m_hi = -INFINITY;
 #pragma unroll
@@ -486,11 +353,8 @@ __global__ void __launch_bounds__(NT, 1)
         if constexpr (kRows) {
           const int64_t tn = snake_row(sk + 1, g, G, R);
           if (tt == 0 && tn >= 0) issue_q(tn);
-        } else {
-          // the next segment's row, in this CTA's order
-          const RangeOrder o{S.ord[0], S.ord[1], S.ord[2], S.ord[3]};
-          const int64_t seg_len = min(o.u1, (t + 1) * upt) - max(o.u0, t * upt);
-          if (tt == 0 && i + seg_len < n) issue_q(o.at(i + seg_len) / upt);
+        } else if (tt == 0 && t < t_last) {
+          issue_q(t + 1);
         }
       }
       const int slot = i % NSLOT;
@@ -630,10 +494,6 @@ __global__ void __launch_bounds__(NT, 1)
             *reinterpret_cast<uint32_t*>(ob + (g8 + 8) * p.o_sh + d) =
                 pack_bf16x2(o[nt][2] * f_hi, o[nt][3] * f_hi);
           }
-        } else if (p.merge_ordered && !kLse &&
-                   cta_of_unit(t * upt + upt - 1, p.units, G) == g) {
-          // this CTA holds the row's last part, run last: merged after the loop
-          owner_pending = true;
         } else {
           const int64_t pslot = 2 * g + (t == t_first ? 0 : 1);
           float* pacc = p.part_acc + pslot * kPartAccFloats;
@@ -664,37 +524,22 @@ __global__ void __launch_bounds__(NT, 1)
               p.tickets[f] = 0;
               S.merge_row[S.n_merge++] = t;  // merged after the last unit (registers free)
             }
-          } else if (p.merge_ordered && !kLse) {
-            // one more part of row t stored: the row's last CTA counts them
-            __threadfence();
-            named_bar(5, NCT);
-            if (tt == 0) atomicAdd(p.tickets + cta_of_unit(t * upt, p.units, G), 1);
           }
         }
       }
       }
       if (seg_end) ++seg;
       seg_first = seg_end;
-      if constexpr (kRows) {
-        if (++kb == nu_t) {
-          kb = 0;
+      if (++kb == nu_t) {
+        kb = 0;
+        if constexpr (kRows) {
           t = snake_row(++sk, g, G, R);
           nu_t = nu_n;
           nu_n = units_of_row(p, snake_row(sk + 1, g, G, R));
-        }
-      } else if (i + 1 < n) {
-        if (i + 1 == j1 || i + 1 == j2) {
-          const int64_t u = (i + 1 == j2) ? S.ord[0] : S.ord[2];
-          t = u / upt;
-          kb = u - t * upt;
-        } else if (++kb == upt) {
-          kb = 0;
+        } else {
           ++t;
         }
       }
-    }
-    if constexpr (!kRows && !kLse && !kGatherOnly) {
-      if (owner_pending) merge_owned_row(p, S, t, g, o, m_lo, m_hi, lacc[0], lacc[2], c, g8, q4, tt);
     }
     // After an error the last Q load issued may still be in flight: wait for
     // it (its phase is the only one not yet seen) before the CTA exits.
@@ -791,14 +636,8 @@ cudaError_t launch_ws(const Params& p, cudaStream_t st) {
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  if (p.merge_ordered) {
-    // CTAs wait for parts other CTAs store: all must be resident at once
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-  } else {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-  }
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   auto* kern = p.lse != nullptr ? (rows ? sa_ws_fwd_kernel<true, true> : sa_ws_fwd_kernel<true, false>)
@@ -806,7 +645,7 @@ cudaError_t launch_ws(const Params& p, cudaStream_t st) {
   if (opt_gather_only() && p.lse == nullptr)
     kern = rows ? sa_ws_fwd_kernel<false, true, true> : sa_ws_fwd_kernel<false, false, true>;
   e = cudaLaunchKernelEx(&cfg, kern, p, q_map);
-  if (e != cudaSuccess || p.merge_in_kernel || p.merge_ordered || rows) return e;
+  if (e != cudaSuccess || p.merge_in_kernel || rows) return e;
   return launch_combine(p, st);
 }
 

@@ -7,7 +7,7 @@
 // Algorithm: track-01/submission.py:276-347 (math of reference.py:24-40);
 // masking of submission.py:313-322; sink in the denominator only
 // (submission.py:340-345).  Work schedule, split rows and their merges:
-// sa_common.cuh, as in sa_ws.cu, whose producer this kernel shares.
+// sa_common.cuh, as in sa_ws.cu, whose producer this kernel repeats.
 //
 // Why split the products this way: with 16 heads, S^T on tcgen05 would put
 // the heads on N = 16 and the 64 keys of a unit on M = 64: 32 instructions of
@@ -89,7 +89,6 @@ struct __align__(1024) Smem {
   int n_merge;
   int64_t merge_row[2];
   int n_units;  // row schedule: units of this CTA
-  int64_t ord[4];  // unit ranges: u0, u1, u_fe, u_ls of this CTA's RangeOrder
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + manual 1 KiB alignment
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -140,82 +139,6 @@ __device__ __forceinline__ void tmem_block(uint32_t tmem, int c, int j, float (&
   tmem_ld16(tmem_at(tmem, 32 * c, 16 * j), v);
 }
 
-// Ordered merge of a split row (Params::merge_ordered; see sa_ws.cu): this
-// CTA ran the row's last part, whose O is in TMEM; m / l for all heads in
-// shared memory (m_row, and the summed row sums in red_sum).
-__device__ __forceinline__ void merge_owned_row_tmem(const Params& p, Smem& S, int64_t t,
-                                                     int64_t g, uint32_t tmem, int c, int lane,
-                                                     int tt) {
-  const int64_t upt = p.upt, ts = t * upt, G = p.grid;
-  const int64_t f = cta_of_unit(ts, p.units, G);
-  const int np = static_cast<int>(g - f);  // parts held by CTAs f .. g-1
-  const bool f_mid = unit_begin(f, p.units, G) < ts;
-  if (tt == 0) {
-    bool ok = false;
-    for (uint32_t k = 0; k < kSpinLimit; ++k) {
-      int v;
-      asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(p.tickets + f) : "memory");
-      if (v >= np) {
-        ok = true;
-        break;
-      }
-      __nanosleep(64);
-    }
-    if (ok) {
-      p.tickets[f] = 0;  // every part counted: zero for the next call
-    } else {
-      set_err(S, 9);
-    }
-  }
-  named_bar(5, NCT);
-  if (*reinterpret_cast<volatile int*>(&S.err) == 9) return;
-  __threadfence();
-  auto slot_of = [&](int k) -> int64_t { return (k == 0 && f_mid) ? 2 * f + 1 : 2 * (f + k); };
-  float M[16], den[16], w[16];
-#pragma unroll
-  for (int h = 0; h < 16; ++h) {
-    const float sk = __ldg(p.sink + h) * kLog2e;
-    M[h] = fmaxf(sk, S.m_row[h]);
-  }
-  for (int k = 0; k < np; ++k) {
-    const float* ml = p.part_ml + slot_of(k) * kPartMlFloats;
-#pragma unroll
-    for (int h = 0; h < 16; ++h) M[h] = fmaxf(M[h], __ldcg(ml + h));
-  }
-#pragma unroll
-  for (int h = 0; h < 16; ++h) {
-    const float sk = __ldg(p.sink + h) * kLog2e;
-    w[h] = exp2f(S.m_row[h] - M[h]);  // 0 for an empty part
-    const float lh = S.red_sum[0][h] + S.red_sum[1][h] + S.red_sum[2][h] + S.red_sum[3][h];
-    den[h] = lh * w[h] + exp2f(sk - M[h]);
-  }
-  for (int k = 0; k < np; ++k) {
-    const float* ml = p.part_ml + slot_of(k) * kPartMlFloats;
-#pragma unroll
-    for (int h = 0; h < 16; ++h) den[h] += __ldcg(ml + kHeads + h) * exp2f(__ldcg(ml + h) - M[h]);
-  }
-  const int64_t tb = t / p.m, tm = t - tb * p.m;
-  __nv_bfloat16* ob = p.o + tb * p.o_sb + tm * p.o_sm;
-#pragma unroll 1
-  for (int j = 0; j < 4; ++j) {
-    const int col = 128 * j + 32 * c + lane;
-    float v[16];
-    tmem_block(tmem, c, j, v);
-    tmem_wait_ld();
-#pragma unroll
-    for (int h = 0; h < 16; ++h) v[h] *= w[h];
-    for (int k = 0; k < np; ++k) {
-      const int64_t sl = slot_of(k);
-      const float* ml = p.part_ml + sl * kPartMlFloats;
-      const float* acc = p.part_acc + sl * kPartAccFloats + col;
-#pragma unroll
-      for (int h = 0; h < 16; ++h) v[h] += __ldcg(acc + h * kDim) * exp2f(__ldcg(ml + h) - M[h]);
-    }
-#pragma unroll
-    for (int h = 0; h < 16; ++h) ob[h * p.o_sh + col] = __float2bfloat16_rn(v[h] / den[h]);
-  }
-}
-
 // kLse: also write the row log-sum-exp (training forward).  kRows: the row
 // schedule of sa_common.cuh instead of contiguous unit ranges.
 template <bool kLse, bool kRows>
@@ -238,6 +161,7 @@ __global__ void __launch_bounds__(NT, 1)
   int n = static_cast<int>(u1 - u0);  // units of this CTA (row schedule: below)
   const int64_t upt = p.upt;
   const int64_t t_first = kRows ? snake_row(0, g, G, R) : u0 / upt;
+  const int64_t t_last = (u1 - 1) / upt;  // (unit ranges only)
   const int64_t kb_first = kRows ? 0 : u0 - t_first * upt;
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
@@ -253,14 +177,6 @@ __global__ void __launch_bounds__(NT, 1)
     S.spin = p.spin != 0u ? p.spin : kSpinLimit;
     S.n_merge = 0;
     S.n_units = 0;
-    if constexpr (!kRows) {
-      RangeOrder o;
-      o.init(u0, u1, upt);
-      S.ord[0] = o.u0;
-      S.ord[1] = o.u1;
-      S.ord[2] = o.u_fe;
-      S.ord[3] = o.u_ls;
-    }
     fence_mbar_init();
   }
   if (warp == 4) {  // the first consumer warp owns the tensor memory
@@ -294,16 +210,7 @@ __global__ void __launch_bounds__(NT, 1)
     // contiguous bytes of one row) into the 128-byte-swizzled slab layout.
     const uint64_t pol = l2_policy_kv(p.kv_policy);
     const int c = tid & 63, par = tid >> 6, j = c >> 3, cc = c & 7;
-    // unit ranges: the order of sa_common.cuh (RangeOrder, kept in S.ord):
-    // positions j1 and j2 jump to the next piece
-    int j1 = 0, j2 = 0;
     int64_t t = t_first, kb = kb_first;
-    if constexpr (!kRows) {
-      j1 = static_cast<int>(S.ord[1] - S.ord[3]);
-      j2 = j1 + static_cast<int>(S.ord[3] - S.ord[2]);
-      t = S.ord[3] / upt;
-      kb = S.ord[3] - t * upt;
-    }
     int64_t tb = t / p.m, tm = t - tb * p.m;
     int64_t sk = 0, nu_t = upt, nu_n = 0;
     if constexpr (kRows) {
@@ -321,24 +228,15 @@ __global__ void __launch_bounds__(NT, 1)
     for (int i = 0; i < n; ++i) {
       const int32_t ia = na, ib = nb;
       const int64_t cur_tb = tb;
-      if constexpr (kRows) {
-        if (++kb == nu_t) {
-          kb = 0;
+      if (++kb == nu_t) {
+        kb = 0;
+        if constexpr (kRows) {
           t = snake_row(++sk, g, G, R);
           tb = t / p.m;
           tm = t - tb * p.m;
           nu_t = nu_n;
           nu_n = units_of_row(p, snake_row(sk + 1, g, G, R));
-        }
-      } else if (i + 1 < n) {
-        if (i + 1 == j1 || i + 1 == j2) {  // the next piece of the order
-          const int64_t u = (i + 1 == j2) ? S.ord[0] : S.ord[2];
-          t = u / upt;
-          kb = u - t * upt;
-          tb = t / p.m;
-          tm = t - tb * p.m;
-        } else if (++kb == upt) {
-          kb = 0;
+        } else {
           ++t;
           if (++tm == p.m) {
             tm = 0;
@@ -399,15 +297,8 @@ __global__ void __launch_bounds__(NT, 1)
         tma_load_4d(qbase + jq * 2048, &q_map, 64 * jq, 0, (int32_t)qm, (int32_t)qb,
                     smem_u32(&S.q_full));
     };
-    int j1 = 0, j2 = 0;  // (unit ranges: as the producer's)
     int64_t t = t_first, kb = kb_first, seg_kb0 = kb_first;
-    if constexpr (!kRows) {
-      j1 = static_cast<int>(S.ord[1] - S.ord[3]);
-      j2 = j1 + static_cast<int>(S.ord[3] - S.ord[2]);
-      t = S.ord[3] / upt;
-      kb = S.ord[3] - t * upt;
-    }
-    if (tt == 0) issue_q(t);  // the first row in this CTA's order
+    if (tt == 0) issue_q(t_first);
     int64_t sk = 0, nu_t = upt, nu_n = 0;
     if constexpr (kRows) {
       nu_t = units_of_row(p, t);
@@ -415,9 +306,8 @@ __global__ void __launch_bounds__(NT, 1)
     }
     int seg = 0;
     bool seg_first = true;
-    bool owner_pending = false;
     for (int i = 0; i < n; ++i) {
-      const bool seg_end = (i == n - 1) || kb == nu_t - 1 || (!kRows && (i + 1 == j1 || i + 1 == j2));
+      const bool seg_end = (i == n - 1) || kb == nu_t - 1;
       const bool unit0 = seg_first;  // the segment's first unit: O is written, not added
       if (seg_first) {
         m_lo = m_hi = -INFINITY;
@@ -436,10 +326,8 @@ __global__ void __launch_bounds__(NT, 1)
         if constexpr (kRows) {
           const int64_t tn = snake_row(sk + 1, g, G, R);
           if (tt == 0 && tn >= 0) issue_q(tn);
-        } else {
-          const RangeOrder o{S.ord[0], S.ord[1], S.ord[2], S.ord[3]};
-          const int64_t seg_len = min(o.u1, (t + 1) * upt) - max(o.u0, t * upt);
-          if (tt == 0 && i + seg_len < n) issue_q(o.at(i + seg_len) / upt);
+        } else if (tt == 0 && t < t_last) {
+          issue_q(t + 1);
         }
       }
       const int slot = i % NSLOT;
@@ -588,18 +476,12 @@ __global__ void __launch_bounds__(NT, 1)
           return S.red_sum[0][h] + S.red_sum[1][h] + S.red_sum[2][h] + S.red_sum[3][h];
         };
         const bool full_row = kRows || (seg_kb0 == 0 && kb == upt - 1);
-        const bool owner = !full_row && p.merge_ordered && !kLse &&
-                           cta_of_unit(t * upt + upt - 1, p.units, G) == g;
         if (kLse && full_row && c == 0 && q4 == 0) {
           p.lse[t * p.lse_rs + g8] = row_lse2(m_lo, lsum(g8), __ldg(p.sink + g8) * kLog2e);
           p.lse[t * p.lse_rs + g8 + 8] =
               row_lse2(m_hi, lsum(g8 + 8), __ldg(p.sink + g8 + 8) * kLog2e);
         }
-        if (owner) {
-          // this CTA's last segment (its order puts it last): merged after the
-          // loop (S.m_row and S.red_sum keep this segment's values until then)
-          owner_pending = true;
-        } else {
+        {
           // wait for the segment's MMAs, then read O (this thread: one column
           // per block, all 16 heads)
           wait_or_err(S, S.pv_done[i & 1], (i >> 1) & 1, 12);
@@ -643,10 +525,6 @@ __global__ void __launch_bounds__(NT, 1)
                 p.tickets[f0] = 0;
                 S.merge_row[S.n_merge++] = t;  // merged after the last unit
               }
-            } else if (p.merge_ordered && !kLse) {
-              __threadfence();
-              named_bar(5, NCT);
-              if (tt == 0) atomicAdd(p.tickets + f0, 1);
             }
           }
         }
@@ -655,30 +533,15 @@ __global__ void __launch_bounds__(NT, 1)
       }
       if (seg_end) ++seg;
       seg_first = seg_end;
-      if constexpr (kRows) {
-        if (++kb == nu_t) {
-          kb = 0;
+      if (++kb == nu_t) {
+        kb = 0;
+        if constexpr (kRows) {
           t = snake_row(++sk, g, G, R);
           nu_t = nu_n;
           nu_n = units_of_row(p, snake_row(sk + 1, g, G, R));
-        }
-      } else if (i + 1 < n) {
-        if (i + 1 == j1 || i + 1 == j2) {
-          const int64_t u = (i + 1 == j2) ? S.ord[0] : S.ord[2];
-          t = u / upt;
-          kb = u - t * upt;
-        } else if (++kb == upt) {
-          kb = 0;
+        } else {
           ++t;
         }
-      }
-    }
-    if constexpr (!kRows && !kLse) {
-      if (owner_pending) {
-        wait_or_err(S, S.pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1, 12);
-        tc_fence_after();
-        merge_owned_row_tmem(p, S, t, g, tmem, c, lane, tt);
-        tc_fence_before();
       }
     }
     // Before the tensor memory is freed: the last MMAs are done (bounded;
@@ -772,19 +635,14 @@ cudaError_t launch_wt(const Params& p, cudaStream_t st) {
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  if (p.merge_ordered) {
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-  } else {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-  }
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   auto* kern = p.lse != nullptr ? (rows ? sa_wt_fwd_kernel<true, true> : sa_wt_fwd_kernel<true, false>)
                                 : (rows ? sa_wt_fwd_kernel<false, true> : sa_wt_fwd_kernel<false, false>);
   e = cudaLaunchKernelEx(&cfg, kern, p, q_map);
-  if (e != cudaSuccess || p.merge_in_kernel || p.merge_ordered || rows) return e;
+  if (e != cudaSuccess || p.merge_in_kernel || rows) return e;
   return launch_combine(p, st);
 }
 
