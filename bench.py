@@ -124,6 +124,15 @@ class L2Flush:
                 "dirty lines are written back), flush untimed")
 
 
+def emit(args, d):
+    """Print one op's JSON line, or hand it back when the default run
+    collects the other ops' lines into its own."""
+    if getattr(args, "collect", False):
+        return d
+    print(json.dumps(d), flush=True)
+    return d
+
+
 def dist_env():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     return int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")), ws
@@ -536,15 +545,14 @@ def run_hc_sinkhorn(args):
     tokens = b * s_
     peak, kind = measured_peaks()
     achieved = tokens * 192 / (ms / 1e3) / 1e9
-    print(json.dumps({
+    return emit(args, {
         "metric": "hc_split_sinkhorn tokens/s", "value": tokens / (ms / 1e3), "unit": "tokens/s",
         "n_gpus": 1, "steps": K, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "dtype": "f32", "data": "synthetic (seeded randn)",
         "config": {"workload": "track-02 1k-1-64 prefill", "shape": [b, s_, 24],
                    "l2": "flushed before every timed step, flush untimed"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "note": "192 algorithmic bytes per token"}}),
-        flush=True)
+                     "frac": achieved / peak, "note": "192 algorithmic bytes per token"}})
 
 
 def run_backward(args):
@@ -573,7 +581,8 @@ def run_backward(args):
     import sparse_attn
     from sparse_attn.op import _forward_train
     dev = torch.device("cuda", 0)
-    q, kv, sink, idx = device_inputs(cfg, seed=1000, device=dev)
+    from sparse_attn.shard import RowBlock
+    q, kv, sink, idx = block_inputs(cfg, RowBlock(0, cfg.b, 0, cfg.m), 1000, dev)
     o, lse = _forward_train(q, kv, sink, idx, SCALE)  # the training forward keeps the lse
     do = torch.randn(q.shape, device=dev, dtype=torch.bfloat16)
     flush = L2Flush(dev)
@@ -592,14 +601,14 @@ def run_backward(args):
     torch.cuda.synchronize()
     ms = sum(a.elapsed_time(e) for a, e in zip(st, en)) / K
     valid = int(((idx >= 0) & (idx < cfg.kv_len)).sum().item())
-    print(json.dumps({
+    return emit(args, {
         "metric": "sparse_attn backward query-tokens/s", "value": cfg.b * cfg.m / (ms / 1e3),
         "unit": "query-tokens/s", "n_gpus": 1, "steps": K, "ms_per_step": ms,
         "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": cfg.name, "b": cfg.b, "m": cfg.m, "kv_len": cfg.kv_len,
                    "topk": cfg.topk, "includes": "zeroing of the fp32 dkv buffer, sa_bwd "
                    "(one pass, given the training forward's lse), dkv cast to bf16"},
-        "gathered_kv_gbs": valid * D * 2 / (ms / 1e3) / 1e9}), flush=True)
+        "gathered_kv_gbs": valid * D * 2 / (ms / 1e3) / 1e9})
 
 
 def run_indexer(args):
@@ -648,12 +657,12 @@ def run_indexer(args):
     ms = sum(a.elapsed_time(e) for a, e in zip(st, en)) / K
     rows = cfg.b * cfg.m
     flops = 2.0 * rows * cfg.kv_len * 64 * 128
-    print(json.dumps({
+    return emit(args, {
         "metric": "indexer query-tokens/s", "value": rows / (ms / 1e3), "unit": "query-tokens/s",
         "n_gpus": 1, "steps": K, "ms_per_step": ms, "higher_is_better": True, "dtype": "bf16",
         "config": {"workload": cfg.name, "b": cfg.b, "m": cfg.m, "kv_len": cfg.kv_len,
                    "topk": cfg.topk, "index_heads": 64, "index_dim": 128},
-        "score_tflops": flops / (ms / 1e3) / 1e12}), flush=True)
+        "score_tflops": flops / (ms / 1e3) / 1e12})
 
 
 # ----------------------------------------------------------------------------
@@ -702,7 +711,6 @@ class Case:
         blk = self.blocks[0]
         icfg = dataclasses.replace(self.cfg, b=blk.b1 - blk.b0, m=blk.m1 - blk.m0)
         return make_indices(icfg, torch.Generator().manual_seed(self.seed + 7919 * r), m0=blk.m0)
-
 
 def timed_steps(step, K, flush, stream, barrier, clocks_dev=None):
     """K L2-flushed steps timed by CUDA events (flush outside the events).
@@ -1117,6 +1125,32 @@ def main():
             torch.cuda.empty_cache()
             per_config[name] = r
 
+    # the other rows of the scope table, measured in the same run at one GPU:
+    # the fp8 KV cache at decode, the backward pass, the top-k index producer,
+    # track-02's hc_split_sinkhorn
+    other_ops = {}
+    if world == 1 and not args.no_per_config and not fp8:
+        r = measure_config(CONFIGS["decode"], args, rank, world, dev, flush, barrier,
+                           PER_CONFIG_STEPS["decode"], headline=False, fp8=True, variant=0,
+                           l2_gbs=l2_gbs, with_e2e=False, with_cpu=False)
+        r.pop("_case")
+        per_config["decode:fp8"] = r
+        torch.cuda.empty_cache()
+        import copy
+        for name, fn, over in (("sparse_attn_bwd:causal", run_backward,
+                                {"config": "causal", "steps": 20}),
+                               ("indexer:decode", run_indexer, {"config": "decode", "steps": 50}),
+                               ("hc_split_sinkhorn", run_hc_sinkhorn, {"steps": 200})):
+            a = copy.copy(args)
+            a.collect, a.impl = True, "ours"
+            for k, v in over.items():
+                setattr(a, k, v)
+            try:
+                other_ops[name] = fn(a)
+            except Exception as e:  # noqa: BLE001 - reported in the line, never fatal
+                other_ops[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
+            torch.cuda.empty_cache()
+
     if rank != 0:
         if world > 1:
             torch.distributed.destroy_process_group()
@@ -1164,6 +1198,8 @@ def main():
         line["triton_reference"] = triton
     if per_config:
         line["per_config"] = per_config
+    if other_ops:
+        line["other_ops"] = other_ops
     print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
