@@ -185,6 +185,12 @@ int sa_device_status_reset(void);
  *                        gather its rows and discard them, writing no
  *                        output (the gather's share of the kernel's time);
  *                        0 (default) = off.
+ *   SA_OPT_HEAD_GROUPS   h > 16 on the default sa_fwd kernel: 1 (default)
+ *                        runs all groups of 16 heads in one launch, the
+ *                        groups' CTAs side by side over the same rows, so
+ *                        each KV row is read from HBM about once; 0 runs
+ *                        the groups one after another, each gathering the
+ *                        rows again.
  * Options are read when a call is made; returns SA_ERR_INVALID_ARG for an
  * unknown option or value.  No counterpart in the reference. */
 #define SA_OPT_ROW_SCHEDULE 1
@@ -193,6 +199,7 @@ int sa_device_status_reset(void);
 #define SA_OPT_TEST_STALL 4
 #define SA_OPT_KV_POLICY 5
 #define SA_OPT_GATHER_ONLY 6
+#define SA_OPT_HEAD_GROUPS 7
 int sa_set_option(int option, int64_t value);
 int64_t sa_get_option(int option);
 

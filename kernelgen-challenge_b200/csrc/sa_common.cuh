@@ -78,6 +78,13 @@ struct Params {
   // L2 policy of the KV row gathers: 0 evict_first, 1 evict_normal,
   // 2 evict_last (l2_policy_kv)
   int kv_policy;
+  // Head groups of 16 run by one launch (ws kernel; 1 elsewhere): group
+  // blockIdx.y reads heads 16y..16y+15 of q (the Q map spans all hg * 16) and
+  // writes them in o and lse; its CTAs use workspace slots and tickets
+  // [y * grid, (y + 1) * grid).  The groups' CTAs with one blockIdx.x walk the
+  // same units at the same time, so a KV row gathered for one group is an L2
+  // hit for the others.
+  int hg;
 };
 
 // Process-wide options (sa_set_option, sa_abi.cu).
@@ -99,6 +106,20 @@ __device__ __forceinline__ float row_lse2(float m_run, float l_run, float sink_l
 // Workspace layout shared by the host (sizing) and the kernels.
 constexpr size_t kPartAccFloats = (size_t)kHeads * kDim;
 constexpr size_t kPartMlFloats = 2 * kHeads;
+
+// The Params of head group y (see Params::hg): output, sink, lse and
+// workspace pointers moved to the group's heads and slots.
+__device__ __forceinline__ Params group_params(const Params& p, int y) {
+  Params r = p;
+  const int64_t gb = (int64_t)y * p.grid;
+  r.o += (int64_t)y * kHeads * p.o_sh;
+  r.sink += y * kHeads;
+  if (r.lse != nullptr) r.lse += y * kHeads;
+  r.part_acc += 2 * gb * kPartAccFloats;
+  r.part_ml += 2 * gb * kPartMlFloats;
+  r.tickets += gb;
+  return r;
+}
 
 __host__ __device__ constexpr size_t ws_acc_bytes(int grid) {
   return ((size_t)2 * grid * kPartAccFloats * sizeof(float) + 255) & ~(size_t)255;

@@ -325,7 +325,8 @@ __global__ void __launch_bounds__(64, 8) sa_combine_kernel(const Params p,
   const bool f_mid = unit_begin(f, U, G) < ts;
   const int np = static_cast<int>(g - f + 1);
 
-  merge_split_row(p, f, np, f_mid, t, blockIdx.y, threadIdx.x * 8);
+  // blockIdx.z: the head group (Params::hg)
+  merge_split_row(group_params(p, blockIdx.z), f, np, f_mid, t, blockIdx.y, threadIdx.x * 8);
 }
 
 // Owner CTAs of the split rows (the combine kernel's blocks).
@@ -344,7 +345,7 @@ cudaError_t launch_combine(const Params& p, cudaStream_t st) {
   const int rows = split_rows(p, &owners);
   if (rows == 0) return cudaSuccess;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(rows), kHeads, 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(rows), kHeads, static_cast<unsigned>(p.hg));
   cfg.blockDim = dim3(64, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;

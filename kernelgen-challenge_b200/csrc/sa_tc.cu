@@ -508,18 +508,19 @@ cudaError_t encode_q_map(const Params& p, CUtensorMap* q_map) {
   // are unchanged (the common case of a serving loop with fixed buffers)
   struct Cached {
     const void* q = nullptr;
-    int64_t m = 0, b = 0, sh = 0, sm = 0, sb = 0;
+    int64_t m = 0, b = 0, sh = 0, sm = 0, sb = 0, heads = 0;
     CUtensorMap map;
   };
   thread_local Cached cache;
+  const int64_t heads = (int64_t)kHeads * (p.hg > 1 ? p.hg : 1);  // every head group's
   if (cache.q == p.q && cache.m == p.m && cache.b == p.b && cache.sh == p.q_sh &&
-      cache.sm == p.q_sm && cache.sb == p.q_sb) {
+      cache.sm == p.q_sm && cache.sb == p.q_sb && cache.heads == heads) {
     *q_map = cache.map;
     return cudaSuccess;
   }
   auto enc = encoder();
   if (enc == nullptr) return cudaErrorNotSupported;
-  cuuint64_t dims[4] = {(cuuint64_t)kDim, (cuuint64_t)kHeads, (cuuint64_t)p.m, (cuuint64_t)p.b};
+  cuuint64_t dims[4] = {(cuuint64_t)kDim, (cuuint64_t)heads, (cuuint64_t)p.m, (cuuint64_t)p.b};
   cuuint64_t strides[3] = {(cuuint64_t)p.q_sh * 2, (cuuint64_t)p.q_sm * 2, (cuuint64_t)p.q_sb * 2};
   cuuint32_t box[4] = {64, (cuuint32_t)kHeads, 1, 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
@@ -533,6 +534,7 @@ cudaError_t encode_q_map(const Params& p, CUtensorMap* q_map) {
   cache.sh = p.q_sh;
   cache.sm = p.q_sm;
   cache.sb = p.q_sb;
+  cache.heads = heads;
   cache.map = *q_map;
   return cudaSuccess;
 }

@@ -318,7 +318,7 @@ __global__ void __launch_bounds__(NT, 1)
       mbar_arrive_expect_tx(smem_u32(&S.q_full), Q_BYTES);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        tma_load_4d(qbase + j * 2048, &q_map, 64 * j, 0, (int32_t)qm, (int32_t)qb,
+        tma_load_4d(qbase + j * 2048, &q_map, 64 * j, kHeads * (int32_t)blockIdx.y, (int32_t)qm, (int32_t)qb,
                     smem_u32(&S.q_full));
     };
     if (tt == 0) issue_q(t_first);
@@ -478,14 +478,16 @@ __global__ void __launch_bounds__(NT, 1)
         // ---------------- epilogue of the segment ending at unit i ----------
         const int64_t tb = t / p.m, tm = t - tb * p.m;
         const float l_lo = lacc[0], l_hi = lacc[2];
+        const int hy = kHeads * (int)blockIdx.y;  // first head of this CTA's group
         if (kRows || (seg_kb0 == 0 && kb == upt - 1)) {
-          const float f_lo = sink_factor(m_lo, l_lo, __ldg(p.sink + g8) * kLog2e);
-          const float f_hi = sink_factor(m_hi, l_hi, __ldg(p.sink + g8 + 8) * kLog2e);
+          const float f_lo = sink_factor(m_lo, l_lo, __ldg(p.sink + hy + g8) * kLog2e);
+          const float f_hi = sink_factor(m_hi, l_hi, __ldg(p.sink + hy + g8 + 8) * kLog2e);
           if (kLse && c == 0 && q4 == 0) {
-            p.lse[t * p.lse_rs + g8] = row_lse2(m_lo, l_lo, __ldg(p.sink + g8) * kLog2e);
-            p.lse[t * p.lse_rs + g8 + 8] = row_lse2(m_hi, l_hi, __ldg(p.sink + g8 + 8) * kLog2e);
+            float* lr = p.lse + t * p.lse_rs + hy;
+            lr[g8] = row_lse2(m_lo, l_lo, __ldg(p.sink + hy + g8) * kLog2e);
+            lr[g8 + 8] = row_lse2(m_hi, l_hi, __ldg(p.sink + hy + g8 + 8) * kLog2e);
           }
-          __nv_bfloat16* ob = p.o + tb * p.o_sb + tm * p.o_sm;
+          __nv_bfloat16* ob = p.o + tb * p.o_sb + tm * p.o_sm + hy * p.o_sh;
 #pragma unroll
           for (int nt = 0; nt < 16; ++nt) {
             const int d = 128 * c + 8 * nt + 2 * q4;
@@ -495,7 +497,7 @@ __global__ void __launch_bounds__(NT, 1)
                 pack_bf16x2(o[nt][2] * f_hi, o[nt][3] * f_hi);
           }
         } else {
-          const int64_t pslot = 2 * g + (t == t_first ? 0 : 1);
+          const int64_t pslot = 2 * (g + G * blockIdx.y) + (t == t_first ? 0 : 1);
           float* pacc = p.part_acc + pslot * kPartAccFloats;
 #pragma unroll
           for (int nt = 0; nt < 16; ++nt) {
@@ -520,8 +522,9 @@ __global__ void __launch_bounds__(NT, 1)
             const int np = static_cast<int>(cta_of_unit(ts + upt - 1, p.units, G) - f + 1);
             __threadfence();
             named_bar(5, NCT);
-            if (tt == 0 && atomicAdd(p.tickets + f, 1) == np - 1) {
-              p.tickets[f] = 0;
+            int* tk = p.tickets + G * blockIdx.y + f;
+            if (tt == 0 && atomicAdd(tk, 1) == np - 1) {
+              *tk = 0;
               S.merge_row[S.n_merge++] = t;  // merged after the last unit (registers free)
             }
           }
@@ -555,6 +558,7 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();
   if (S.n_merge > 0) {
     __threadfence();
+    const Params gp = group_params(p, blockIdx.y);
     for (int r = 0; r < S.n_merge; ++r) {
       const int64_t tr = S.merge_row[r], ts = tr * p.upt;
       const int64_t f = cta_of_unit(ts, p.units, G);
@@ -565,7 +569,7 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int k = k0 + e * NT + tid;
-          merge_split_row(p, f, np, f_mid, tr, k / (kDim / 8), (k % (kDim / 8)) * 8);
+          merge_split_row(gp, f, np, f_mid, tr, k / (kDim / 8), (k % (kDim / 8)) * 8);
         }
       }
     }
@@ -631,7 +635,7 @@ cudaError_t launch_ws(const Params& p, cudaStream_t st) {
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(p.grid), static_cast<unsigned>(p.hg), 1);
   cfg.blockDim = dim3(NT, 1, 1);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = st;

@@ -29,6 +29,7 @@ SA_OPT_SPIN_LIMIT = 3
 SA_OPT_TEST_STALL = 4
 SA_OPT_KV_POLICY = 5
 SA_OPT_GATHER_ONLY = 6
+SA_OPT_HEAD_GROUPS = 7
 
 # every function the header declares, with its ctypes signature
 _I64 = ctypes.c_int64

@@ -156,3 +156,29 @@ def test_new_ops_reject_cpu_tensors():
                                       hc_mult=3)
     with pytest.raises(RuntimeError, match="CUDA"):
         sparse_attn.hc_split_sinkhorn(torch.zeros(1, 1, 24), torch.zeros(3), torch.zeros(24))
+
+
+def test_options_round_trip_on_the_host():
+    """sa_set_option / sa_get_option need no GPU: every option keeps the value
+    set, rejects values outside its range, and the defaults come back."""
+    lib = _lib.lib()
+    cases = {
+        _lib.SA_OPT_ROW_SCHEDULE: (0, 2),
+        _lib.SA_OPT_INDEXER_TC: (0, -1),
+        _lib.SA_OPT_TEST_STALL: (1, 2),
+        _lib.SA_OPT_KV_POLICY: (2, 3),
+        _lib.SA_OPT_GATHER_ONLY: (1, 5),
+        _lib.SA_OPT_HEAD_GROUPS: (0, 2),
+    }
+    for opt, (good, bad) in cases.items():
+        old = lib.sa_get_option(opt)
+        try:
+            assert lib.sa_set_option(opt, good) == _lib.SA_OK
+            assert lib.sa_get_option(opt) == good
+            assert lib.sa_set_option(opt, bad) == _lib.SA_ERR_INVALID_ARG
+            assert lib.sa_get_option(opt) == good
+        finally:
+            assert lib.sa_set_option(opt, old) == _lib.SA_OK
+    assert lib.sa_get_option(_lib.SA_OPT_HEAD_GROUPS) == 1
+    assert lib.sa_get_option(99) == -1
+    assert lib.sa_set_option(99, 0) == _lib.SA_ERR_INVALID_ARG

@@ -14,6 +14,7 @@ from helpers import assert_close, load_golden
 from oracle.sparse_attn_oracle import sparse_attn_oracle
 from sparse_attn import (SA_VARIANT_MMA, SA_VARIANT_TCGEN05, SA_VARIANT_WS, SA_VARIANT_WT,
                          sparse_attn, sparse_attn_out)
+from sparse_attn import _lib
 from sparse_attn import lib as _salib
 from sparse_attn.workloads import CONFIGS, make_inputs
 
@@ -223,6 +224,40 @@ def test_more_heads_strided_q_and_o():
     sparse_attn_out(ob[:, :, 16:16 + h], wide[:, :, 8:8 + h], kvc, sc, ic, scale)
     assert_close(ob[:, :, 16:16 + h], ref, what="strided h=48")
     assert not ob[:, :, :16].any() and not ob[:, :, 16 + h:].any()
+
+
+def _decode_heads_case(h, seed=3, b=6, kv_len=4096, topk=2048):
+    """Decode-shaped rows with many heads: every row split over several CTAs."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(b, 1, h, 512, generator=g).to(torch.bfloat16)
+    kv = torch.randn(b, kv_len, 512, generator=g).to(torch.bfloat16)
+    sink = torch.randn(h, generator=g)
+    idx = torch.stack([torch.randperm(kv_len, generator=g)[:topk] for _ in range(b)])
+    idx = idx.to(torch.int32).reshape(b, 1, topk)
+    idx[2, 0, 1500:] = -1
+    return q, kv, sink, idx, 512 ** -0.5
+
+
+@pytest.mark.parametrize("shape", ["decode", "prefill"])
+@pytest.mark.parametrize("h,grid", [(32, 0), (64, 0), (48, 100), (64, 5)])
+def test_head_groups_one_launch_and_in_turn(shape, h, grid):
+    """h > 16 on the default kernel: all head groups in one launch (the
+    default) and one group after another (SA_OPT_HEAD_GROUPS = 0) both match
+    the oracle, on split decode rows (combine kernel) and on prefill rows."""
+    if shape == "decode":
+        q, kv, sink, idx, scale = _decode_heads_case(h)
+    else:
+        q, kv, sink, idx, scale = _many_heads_case(h, seed=h + grid)
+    ref = sparse_attn_oracle(q, kv, sink, idx, scale)
+    outs = []
+    for mode in (1, 0):
+        old = _lib.set_option(_lib.SA_OPT_HEAD_GROUPS, mode)
+        try:
+            outs.append(run_gpu(q, kv, sink, idx, scale, grid=grid))
+        finally:
+            _lib.set_option(_lib.SA_OPT_HEAD_GROUPS, old)
+        assert_close(outs[-1], ref, what=f"{shape} h={h} grid={grid} head groups mode {mode}")
+    assert _lib.device_status() == 0
 
 
 def _ragged_case(seed=11):
