@@ -98,8 +98,8 @@ int sa_fwd_train(const void* q, const void* kv, const float* sink, const int32_t
  * output o, its lse from sa_fwd_train (or NULL: recomputed by a first pass)
  * and the upstream gradient dout (laid out like o: o_strides), writes
  * dq (bf16, contiguous [b, m, h, 512]) and ADDS into dkv (fp32 [b, kv_len, 512],
- * element strides dkv_strides, 8-byte aligned) and dsink (fp32 [h]); zero
- * those two first for a plain gradient.  Masked slots (-1 or out of range)
+ * element strides dkv_strides, multiples of 4, 16-byte aligned) and dsink
+ * (fp32 [h]); zero those two first for a plain gradient.  Masked slots (-1 or out of range)
  * contribute nothing; duplicated indices add.  The math is the gradient of
  * the reference forward (track-01/reference/reference.py:24-40), which has no
  * backward of its own. */

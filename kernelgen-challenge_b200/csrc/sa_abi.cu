@@ -521,12 +521,12 @@ static int bwd_group(const void* q, const void* kv, const float* sink, const int
   if (q_strides[3] != 1 || kv_strides[2] != 1 || o_strides[3] != 1 || dkv_strides[2] != 1)
     return SA_ERR_INVALID_ARG;
   if (!aligned16(q) || !aligned16(kv) || !aligned16(o) || !aligned16(dout) || !aligned16(dq) ||
-      (reinterpret_cast<uintptr_t>(dkv) & 7u) != 0 || (reinterpret_cast<uintptr_t>(idx) & 3u) != 0)
+      (reinterpret_cast<uintptr_t>(dkv) & 15u) != 0 || (reinterpret_cast<uintptr_t>(idx) & 3u) != 0)
     return SA_ERR_INVALID_ARG;
   for (int i = 0; i < 3; ++i)
     if ((q_strides[i] % 8) != 0 || (o_strides[i] % 8) != 0) return SA_ERR_INVALID_ARG;
   for (int i = 0; i < 2; ++i)
-    if ((kv_strides[i] % 8) != 0 || (dkv_strides[i] % 2) != 0) return SA_ERR_INVALID_ARG;
+    if ((kv_strides[i] % 8) != 0 || (dkv_strides[i] % 4) != 0) return SA_ERR_INVALID_ARG;
   if (kv_len > INT32_MAX || b * m > INT32_MAX) return SA_ERR_INVALID_ARG;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

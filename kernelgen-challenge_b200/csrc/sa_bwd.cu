@@ -22,8 +22,9 @@
 //           dS = P (dP - D) * scale into shared memory (bf16), then
 //           dq[16 x 64w..64w+63] += dS . K   (registers, whole row)
 //           dkv [16 keys of group w & 3 x 256 columns of half w >> 2]
-//             = dS^T . Q + P^T . dO in 64-column chunks, added into an fp32
-//             gradient buffer with 8-byte atomics (masked slots skip)
+//             = dS^T . Q + P^T . dO in 64-column chunks, staged in shared
+//             memory and added into an fp32 gradient buffer by TMA bulk
+//             reductions, 256 bytes per key (masked slots skip)
 // All products are bf16 warp MMAs with fp32 accumulation.
 #include "sa_common.cuh"
 
@@ -60,6 +61,10 @@ struct __align__(1024) Smem {
   float D[kHeads];
   float M[kHeads];      // log2-domain max including the sink
   float invZ[kHeads];
+  // per warp: its [16 keys x 64 cols] fp32 dkv chunk, rows padded to 288 bytes
+  // (the fragment stores of a half-warp hit 32 distinct banks), read by the
+  // bulk reductions
+  float dk[NW][16][72];
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 
@@ -71,8 +76,32 @@ __device__ __forceinline__ uint32_t t_chunk(int h, int c) {
   return (c >> 3) * 2048 + h * 128 + (((c & 7) ^ (h & 7)) << 4);
 }
 
-__device__ __forceinline__ void red_add_f2(float* addr, float a, float b) {
-  atomicAdd(reinterpret_cast<float2*>(addr), make_float2(a, b));
+// dst[0..bytes) += src (fp32, element-wise, in L2), by the TMA unit; both
+// addresses 16-byte aligned, bytes a multiple of 16
+__device__ __forceinline__ void bulk_reduce_add_f32(float* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;\n" ::"l"(
+                   dst),
+               "r"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+}
+// all but this thread's newest N bulk-operation groups have finished
+// reading shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(N) : "memory");
+}
+// ... and are complete
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ void sts64f(uint32_t addr, float a, float b) {
+  asm volatile("st.shared.v2.f32 [%0], {%1,%2};\n" ::"r"(addr), "f"(a), "f"(b) : "memory");
 }
 
 __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
@@ -313,10 +342,10 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
       uint32_t ad[4], ap[4];
       ldmatrix_x4_trans(ad, dsbase + p_chunk(hr, kc));
       ldmatrix_x4_trans(ap, pbase + p_chunk(hr, kc));
-      const int key_lo = 16 * kg + g8, key_hi = key_lo + 8;
-      const int32_t id_lo = S.ids[s][key_lo], id_hi = S.ids[s][key_hi];
-      float* dlo = bp.dkv + tb * bp.dkv_sb + (int64_t)(id_lo < 0 ? 0 : id_lo) * bp.dkv_sn;
-      float* dhi = bp.dkv + tb * bp.dkv_sb + (int64_t)(id_hi < 0 ? 0 : id_hi) * bp.dkv_sn;
+      // lanes 0..15 add key 16kg + lane's row of each chunk
+      const int32_t id_mine = lane < 16 ? S.ids[s][16 * kg + lane] : -1;
+      float* drow = bp.dkv + tb * bp.dkv_sb + (int64_t)(id_mine < 0 ? 0 : id_mine) * bp.dkv_sn;
+      const uint32_t stage = smem_u32(&S.dk[warp][0][0]);
       // B-fragments (k = heads, n = columns) by transposed loads of the Q / dO
       // tiles: matrices (heads 0-7 | 8-15) x (columns n0..n0+7 | n0+8..n0+15)
       const int br = (lane & 7) + 8 * (mt & 1), bcol = (mt >> 1);
@@ -336,17 +365,30 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
           mma_16816(acc[2 * np], ap, bd[0], bd[1]);
           mma_16816(acc[2 * np + 1], ap, bd[2], bd[3]);
         }
+        // the chunk to the warp's stage (once the previous chunk's reductions
+        // have read it), then one 256-byte bulk reduction per valid key.
+        // (Two 128-byte stages, one filled while the other's reductions run,
+        // were slower: the reductions' cost grows with their count.)
+        bulk_wait_read<0>();
+        __syncwarp();
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
-          const int col = 64 * cb + 8 * nt + 2 * q4;
-          if (id_lo >= 0) red_add_f2(dlo + col, acc[nt][0], acc[nt][1]);
-          if (id_hi >= 0) red_add_f2(dhi + col, acc[nt][2], acc[nt][3]);
+          const uint32_t c4 = (8 * nt + 2 * q4) * 4;
+          sts64f(stage + g8 * 288 + c4, acc[nt][0], acc[nt][1]);
+          sts64f(stage + (g8 + 8) * 288 + c4, acc[nt][2], acc[nt][3]);
+        }
+        fence_proxy_async_smem();  // the stores precede the reductions' reads
+        __syncwarp();
+        if (id_mine >= 0) {
+          bulk_reduce_add_f32(drow + 64 * cb, stage + lane * 288, 256);
+          bulk_commit();
         }
       }
     }
     __syncthreads();  // slot s and the P / dS tiles free
   }
   cp_async_wait<0>();  // (no units: the Q / dO copies)
+  bulk_wait();         // the dkv reductions are done before the CTA exits
   // ---- dq of this row (the scale is already in dS)
   __nv_bfloat16* dqr = bp.dq + row * bp.dq_rs;
 #pragma unroll
