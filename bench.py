@@ -400,61 +400,124 @@ def measure_e2e(idx_maker, q, kv, kscale, sink, idx, dev, stream, flush, K, barr
             sparse_attn.sparse_attn_out(o, qd, kv, sink, idd, SCALE)
         return o
 
-    # One CUDA graph holds S steps, each with its own device buffers: the
-    # host-to-device copies run in order on one copy stream, step j's op waits
-    # only for its own inputs (so it overlaps the copies of later steps), and
-    # its device-to-host copy runs on a second copy stream.  Replaying the
-    # graph keeps the host out of the loop, as a decode server does.  S is as
-    # large as 256 MiB of step buffers allows (32 at decode): every graph
-    # boundary drains the pipeline once.
+    cin, cout = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     step_bytes = qb + ib + qb
     S = int(max(2, min(32, (256 << 20) // step_bytes)))
-    cin, cout = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    slab_d = [torch.empty(qb + ib, dtype=torch.uint8, device=dev) for _ in range(S)]
-    qd = [x[:qb].view(q.dtype).view(q.shape) for x in slab_d]
-    idd = [x[qb:].view(idx.dtype).view(idx.shape) for x in slab_d]
-    od = [torch.empty_like(q) for _ in range(S)]
-    o_hs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(S)]
-    op_out(od[0], qd[0].copy_(q), idd[0].copy_(idx))  # workspace of the capture stream, module loads
-    torch.cuda.synchronize()
-    graphs = []
-    for gi in range(nset):  # one graph per rotation of the index sets
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr):
-            cs = torch.cuda.current_stream()
-            cin.wait_stream(cs)
-            cout.wait_stream(cs)
-            ins = []
-            with torch.cuda.stream(cin):
+    if S >= 8:
+        # Short steps (decode, MTP): one CUDA graph holds S steps, each with its
+        # own device buffers: the host-to-device copies run in order on one
+        # copy stream, step j's op waits only for its own inputs (so it
+        # overlaps the copies of later steps), and its device-to-host copy runs
+        # on a second copy stream.  Replaying the graph keeps the host out of
+        # the loop, as a decode server does.  S is as large as 256 MiB of step
+        # buffers allows (32 at decode): every graph boundary drains the
+        # pipeline once.
+        slab_d = [torch.empty(qb + ib, dtype=torch.uint8, device=dev) for _ in range(S)]
+        qd = [x[:qb].view(q.dtype).view(q.shape) for x in slab_d]
+        idd = [x[qb:].view(idx.dtype).view(idx.shape) for x in slab_d]
+        od = [torch.empty_like(q) for _ in range(S)]
+        o_hs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(S)]
+        op_out(od[0], qd[0].copy_(q), idd[0].copy_(idx))  # workspace of the capture stream
+        torch.cuda.synchronize()
+        graphs = []
+        for gi in range(nset):  # one graph per rotation of the index sets
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                cs = torch.cuda.current_stream()
+                cin.wait_stream(cs)
+                cout.wait_stream(cs)
+                ins = []
+                with torch.cuda.stream(cin):
+                    for j in range(S):
+                        slab_d[j].copy_(slab_h[(gi * S + j) % nset], non_blocking=True)
+                        ev = torch.cuda.Event()
+                        ev.record(cin)
+                        ins.append(ev)
                 for j in range(S):
-                    slab_d[j].copy_(slab_h[(gi * S + j) % nset], non_blocking=True)
+                    cs.wait_event(ins[j])
+                    out = op_out(od[j], qd[j], idd[j])
                     ev = torch.cuda.Event()
-                    ev.record(cin)
-                    ins.append(ev)
-            for j in range(S):
-                cs.wait_event(ins[j])
-                out = op_out(od[j], qd[j], idd[j])
-                ev = torch.cuda.Event()
-                ev.record(cs)
+                    ev.record(cs)
+                    with torch.cuda.stream(cout):
+                        cout.wait_event(ev)
+                        o_hs[j].copy_(out, non_blocking=True)
+                cs.wait_stream(cin)
+                cs.wait_stream(cout)
+            graphs.append(gr)
+        reps = max(1, ke // S)
+        for gr in graphs:
+            gr.replay()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        t0.record(stream)
+        for r in range(reps):
+            graphs[r % nset].replay()
+        t1.record(stream)
+        barrier()
+        p_ms = t0.elapsed_time(t1)
+        ke_p = reps * S
+        how = (f"CUDA graphs of {S} steps replayed: each step's H2D copy of q and the indices "
+               "(one pinned slab), op into a preallocated o, D2H copy of o; copies of later "
+               "steps overlap the op of earlier ones (two copy streams); 4 rotating index "
+               "sets instead of an L2 flush")
+    else:
+        # Long steps (prefill): the same pipeline driven from the host without
+        # graphs (the host's enqueue time is small against a step), over NB
+        # rotating buffer sets, so it never drains: step k's H2D copy waits only
+        # until op k - NB has read its slab, its op for its inputs and for the
+        # D2H copy of step k - NB to have read its output buffer.  The copies
+        # of steps k + 1 and k - 1 run during op k on the two copy streams.
+        NB = 3
+        slab_d = [torch.empty(qb + ib, dtype=torch.uint8, device=dev) for _ in range(NB)]
+        qd = [x[:qb].view(q.dtype).view(q.shape) for x in slab_d]
+        idd = [x[qb:].view(idx.dtype).view(idx.shape) for x in slab_d]
+        od = [torch.empty_like(q) for _ in range(NB)]
+        o_hs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(NB)]
+        cs = stream
+        op_done = [torch.cuda.Event() for _ in range(NB)]
+        in_done = [torch.cuda.Event() for _ in range(NB)]
+        out_done = [torch.cuda.Event() for _ in range(NB)]
+
+        def run(first, n):
+            for k in range(first, first + n):
+                j = k % NB
+                with torch.cuda.stream(cin):
+                    if k >= NB:
+                        cin.wait_event(op_done[j])
+                    slab_d[j].copy_(slab_h[k % nset], non_blocking=True)
+                    in_done[j].record(cin)
+                cs.wait_event(in_done[j])
+                if k >= NB:
+                    cs.wait_event(out_done[j])
+                with torch.cuda.stream(cs):
+                    op_out(od[j], qd[j], idd[j])
+                op_done[j].record(cs)
                 with torch.cuda.stream(cout):
-                    cout.wait_event(ev)
-                    o_hs[j].copy_(out, non_blocking=True)
-            cs.wait_stream(cin)
-            cs.wait_stream(cout)
-        graphs.append(gr)
-    reps = max(1, ke // S)
-    for gr in graphs:
-        gr.replay()
-    torch.cuda.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    t0.record(stream)
-    for r in range(reps):
-        graphs[r % nset].replay()
-    t1.record(stream)
-    barrier()
-    p_ms = t0.elapsed_time(t1)
-    ke_p = reps * S
+                    cout.wait_event(op_done[j])
+                    o_hs[j].copy_(od[j], non_blocking=True)
+                    out_done[j].record(cout)
+
+        ke_p = max(ke, 3 * NB)
+        run(0, NB)  # warm-up: workspace, module loads
+        cs.wait_stream(cin)
+        cs.wait_stream(cout)
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        t0.record(cs)
+        run(NB, ke_p)
+        cs.wait_stream(cin)
+        cs.wait_stream(cout)
+        t1.record(cs)
+        barrier()
+        torch.cuda.synchronize()
+        p_ms = t0.elapsed_time(t1)
+        how = (f"{NB} rotating buffer sets driven from the host (no graph, no drain): each "
+               "step's H2D copy of q and the indices (one pinned slab), op into a "
+               "preallocated o, D2H copy of o; the copies of the next and previous steps "
+               "overlap each op (two copy streams); 4 rotating index sets instead of an "
+               "L2 flush")
 
     # serial: copy in, op, copy out on one stream, L2 flushed before each step
     def serial_step(k):  # the drop-in call, as a caller with no staging would make it
@@ -484,10 +547,7 @@ def measure_e2e(idx_maker, q, kv, kscale, sink, idx, dev, stream, flush, K, barr
             "d2h_bytes_per_step": q.numel() * q.element_size(),
             "steps": ke_p, "kv_cache_resident": True,
             "api": "sparse_attn.sparse_attn_fp8_out" if fp8 else "sparse_attn.sparse_attn_out",
-            "pipelined": f"CUDA graphs of {S} steps replayed: each step's H2D copy of q and "
-                         "the indices (one pinned slab), op into a preallocated o, D2H copy "
-                         "of o; copies of later steps overlap the op of earlier ones (two "
-                         "copy streams); 4 rotating index sets instead of an L2 flush",
+            "pipelined": how,
             "serial": {"value": job_tokens * ke / (s_ms / 1e3),
                        "api": "sparse_attn.sparse_attn_fp8" if fp8 else "sparse_attn.sparse_attn",
                        "note": "no overlap, two H2D copies, 256 MiB L2 flush before every "
