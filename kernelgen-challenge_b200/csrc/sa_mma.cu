@@ -325,8 +325,11 @@ __global__ void __launch_bounds__(64, 8) sa_combine_kernel(const Params p,
   const bool f_mid = unit_begin(f, U, G) < ts;
   const int np = static_cast<int>(g - f + 1);
 
-  // blockIdx.z: the head group (Params::hg)
-  merge_split_row(group_params(p, blockIdx.z), f, np, f_mid, t, blockIdx.y, threadIdx.x * 8);
+  if (p.hg > 1) {  // blockIdx.z: the head group (Params::hg)
+    merge_split_row(group_params(p, blockIdx.z), f, np, f_mid, t, blockIdx.y, threadIdx.x * 8);
+  } else {
+    merge_split_row(p, f, np, f_mid, t, blockIdx.y, threadIdx.x * 8);
+  }
 }
 
 // Owner CTAs of the split rows (the combine kernel's blocks).

@@ -158,7 +158,10 @@ __global__ void __launch_bounds__(256) sa_row_units_kernel(const Params p, int* 
 // kGatherOnly (diagnostic, SA_OPT_GATHER_ONLY): the same pipeline, but the
 // consumers release each unit as soon as it lands and compute nothing; the
 // output is left unwritten.  Its time is the gather's share of the kernel.
-template <bool kLse, bool kRows, bool kGatherOnly = false>
+// kGroups: several head groups in one launch (Params::hg, blockIdx.y = the
+// group); separate instances, since the group offsets alone cost the
+// single-group kernel 6-10 % at decode and MTP shapes.
+template <bool kLse, bool kRows, bool kGatherOnly = false, bool kGroups = false>
 __global__ void __launch_bounds__(NT, 1)
     sa_ws_fwd_kernel(const Params p, const __grid_constant__ CUtensorMap q_map) {
   extern __shared__ uint8_t smem_raw[];
@@ -318,7 +321,7 @@ __global__ void __launch_bounds__(NT, 1)
       mbar_arrive_expect_tx(smem_u32(&S.q_full), Q_BYTES);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        tma_load_4d(qbase + j * 2048, &q_map, 64 * j, kHeads * (int32_t)blockIdx.y, (int32_t)qm, (int32_t)qb,
+        tma_load_4d(qbase + j * 2048, &q_map, 64 * j, kGroups ? kHeads * (int32_t)blockIdx.y : 0, (int32_t)qm, (int32_t)qb,
                     smem_u32(&S.q_full));
     };
     if (tt == 0) issue_q(t_first);
@@ -478,7 +481,7 @@ __global__ void __launch_bounds__(NT, 1)
         // ---------------- epilogue of the segment ending at unit i ----------
         const int64_t tb = t / p.m, tm = t - tb * p.m;
         const float l_lo = lacc[0], l_hi = lacc[2];
-        const int hy = kHeads * (int)blockIdx.y;  // first head of this CTA's group
+        const int hy = kGroups ? kHeads * (int)blockIdx.y : 0;  // first head of this CTA's group
         if (kRows || (seg_kb0 == 0 && kb == upt - 1)) {
           const float f_lo = sink_factor(m_lo, l_lo, __ldg(p.sink + hy + g8) * kLog2e);
           const float f_hi = sink_factor(m_hi, l_hi, __ldg(p.sink + hy + g8 + 8) * kLog2e);
@@ -497,7 +500,7 @@ __global__ void __launch_bounds__(NT, 1)
                 pack_bf16x2(o[nt][2] * f_hi, o[nt][3] * f_hi);
           }
         } else {
-          const int64_t pslot = 2 * (g + G * blockIdx.y) + (t == t_first ? 0 : 1);
+          const int64_t pslot = 2 * (kGroups ? g + G * blockIdx.y : g) + (t == t_first ? 0 : 1);
           float* pacc = p.part_acc + pslot * kPartAccFloats;
 #pragma unroll
           for (int nt = 0; nt < 16; ++nt) {
@@ -522,7 +525,7 @@ __global__ void __launch_bounds__(NT, 1)
             const int np = static_cast<int>(cta_of_unit(ts + upt - 1, p.units, G) - f + 1);
             __threadfence();
             named_bar(5, NCT);
-            int* tk = p.tickets + G * blockIdx.y + f;
+            int* tk = p.tickets + (kGroups ? G * blockIdx.y : 0) + f;
             if (tt == 0 && atomicAdd(tk, 1) == np - 1) {
               *tk = 0;
               S.merge_row[S.n_merge++] = t;  // merged after the last unit (registers free)
@@ -558,7 +561,7 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();
   if (S.n_merge > 0) {
     __threadfence();
-    const Params gp = group_params(p, blockIdx.y);
+    const Params gp = kGroups ? group_params(p, blockIdx.y) : p;
     for (int r = 0; r < S.n_merge; ++r) {
       const int64_t tr = S.merge_row[r], ts = tr * p.upt;
       const int64_t f = cta_of_unit(ts, p.units, G);
@@ -621,7 +624,11 @@ cudaError_t launch_ws(const Params& p, cudaStream_t st) {
   e = once_per_device(attr_once, [] {
     for (auto* k : {sa_ws_fwd_kernel<false, false>, sa_ws_fwd_kernel<true, false>,
                     sa_ws_fwd_kernel<false, true>, sa_ws_fwd_kernel<true, true>,
-                    sa_ws_fwd_kernel<false, false, true>, sa_ws_fwd_kernel<false, true, true>}) {
+                    sa_ws_fwd_kernel<false, false, true>, sa_ws_fwd_kernel<false, true, true>,
+                    sa_ws_fwd_kernel<false, false, false, true>,
+                    sa_ws_fwd_kernel<true, false, false, true>,
+                    sa_ws_fwd_kernel<false, true, false, true>,
+                    sa_ws_fwd_kernel<true, true, false, true>}) {
       const cudaError_t e1 =
           cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
       if (e1 != cudaSuccess) return e1;
@@ -646,7 +653,13 @@ cudaError_t launch_ws(const Params& p, cudaStream_t st) {
   cfg.numAttrs = 1;
   auto* kern = p.lse != nullptr ? (rows ? sa_ws_fwd_kernel<true, true> : sa_ws_fwd_kernel<true, false>)
                                 : (rows ? sa_ws_fwd_kernel<false, true> : sa_ws_fwd_kernel<false, false>);
-  if (opt_gather_only() && p.lse == nullptr)
+  if (p.hg > 1)
+    kern = p.lse != nullptr
+               ? (rows ? sa_ws_fwd_kernel<true, true, false, true>
+                       : sa_ws_fwd_kernel<true, false, false, true>)
+               : (rows ? sa_ws_fwd_kernel<false, true, false, true>
+                       : sa_ws_fwd_kernel<false, false, false, true>);
+  else if (opt_gather_only() && p.lse == nullptr)
     kern = rows ? sa_ws_fwd_kernel<false, true, true> : sa_ws_fwd_kernel<false, false, true>;
   e = cudaLaunchKernelEx(&cfg, kern, p, q_map);
   if (e != cudaSuccess || p.merge_in_kernel || rows) return e;
