@@ -110,6 +110,23 @@ int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx,
            const int64_t kv_strides[3], const int64_t idx_strides[3], const int64_t o_strides[4],
            const int64_t dkv_strides[3], float scale, void* stream);
 
+/* The kv rows that one call's valid slots name (idx as for sa_fwd), in a
+ * dense fp32 KV gradient laid out like the dkv of sa_bwd (strides multiples
+ * of 4, 16-byte aligned).  A decode-shaped backward touches only
+ * b * m * topk of the b * kv_len rows, so a caller that needs the dense
+ * gradient can zero just those rows of an uninitialised fp32 buffer before
+ * sa_bwd (sa_dkv_zero_rows) and afterwards cast just those rows into a
+ * zero-filled bf16 gradient (sa_dkv_cast_rows: out rows of 512 bf16,
+ * strides out_strides, multiples of 4, 8-byte aligned).  Masked slots touch
+ * nothing; duplicated indices repeat the same stores.  No counterpart in the
+ * reference, which has no backward. */
+int sa_dkv_zero_rows(float* dkv, const int32_t* idx, int64_t b, int64_t m, int64_t topk,
+                     int64_t kv_len, const int64_t idx_strides[3], const int64_t dkv_strides[3],
+                     void* stream);
+int sa_dkv_cast_rows(const float* dkv, void* out, const int32_t* idx, int64_t b, int64_t m,
+                     int64_t topk, int64_t kv_len, const int64_t idx_strides[3],
+                     const int64_t dkv_strides[3], const int64_t out_strides[3], void* stream);
+
 /* Top-k index producer (lightning indexer): the step that feeds topk_idxs.
  * The reference takes topk_idxs as an input and has none (track-01/
  * requirements.md:1-5); this follows the published DeepSeek-V3.2 indexer:

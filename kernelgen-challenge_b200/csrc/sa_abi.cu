@@ -54,6 +54,10 @@ cudaError_t launch_bwd(const Params& f, const __nv_bfloat16* dout, __nv_bfloat16
                        int64_t dq_rs, float* dkv,
                        float* dsink, int64_t dkv_sb, int64_t dkv_sn, float scale,
                        cudaStream_t st);
+cudaError_t launch_dkv_rows(bool cast, float* dkv, __nv_bfloat16* out, const int32_t* idx,
+                            int64_t b, int64_t m, int64_t topk, int64_t kv_len,
+                            const int64_t idx_strides[3], const int64_t dkv_strides[3],
+                            const int64_t out_strides[3], int sms, cudaStream_t st);
 }  // namespace sa
 
 namespace {
@@ -655,6 +659,51 @@ int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx,
     if (rc != SA_OK) return rc;
   }
   return SA_OK;
+}
+
+// sa_dkv_zero_rows / sa_dkv_cast_rows: the kv rows one call's valid slots
+// name, in a dense gradient.
+static int dkv_rows(bool cast, float* dkv, void* out, const int32_t* idx, int64_t b, int64_t m,
+                    int64_t topk, int64_t kv_len, const int64_t idx_strides[3],
+                    const int64_t dkv_strides[3], const int64_t out_strides[3], void* stream) {
+  t_last_cuda_error = 0;
+  if (b < 0 || m < 0 || topk < 0 || kv_len < 0) return SA_ERR_INVALID_ARG;
+  if (b == 0 || m == 0 || topk == 0) return SA_OK;
+  if (!dkv || !idx || !idx_strides || !dkv_strides || (cast && (!out || !out_strides)))
+    return SA_ERR_INVALID_ARG;
+  if (dkv_strides[2] != 1 || (cast && out_strides[2] != 1)) return SA_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(dkv) & 15u) != 0 || (reinterpret_cast<uintptr_t>(idx) & 3u) != 0)
+    return SA_ERR_INVALID_ARG;
+  if (cast && (reinterpret_cast<uintptr_t>(out) & 7u) != 0) return SA_ERR_INVALID_ARG;
+  for (int i = 0; i < 2; ++i) {
+    if ((dkv_strides[i] % 4) != 0) return SA_ERR_INVALID_ARG;
+    if (cast && (out_strides[i] % 4) != 0) return SA_ERR_INVALID_ARG;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e);
+  const DeviceInfo* di = device_info(dev);
+  if (di == nullptr) return SA_ERR_UNSUPPORTED;
+  if (di->err != cudaSuccess) return fail_cuda(di->err);
+  e = sa::launch_dkv_rows(cast, dkv, static_cast<__nv_bfloat16*>(out), idx, b, m, topk, kv_len,
+                          idx_strides, dkv_strides, out_strides, di->sms,
+                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail_cuda(e);
+  return SA_OK;
+}
+
+int sa_dkv_zero_rows(float* dkv, const int32_t* idx, int64_t b, int64_t m, int64_t topk,
+                     int64_t kv_len, const int64_t idx_strides[3], const int64_t dkv_strides[3],
+                     void* stream) {
+  return dkv_rows(false, dkv, nullptr, idx, b, m, topk, kv_len, idx_strides, dkv_strides,
+                  nullptr, stream);
+}
+
+int sa_dkv_cast_rows(const float* dkv, void* out, const int32_t* idx, int64_t b, int64_t m,
+                     int64_t topk, int64_t kv_len, const int64_t idx_strides[3],
+                     const int64_t dkv_strides[3], const int64_t out_strides[3], void* stream) {
+  return dkv_rows(true, const_cast<float*>(dkv), out, idx, b, m, topk, kv_len, idx_strides,
+                  dkv_strides, out_strides, stream);
 }
 
 size_t sa_indexer_workspace_bytes(int64_t b, int64_t m, int64_t kv_len) {

@@ -401,6 +401,66 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
 
 }  // namespace bwd_path
 
+// ---------------------------------------------------------------------------
+// The rows of a dense KV gradient that one call touches: the kv rows its
+// valid slots name.  Decode-shaped calls touch far fewer rows than the cache
+// holds (b = 64 x 2048 slots of a 32,768-row cache), so the fp32 buffer the
+// backward kernel adds into is zeroed, and cast to bf16, on those rows only.
+// One warp per (b, m, slot); each instruction of the warp covers 512
+// contiguous bytes of the row.  Duplicated indices repeat the same stores.
+struct RowsParams {
+  float* dkv;                // fp32 [b][kv_len][512], strides dkv_sb, dkv_sn
+  __nv_bfloat16* out;        // kCast: bf16 rows, strides out_sb, out_sn
+  const int32_t* idx;
+  int64_t b, m, topk, kv_len;
+  int64_t i_sb, i_sm, i_sk, dkv_sb, dkv_sn, out_sb, out_sn;
+};
+
+template <bool kCast>
+__global__ void __launch_bounds__(256) sa_dkv_rows_kernel(const RowsParams rp) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nslot = rp.b * rp.m * rp.topk;
+  for (int64_t w = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); w < nslot;
+       w += (int64_t)gridDim.x * 8) {
+    const int64_t r = w / rp.topk, k = w - r * rp.topk;
+    const int64_t tb = r / rp.m, tm = r - tb * rp.m;
+    const int32_t id = __ldg(rp.idx + tb * rp.i_sb + tm * rp.i_sm + k * rp.i_sk);
+    if (id < 0 || (int64_t)id >= rp.kv_len) continue;  // masked: no row touched
+    float4* row = reinterpret_cast<float4*>(rp.dkv + tb * rp.dkv_sb + (int64_t)id * rp.dkv_sn);
+    if constexpr (kCast) {
+      uint2* orow = reinterpret_cast<uint2*>(rp.out + tb * rp.out_sb + (int64_t)id * rp.out_sn);
+      float4 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = __ldcg(row + lane + 32 * j);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        orow[lane + 32 * j] = make_uint2(pack_bf16x2(v[j].x, v[j].y), pack_bf16x2(v[j].z, v[j].w));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) row[lane + 32 * j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+}
+
+cudaError_t launch_dkv_rows(bool cast, float* dkv, __nv_bfloat16* out, const int32_t* idx,
+                            int64_t b, int64_t m, int64_t topk, int64_t kv_len,
+                            const int64_t idx_strides[3], const int64_t dkv_strides[3],
+                            const int64_t out_strides[3], int sms, cudaStream_t st) {
+  RowsParams rp{dkv, out, idx, b, m, topk, kv_len,
+                idx_strides[0], idx_strides[1], idx_strides[2], dkv_strides[0], dkv_strides[1],
+                cast ? out_strides[0] : 0, cast ? out_strides[1] : 0};
+  const int64_t nslot = b * m * topk;
+  if (nslot == 0) return cudaSuccess;
+  int64_t blocks = (nslot + 7) / 8;
+  if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;
+  if (cast) {
+    sa_dkv_rows_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, st>>>(rp);
+  } else {
+    sa_dkv_rows_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, st>>>(rp);
+  }
+  return cudaGetLastError();
+}
+
 cudaError_t launch_bwd(const Params& f, const __nv_bfloat16* dout, __nv_bfloat16* dq,
                        int64_t dq_rs, float* dkv, float* dsink, int64_t dkv_sb, int64_t dkv_sn, float scale,
                        cudaStream_t st) {

@@ -229,13 +229,26 @@ def sparse_attn_backward(q, kv, attn_sink, topk_idxs, scale, o, do, lse=None):
     kv_c = kv if _row_ok(kv) else kv.contiguous()
     o_c, do_c = o.contiguous(), do.to(q.dtype).contiguous()
     dq = torch.empty(b, m, h, d, dtype=q.dtype, device=q.device)
-    dkv = torch.zeros(kv.shape, dtype=torch.float32, device=q.device)
+    topk = topk_idxs.shape[-1]
+    # Few touched rows (m * topk < kv_len: decode, MTP): the fp32 buffer is
+    # zeroed, and cast to the bf16 gradient, on the rows the valid slots name
+    # only; the rest of the bf16 gradient is a plain zero fill.
+    rows_only = m * topk < kv.shape[1] and b * m > 0
+    if rows_only:
+        dkv = torch.empty(kv.shape, dtype=torch.float32, device=q.device)
+    else:
+        dkv = torch.zeros(kv.shape, dtype=torch.float32, device=q.device)
     dsink = torch.zeros(h, dtype=torch.float32, device=q.device)
     if dq.numel() == 0:
         return dq, dkv.to(kv.dtype), dsink.to(attn_sink.dtype)
     with torch.cuda.device(q.device):
         st = torch.cuda.current_stream(q.device)
         lse_c = None if lse is None else lse.float().contiguous()
+        ids = (b, m, topk, kv.shape[1], _lib.i64_array(topk_idxs.stride()))
+        if rows_only:
+            _lib.check(_lib.lib().sa_dkv_zero_rows(
+                dkv.data_ptr(), topk_idxs.data_ptr(), *ids[:4], ids[4],
+                _lib.i64_array(dkv.stride()), st.cuda_stream))
         _lib.check(_lib.lib().sa_bwd(
             q_c.data_ptr(), kv_c.data_ptr(), attn_sink.contiguous().data_ptr(),
             topk_idxs.data_ptr(), o_c.data_ptr(), do_c.data_ptr(),
@@ -244,6 +257,12 @@ def sparse_attn_backward(q, kv, attn_sink, topk_idxs, scale, o, do, lse=None):
             _lib.i64_array(q_c.stride()), _lib.i64_array(kv_c.stride()),
             _lib.i64_array(topk_idxs.stride()), _lib.i64_array(o_c.stride()),
             _lib.i64_array(dkv.stride()), float(scale), st.cuda_stream))
+        if rows_only:
+            out = torch.zeros(kv.shape, dtype=kv.dtype, device=q.device)
+            _lib.check(_lib.lib().sa_dkv_cast_rows(
+                dkv.data_ptr(), out.data_ptr(), topk_idxs.data_ptr(), *ids[:4], ids[4],
+                _lib.i64_array(dkv.stride()), _lib.i64_array(out.stride()), st.cuda_stream))
+            return dq, out, dsink.to(attn_sink.dtype)
     return dq, dkv.to(kv.dtype), dsink.to(attn_sink.dtype)
 
 

@@ -126,6 +126,26 @@ def test_backward_entry_validates_before_any_gpu_work():
     assert bwd(dkv_strides=(2048, 511, 1)) == _lib.SA_ERR_INVALID_ARG
 
 
+def test_dkv_row_entries_validate_before_any_gpu_work():
+    L = _lib.lib()
+    ist, dst = _i64(8, 4, 1), _i64(2048, 512, 1)
+
+    def zero(dkv=16, b=1, topk=4, strides=(2048, 512, 1)):
+        return L.sa_dkv_zero_rows(dkv, 16, b, 1, topk, 4, ist, _i64(*strides), None)
+
+    def cast(out=16, strides=(2048, 512, 1)):
+        return L.sa_dkv_cast_rows(16, out, 16, 1, 1, 4, 4, ist, dst, _i64(*strides), None)
+    assert zero(b=0) == _lib.SA_OK and zero(topk=0) == _lib.SA_OK
+    assert zero(b=-1) == _lib.SA_ERR_INVALID_ARG
+    assert zero(dkv=0) == _lib.SA_ERR_INVALID_ARG
+    assert zero(dkv=8) == _lib.SA_ERR_INVALID_ARG                   # fp32 rows 16-byte aligned
+    assert zero(strides=(2048, 510, 1)) == _lib.SA_ERR_INVALID_ARG
+    assert zero(strides=(2048, 512, 2)) == _lib.SA_ERR_INVALID_ARG
+    assert cast(out=0) == _lib.SA_ERR_INVALID_ARG
+    assert cast(out=4) == _lib.SA_ERR_INVALID_ARG                   # bf16 rows 8-byte aligned
+    assert cast(strides=(2048, 514, 1)) == _lib.SA_ERR_INVALID_ARG
+
+
 def test_sinkhorn_entry_validates_before_any_gpu_work():
     L = _lib.lib()
 

@@ -52,6 +52,34 @@ def test_backward_decode_rows():
     _check(q, kv, sink, idx, scale, seed=1, what="decode b=4")
 
 
+def test_backward_touched_rows_only():
+    """m * topk < kv_len: the fp32 gradient is zeroed and cast on the rows the
+    valid slots name only.  Duplicated, -1 and out-of-range indices, a fully
+    masked row; every row no valid slot names is exactly zero."""
+    g = torch.Generator().manual_seed(7)
+    b, m, kv_len, topk, scale = 3, 2, 5000, 700, 512 ** -0.5
+    q = torch.randn(b, m, 16, 512, generator=g).to(torch.bfloat16)
+    kv = torch.randn(b, kv_len, 512, generator=g).to(torch.bfloat16)
+    sink = torch.randn(16, generator=g)
+    idx = torch.randint(0, kv_len, (b, m, topk), generator=g, dtype=torch.int32)
+    idx[0, 0, 10:20] = idx[0, 0, 0]   # duplicates
+    idx[1, 1, 5:50] = -1
+    idx[2, 0, 7] = kv_len + 3         # out of range: masked
+    idx[2, 1] = -1                    # no valid slot
+    assert m * topk < kv_len
+    _check(q, kv, sink, idx, scale, seed=2, what="touched rows")
+    do = torch.randn(q.shape, generator=g).to(torch.bfloat16).cuda()
+    qc, kvc, sc, ic = q.cuda(), kv.cuda(), sink.cuda(), idx.cuda()
+    _, dkv, _ = sparse_attn_backward(qc, kvc, sc, ic, scale, sparse_attn(qc, kvc, sc, ic, scale), do)
+    touched = torch.zeros(b, kv_len, dtype=torch.bool)
+    for bi in range(b):
+        v = idx[bi].reshape(-1)
+        v = v[(v >= 0) & (v < kv_len)].long()
+        touched[bi, v] = True
+    assert dkv.dtype == torch.bfloat16
+    assert not dkv.cpu()[~touched].any()
+
+
 def test_backward_causal_head():
     args = make_golden.make_case("causal_head")
     _check(*args, seed=2, what="causal rows 0-39")
