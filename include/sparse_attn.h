@@ -110,6 +110,20 @@ int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx,
            const int64_t kv_strides[3], const int64_t idx_strides[3], const int64_t o_strides[4],
            const int64_t dkv_strides[3], float scale, void* stream);
 
+/* sa_bwd with an optional fp32 scratch for dq.  dq_acc (NULL, or zero-filled
+ * fp32 laid out like dq: contiguous [b, m, h, 512], 16-byte aligned) lets
+ * a call with the forward's lse and fewer query rows than half the SMs
+ * (decode) cut each row's slots into parts that run on separate CTAs; the
+ * parts add their dq into dq_acc and the library then writes dq from it.
+ * Otherwise, and with dq_acc NULL, it is sa_bwd.  No counterpart in the
+ * reference, which has no backward. */
+int sa_bwd_ex(const void* q, const void* kv, const float* sink, const int32_t* idx,
+              const void* o, const void* dout, const float* lse, void* dq, float* dkv,
+              float* dsink, int64_t b, int64_t m, int64_t h, int64_t d, int64_t kv_len,
+              int64_t topk, const int64_t q_strides[4], const int64_t kv_strides[3],
+              const int64_t idx_strides[3], const int64_t o_strides[4],
+              const int64_t dkv_strides[3], float scale, float* dq_acc, void* stream);
+
 /* The kv rows that one call's valid slots name (idx as for sa_fwd), in a
  * dense fp32 KV gradient laid out like the dkv of sa_bwd (strides multiples
  * of 4, 16-byte aligned).  A decode-shaped backward touches only

@@ -51,9 +51,8 @@ cudaError_t launch_indexer(const __nv_bfloat16* q, const __nv_bfloat16* k, const
                            const int64_t len_strides[2], const int64_t out_strides[3],
                            cudaStream_t st);
 cudaError_t launch_bwd(const Params& f, const __nv_bfloat16* dout, __nv_bfloat16* dq,
-                       int64_t dq_rs, float* dkv,
-                       float* dsink, int64_t dkv_sb, int64_t dkv_sn, float scale,
-                       cudaStream_t st);
+                       int64_t dq_rs, float* dkv, float* dsink, int64_t dkv_sb, int64_t dkv_sn,
+                       float scale, float* dq_acc, int sms, cudaStream_t st);
 cudaError_t launch_dkv_rows(bool cast, float* dkv, __nv_bfloat16* out, const int32_t* idx,
                             int64_t b, int64_t m, int64_t topk, int64_t kv_len,
                             const int64_t idx_strides[3], const int64_t dkv_strides[3],
@@ -514,11 +513,13 @@ static int bwd_group(const void* q, const void* kv, const float* sink, const int
                      int64_t kv_len, int64_t topk, const int64_t q_strides[4],
                      const int64_t kv_strides[3], const int64_t idx_strides[3],
                      const int64_t o_strides[4], const int64_t dkv_strides[3], float scale,
-                     void* stream) {
+                     void* stream, float* dq_acc = nullptr) {
   t_last_cuda_error = 0;
   if (b < 0 || m < 0 || kv_len < 0 || topk < 0) return SA_ERR_INVALID_ARG;
   if (h != sa::kHeads || d != sa::kDim) return SA_ERR_UNSUPPORTED;
   if (b == 0 || m == 0) return SA_OK;
+  if (dq_acc != nullptr && (reinterpret_cast<uintptr_t>(dq_acc) & 15u) != 0)
+    return SA_ERR_INVALID_ARG;
   if (!q || !kv || !sink || !idx || !o || !dout || !dq || !dkv || !dsink || !q_strides ||
       !kv_strides || !idx_strides || !o_strides || !dkv_strides)
     return SA_ERR_INVALID_ARG;
@@ -566,7 +567,7 @@ static int bwd_group(const void* q, const void* kv, const float* sink, const int
   p.lse_rs = h_total;
   e = sa::launch_bwd(p, static_cast<const __nv_bfloat16*>(dout), static_cast<__nv_bfloat16*>(dq),
                      h_total * sa::kDim, dkv, dsink, dkv_strides[0], dkv_strides[1], scale,
-                     static_cast<cudaStream_t>(stream));
+                     dq_acc, di->sms, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail_cuda(e);
   return SA_OK;
 }
@@ -638,16 +639,17 @@ int sa_fwd_fp8(const void* q, const void* kv8, const float* kv_scale, const floa
   return SA_OK;
 }
 
-int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx, const void* o,
-           const void* dout, const float* lse, void* dq, float* dkv, float* dsink, int64_t b,
-           int64_t m, int64_t h, int64_t d, int64_t kv_len, int64_t topk,
-           const int64_t q_strides[4], const int64_t kv_strides[3], const int64_t idx_strides[3],
-           const int64_t o_strides[4], const int64_t dkv_strides[3], float scale, void* stream) {
+static int bwd_impl(const void* q, const void* kv, const float* sink, const int32_t* idx,
+                    const void* o, const void* dout, const float* lse, void* dq, float* dkv,
+                    float* dsink, int64_t b, int64_t m, int64_t h, int64_t d, int64_t kv_len,
+                    int64_t topk, const int64_t q_strides[4], const int64_t kv_strides[3],
+                    const int64_t idx_strides[3], const int64_t o_strides[4],
+                    const int64_t dkv_strides[3], float scale, float* dq_acc, void* stream) {
   const int64_t groups = head_groups(h);
   if (groups == 1 || !q || !o || !dout || !dq || !sink || !dsink || !q_strides || !o_strides)
     return bwd_group(q, kv, sink, idx, o, dout, lse, h, dq, dkv, dsink, b, m,
                      groups == 1 ? h : sa::kHeads, d, kv_len, topk, q_strides, kv_strides,
-                     idx_strides, o_strides, dkv_strides, scale, stream);
+                     idx_strides, o_strides, dkv_strides, scale, stream, dq_acc);
   for (int64_t g = 0; g < groups; ++g) {
     const int64_t k = g * sa::kHeads;
     const int rc = bwd_group(
@@ -655,10 +657,31 @@ int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx,
         head_group_ptr(dout, g, o_strides[2]), lse ? lse + k : nullptr, h,
         const_cast<__nv_bfloat16*>(head_group_ptr(dq, g, sa::kDim)), dkv, dsink + k, b, m,
         sa::kHeads, d, kv_len, topk, q_strides, kv_strides, idx_strides, o_strides, dkv_strides,
-        scale, stream);
+        scale, stream, dq_acc ? dq_acc + k * sa::kDim : nullptr);
     if (rc != SA_OK) return rc;
   }
   return SA_OK;
+}
+
+int sa_bwd(const void* q, const void* kv, const float* sink, const int32_t* idx, const void* o,
+           const void* dout, const float* lse, void* dq, float* dkv, float* dsink, int64_t b,
+           int64_t m, int64_t h, int64_t d, int64_t kv_len, int64_t topk,
+           const int64_t q_strides[4], const int64_t kv_strides[3], const int64_t idx_strides[3],
+           const int64_t o_strides[4], const int64_t dkv_strides[3], float scale, void* stream) {
+  return bwd_impl(q, kv, sink, idx, o, dout, lse, dq, dkv, dsink, b, m, h, d, kv_len, topk,
+                  q_strides, kv_strides, idx_strides, o_strides, dkv_strides, scale, nullptr,
+                  stream);
+}
+
+int sa_bwd_ex(const void* q, const void* kv, const float* sink, const int32_t* idx,
+              const void* o, const void* dout, const float* lse, void* dq, float* dkv,
+              float* dsink, int64_t b, int64_t m, int64_t h, int64_t d, int64_t kv_len,
+              int64_t topk, const int64_t q_strides[4], const int64_t kv_strides[3],
+              const int64_t idx_strides[3], const int64_t o_strides[4],
+              const int64_t dkv_strides[3], float scale, float* dq_acc, void* stream) {
+  return bwd_impl(q, kv, sink, idx, o, dout, lse, dq, dkv, dsink, b, m, h, d, kv_len, topk,
+                  q_strides, kv_strides, idx_strides, o_strides, dkv_strides, scale, dq_acc,
+                  stream);
 }
 
 // sa_dkv_zero_rows / sa_dkv_cast_rows: the kv rows one call's valid slots

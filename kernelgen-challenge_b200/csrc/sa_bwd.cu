@@ -48,6 +48,11 @@ struct BwdParams {
   float* dsink;              // [16] fp32
   int64_t dkv_sb, dkv_sn;
   float scale;
+  // kSplit instance: each row's units are cut into `splits` contiguous parts,
+  // CTA x running part x % splits of row x / splits (one pass: lse given);
+  // the parts add dq into dq_acc (fp32, zero-filled, rows dq_rs floats apart)
+  int splits;
+  float* dq_acc;
 };
 
 struct __align__(1024) Smem {
@@ -104,6 +109,7 @@ __device__ __forceinline__ void sts64f(uint32_t addr, float a, float b) {
   asm volatile("st.shared.v2.f32 [%0], {%1,%2};\n" ::"r"(addr), "f"(a), "f"(b) : "memory");
 }
 
+template <bool kSplit>
 __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
   extern __shared__ uint8_t smem_raw[];
   Smem& S = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -111,7 +117,7 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
   const Params& p = bp.f;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, q4 = lane & 3;
-  const int64_t row = blockIdx.x;
+  const int64_t row = kSplit ? blockIdx.x / bp.splits : blockIdx.x;
   const int64_t tb = row / p.m, tm = row - tb * p.m;
   const int32_t* irow = p.idx + tb * p.i_sb + tm * p.i_sm;
   // Units up to the row's last valid slot: trailing masked slots (causal
@@ -209,8 +215,14 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
 #pragma unroll
   for (int nt = 0; nt < 8; ++nt) dq[nt][0] = dq[nt][1] = dq[nt][2] = dq[nt][3] = 0.f;
 
-  // with the forward's log-sum-exp (sa_fwd_train) pass A is skipped
-  const int64_t i0 = p.lse != nullptr ? U : 0;
+  // with the forward's log-sum-exp (sa_fwd_train) pass A is skipped; the
+  // loop runs i = i0 .. iend - 1, unit i % U (i >= U: pass B)
+  int64_t i0 = p.lse != nullptr ? U : 0, iend = 2 * U;
+  if constexpr (kSplit) {  // (lse given)
+    const int64_t part = blockIdx.x % bp.splits;
+    i0 = U + part * U / bp.splits;
+    iend = U + (part + 1) * U / bp.splits;
+  }
   if (p.lse != nullptr && tid < kHeads) {
     const float sl2 = __ldg(p.sink + tid) * kLog2e;
     const float L = p.lse[row * p.lse_rs + tid];
@@ -219,14 +231,15 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
     // dsink = -p_sink * D once the D of this row is in shared memory (below)
     S.red[0][0][tid] = exp2f(sl2 - L);
   }
-  if (i0 < 2 * U) issue(i0 % U, i0 & 1);
+  if (i0 < iend) issue(i0 % U, i0 & 1);
   if (p.lse != nullptr) {
     __syncthreads();  // D and the sink weights
-    if (tid < kHeads) atomicAdd(bp.dsink + tid, -S.red[0][0][tid] * S.D[tid]);
+    if (tid < kHeads && (!kSplit || blockIdx.x % bp.splits == 0))
+      atomicAdd(bp.dsink + tid, -S.red[0][0][tid] * S.D[tid]);
   }
-  for (int64_t i = i0; i < 2 * U; ++i) {
+  for (int64_t i = i0; i < iend; ++i) {
     const int s = static_cast<int>(i & 1);
-    if (i + 1 < 2 * U) {
+    if (i + 1 < iend) {
       issue((i + 1) % U, s ^ 1);
       cp_async_wait<1>();
     } else {
@@ -390,6 +403,19 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
   cp_async_wait<0>();  // (no units: the Q / dO copies)
   bulk_wait();         // the dkv reductions are done before the CTA exits
   // ---- dq of this row (the scale is already in dS)
+  if constexpr (kSplit) {  // this part's share, added into the fp32 rows
+    if (iend > i0) {
+      float* dqa = bp.dq_acc + row * bp.dq_rs;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int d = 64 * warp + 8 * nt + 2 * q4;
+        atomicAdd(reinterpret_cast<float2*>(dqa + g8 * kDim + d), make_float2(dq[nt][0], dq[nt][1]));
+        atomicAdd(reinterpret_cast<float2*>(dqa + (g8 + 8) * kDim + d),
+                  make_float2(dq[nt][2], dq[nt][3]));
+      }
+    }
+    return;
+  }
   __nv_bfloat16* dqr = bp.dq + row * bp.dq_rs;
 #pragma unroll
   for (int nt = 0; nt < 8; ++nt) {
@@ -398,8 +424,6 @@ __global__ void __launch_bounds__(NT, 1) sa_bwd_kernel(const BwdParams bp) {
     *reinterpret_cast<uint32_t*>(dqr + (g8 + 8) * kDim + d) = pack_bf16x2(dq[nt][2], dq[nt][3]);
   }
 }
-
-}  // namespace bwd_path
 
 // ---------------------------------------------------------------------------
 // The rows of a dense KV gradient that one call touches: the kv rows its
@@ -442,11 +466,25 @@ __global__ void __launch_bounds__(256) sa_dkv_rows_kernel(const RowsParams rp) {
   }
 }
 
+// dq[row][h][:] = bf16(dq_acc[row][h][:]) for the 16 heads of a group
+__global__ void __launch_bounds__(256) sa_dq_cast_kernel(const float* acc, __nv_bfloat16* dq,
+                                                         int64_t rows, int64_t rs) {
+  const int64_t n4 = rows * (kHeads * kDim / 4);
+  for (int64_t k = (int64_t)blockIdx.x * 256 + threadIdx.x; k < n4; k += (int64_t)gridDim.x * 256) {
+    const int64_t r = k / (kHeads * kDim / 4), c = (k - r * (kHeads * kDim / 4)) * 4;
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(acc + r * rs + c));
+    *reinterpret_cast<uint2*>(dq + r * rs + c) =
+        make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  }
+}
+
+}  // namespace bwd_path
+
 cudaError_t launch_dkv_rows(bool cast, float* dkv, __nv_bfloat16* out, const int32_t* idx,
                             int64_t b, int64_t m, int64_t topk, int64_t kv_len,
                             const int64_t idx_strides[3], const int64_t dkv_strides[3],
                             const int64_t out_strides[3], int sms, cudaStream_t st) {
-  RowsParams rp{dkv, out, idx, b, m, topk, kv_len,
+  bwd_path::RowsParams rp{dkv, out, idx, b, m, topk, kv_len,
                 idx_strides[0], idx_strides[1], idx_strides[2], dkv_strides[0], dkv_strides[1],
                 cast ? out_strides[0] : 0, cast ? out_strides[1] : 0};
   const int64_t nslot = b * m * topk;
@@ -454,25 +492,49 @@ cudaError_t launch_dkv_rows(bool cast, float* dkv, __nv_bfloat16* out, const int
   int64_t blocks = (nslot + 7) / 8;
   if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;
   if (cast) {
-    sa_dkv_rows_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, st>>>(rp);
+    bwd_path::sa_dkv_rows_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, st>>>(rp);
   } else {
-    sa_dkv_rows_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, st>>>(rp);
+    bwd_path::sa_dkv_rows_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, st>>>(rp);
   }
   return cudaGetLastError();
 }
 
 cudaError_t launch_bwd(const Params& f, const __nv_bfloat16* dout, __nv_bfloat16* dq,
-                       int64_t dq_rs, float* dkv, float* dsink, int64_t dkv_sb, int64_t dkv_sn, float scale,
-                       cudaStream_t st) {
+                       int64_t dq_rs, float* dkv, float* dsink, int64_t dkv_sb, int64_t dkv_sn,
+                       float scale, float* dq_acc, int sms, cudaStream_t st) {
   using namespace bwd_path;
   static PerDeviceOnce attr_once;
   cudaError_t e = once_per_device(attr_once, [] {
-    return cudaFuncSetAttribute(sa_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    const cudaError_t e1 = cudaFuncSetAttribute(
+        sa_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e1 != cudaSuccess) return e1;
+    return cudaFuncSetAttribute(sa_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)kSmemBytes);
   });
   if (e != cudaSuccess) return e;
-  BwdParams bp{f, dout, dq, dq_rs, dkv, dsink, dkv_sb, dkv_sn, scale};
-  sa_bwd_kernel<<<static_cast<unsigned>(f.b * f.m), NT, kSmemBytes, st>>>(bp);
+  const int64_t rows = f.b * f.m;
+  // Fewer rows than SMs (decode): with the log-sum-exp and an fp32 dq
+  // scratch, each row runs as `splits` parts on as many CTAs, one wave in
+  // all (the kernel holds one CTA per SM); each part keeps >= 2 units.
+  int splits = 1;
+  if (dq_acc != nullptr && f.lse != nullptr && rows > 0 && rows * 2 <= sms) {
+    splits = static_cast<int>(sms / rows);
+    const int64_t max_parts = (f.topk + 2 * UK - 1) / (2 * UK);
+    if (splits > max_parts) splits = static_cast<int>(max_parts > 1 ? max_parts : 1);
+  }
+  BwdParams bp{f, dout, dq, dq_rs, dkv, dsink, dkv_sb, dkv_sn, scale, splits, dq_acc};
+  if (splits == 1) {
+    sa_bwd_kernel<false><<<static_cast<unsigned>(rows), NT, kSmemBytes, st>>>(bp);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || dq_acc == nullptr) return e;
+    return cudaSuccess;  // (dq written by the kernel; dq_acc unused)
+  }
+  sa_bwd_kernel<true><<<static_cast<unsigned>(rows * splits), NT, kSmemBytes, st>>>(bp);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  int64_t blocks = (rows * (kHeads * kDim / 4) + 255) / 256;
+  if (blocks > (int64_t)sms * 8) blocks = (int64_t)sms * 8;
+  sa_dq_cast_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(dq_acc, dq, rows, dq_rs);
   return cudaGetLastError();
 }
 

@@ -59,6 +59,7 @@ SIGNATURES = {
     "sa_quantize_kv_fp8": (ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _I64P, _I64P, _I64P,
                                           _P]),
     "sa_bwd": (ctypes.c_int, [_P] * 10 + [_I64] * 6 + [_I64P] * 5 + [ctypes.c_float, _P]),
+    "sa_bwd_ex": (ctypes.c_int, [_P] * 10 + [_I64] * 6 + [_I64P] * 5 + [ctypes.c_float, _P, _P]),
     "sa_dkv_zero_rows": (ctypes.c_int, [_P, _P] + [_I64] * 4 + [_I64P] * 2 + [_P]),
     "sa_dkv_cast_rows": (ctypes.c_int, [_P] * 3 + [_I64] * 4 + [_I64P] * 3 + [_P]),
     "sa_fwd_train": (ctypes.c_int, [_P] * 6 + [_I64] * 6 + [_I64P] * 4

@@ -203,6 +203,16 @@ def _forward_train(q, kv, attn_sink, topk_idxs, scale):
     return o, lse
 
 
+_SM_COUNTS = {}
+
+
+def _sm_count(device) -> int:
+    idx = torch.device(device).index
+    if idx not in _SM_COUNTS:
+        _SM_COUNTS[idx] = torch.cuda.get_device_properties(device).multi_processor_count
+    return _SM_COUNTS[idx]
+
+
 def sparse_attn_backward(q, kv, attn_sink, topk_idxs, scale, o, do, lse=None):
     """Gradients of ``sparse_attn`` (``sa_bwd`` in ``libsparse_attn.so``).
 
@@ -249,14 +259,20 @@ def sparse_attn_backward(q, kv, attn_sink, topk_idxs, scale, o, do, lse=None):
             _lib.check(_lib.lib().sa_dkv_zero_rows(
                 dkv.data_ptr(), topk_idxs.data_ptr(), *ids[:4], ids[4],
                 _lib.i64_array(dkv.stride()), st.cuda_stream))
-        _lib.check(_lib.lib().sa_bwd(
+        # decode-shaped calls with the lse: rows split over CTAs, dq through
+        # an fp32 scratch (sa_bwd_ex)
+        dq_acc = None
+        if lse_c is not None and 2 * b * m <= _sm_count(q.device):
+            dq_acc = torch.zeros(dq.shape, dtype=torch.float32, device=q.device)
+        _lib.check(_lib.lib().sa_bwd_ex(
             q_c.data_ptr(), kv_c.data_ptr(), attn_sink.contiguous().data_ptr(),
             topk_idxs.data_ptr(), o_c.data_ptr(), do_c.data_ptr(),
             None if lse_c is None else lse_c.data_ptr(), dq.data_ptr(),
             dkv.data_ptr(), dsink.data_ptr(), b, m, h, d, kv.shape[1], topk_idxs.shape[-1],
             _lib.i64_array(q_c.stride()), _lib.i64_array(kv_c.stride()),
             _lib.i64_array(topk_idxs.stride()), _lib.i64_array(o_c.stride()),
-            _lib.i64_array(dkv.stride()), float(scale), st.cuda_stream))
+            _lib.i64_array(dkv.stride()), float(scale),
+            None if dq_acc is None else dq_acc.data_ptr(), st.cuda_stream))
         if rows_only:
             out = torch.zeros(kv.shape, dtype=kv.dtype, device=q.device)
             _lib.check(_lib.lib().sa_dkv_cast_rows(

@@ -180,3 +180,28 @@ def test_training_forward_lse_and_one_pass_backward(name):
     g2 = sparse_attn_backward(qc, kvc, sc, ic, scale, o, do)
     for a, e, what in zip(g1, g2, ("dq", "dkv", "dsink")):
         _close(a, e, f"{name} one-pass vs two-pass {what}")
+
+
+@pytest.mark.parametrize("b,h", [(4, 16), (8, 16), (3, 32), (70, 16)])
+def test_one_pass_backward_with_split_rows(b, h):
+    """Decode rows with the log-sum-exp: when the rows are fewer than half the
+    SMs, each row's slots run as several parts on separate CTAs, dq added
+    through an fp32 scratch (b = 70 stays unsplit).  Against autograd of the
+    oracle, with masked and duplicated slots."""
+    from sparse_attn.op import _forward_train
+    q, kv, sink, idx, scale = make_inputs("decode", seed=11, b=b)
+    if h != 16:
+        q = q.repeat(1, 1, h // 16, 1).contiguous()
+        sink = sink.repeat(h // 16).contiguous()
+    idx[0, 0, 100:400] = -1
+    idx[b - 1, 0, 5:9] = idx[b - 1, 0, 0]
+    g = torch.Generator().manual_seed(4)
+    do = torch.randn(q.shape, generator=g).to(torch.bfloat16)
+    qc, kvc, sc, ic = q.cuda(), kv.cuda(), sink.cuda(), idx.cuda()
+    o, lse = _forward_train(qc, kvc, sc, ic, scale)
+    dq, dkv, dsink = sparse_attn_backward(qc, kvc, sc, ic, scale, o, do.cuda(), lse)
+    torch.cuda.synchronize()
+    _, rq, rkv, rs = sparse_attn_oracle_grads(q, kv, sink, idx, scale, do)
+    _close(dq, rq, f"b={b} h={h} dq")
+    _close(dkv, rkv, f"b={b} h={h} dkv")
+    _close(dsink, rs, f"b={b} h={h} dsink")
