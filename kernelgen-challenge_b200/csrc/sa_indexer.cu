@@ -546,8 +546,10 @@ __device__ __forceinline__ uint32_t radix_round(Get get, int n, uint32_t prefix,
   return digit;
 }
 
-// NT2 threads per row: 512 for long rows, 128 for rows of up to kShortRow
-// keys, so that more rows (each a chain of barriers) run side by side.
+// NT2 threads per row: 1024 for long rows (one row per SM: the row's staged
+// scores fill its shared memory, and the rounds' barrier chains need every
+// warp the SM can hold), 128 for rows of up to kShortRow keys, so that more
+// rows run side by side.
 // Selection: an 11-bit round over the whole row (sign, exponent and three
 // mantissa bits of the scores) finds the bin holding the topk-th largest key;
 // that bin's keys are gathered into a short candidate list, and two more
@@ -799,7 +801,7 @@ cudaError_t launch_indexer(const __nv_bfloat16* q, const __nv_bfloat16* k, const
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                               (int)(kShortRow * sizeof(float)));
     if (e1 != cudaSuccess) return e1;
-    return cudaFuncSetAttribute(sa_indexer_topk_kernel<512>,
+    return cudaFuncSetAttribute(sa_indexer_topk_kernel<1024>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)(kSmemKeys * sizeof(float)));
   });
@@ -824,7 +826,7 @@ cudaError_t launch_indexer(const __nv_bfloat16* q, const __nv_bfloat16* k, const
   if (kv_len <= kShortRow) {
     sa_indexer_topk_kernel<128><<<static_cast<unsigned>(rows), 128, staged, st>>>(P);
   } else {
-    sa_indexer_topk_kernel<512><<<static_cast<unsigned>(rows), 512, staged, st>>>(P);
+    sa_indexer_topk_kernel<1024><<<static_cast<unsigned>(rows), 1024, staged, st>>>(P);
   }
   return cudaGetLastError();
 }
