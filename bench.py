@@ -303,20 +303,31 @@ def cpu_sample_inputs(cfg, rows, seed=0):
 
 
 CPU_IMPL = "fp32 torch CPU restatement of reference.py (oracle/sparse_attn_oracle.py)"
+REF_IMPL = ("the unmodified track-01/reference/reference.py (its torch CPU path), from the "
+            "copy baseline/install_reference.sh puts in baseline/_ref")
 
 
-def cpu_impl():
-    """The reference's algorithm on the host cores, written with the same torch
-    ops as reference.py (the faster CPU form on the GPU hosts: torch's
-    vectorised einsum beats the scalar C restatement in oracle/sa_host.c)."""
-    from oracle.sparse_attn_oracle import sparse_attn_oracle
+def cpu_impl(cfg=None):
+    """(fn, cores, kind, description): the reference's algorithm on the host
+    cores.  Where the reference's own reference.py is installed
+    (baseline/_ref) and the configuration has no -1 slots (reference.py
+    raises on them: the causal rows' padding), that function itself
+    ("reference"); otherwise its restatement with the masking rule, written
+    with the same torch ops ("port")."""
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    return sparse_attn_oracle, cores
+    ref = REF_DIR / "reference" / "reference.py"
+    if cfg is not None and cfg.pattern != "causal" and ref.exists():
+        if str(REF_DIR) not in sys.path:
+            sys.path.insert(0, str(REF_DIR))
+        import importlib
+        return importlib.import_module("reference.reference").sparse_attn, cores, "reference", REF_IMPL
+    from oracle.sparse_attn_oracle import sparse_attn_oracle
+    return sparse_attn_oracle, cores, "port", CPU_IMPL
 
 
 def cpu_throughput(cfg, rows, min_seconds, max_reps):
-    fn, cores = cpu_impl()
+    fn, cores, _, _ = cpu_impl(cfg)
     q, kv, sink, idx, scale, n = cpu_sample_inputs(cfg, rows)
     fn(q, kv, sink, idx, scale)  # warm-up
     reps, t0 = 0, time.perf_counter()
@@ -334,7 +345,7 @@ def run_reference(args):
     if rank != 0:
         return
     cfg = CONFIGS[args.config]
-    fn, cores = cpu_impl()
+    fn, cores, kind, desc = cpu_impl(cfg)
     rows = 16
     q, kv, sink, idx, scale, n = cpu_sample_inputs(cfg, rows)
     for _ in range(max(args.warmup, 0)):
@@ -345,7 +356,7 @@ def run_reference(args):
     el = time.perf_counter() - t0
     val = n * args.steps / el
     sample = (f"{n} query rows of config '{cfg.name}' per step (b=1 slice, kv_len={cfg.kv_len}, "
-              f"topk={cfg.topk}), {CPU_IMPL}")
+              f"topk={cfg.topk}), {desc}")
     line = {
         "metric": METRIC, "value": val, "unit": UNIT, "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -353,7 +364,7 @@ def run_reference(args):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded CPU generator)",
         "config": {"workload": cfg.name, "b": cfg.b, "m": cfg.m, "h": H, "d": D,
                    "kv_len": cfg.kv_len, "topk": cfg.topk, "sample_rows_per_step": n},
-        "cpu_baseline": {"value": val, "unit": UNIT, "cores": cores, "kind": "port",
+        "cpu_baseline": {"value": val, "unit": UNIT, "cores": cores, "kind": kind,
                          "sample": sample},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -905,9 +916,10 @@ def measure_config(cfg, args, rank, world, dev, flush, barrier, K, *, headline, 
         res["e2e"] = None
     if with_cpu and world == 1:
         val, n, reps, el, cores = cpu_throughput(cfg, rows=16, min_seconds=8.0, max_reps=200)
+        _, _, kind, desc = cpu_impl(cfg)
         res["cpu_baseline"] = {
-            "value": val, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{n} query rows of '{cfg.name}' x {reps} reps ({el:.1f} s), {CPU_IMPL}"}
+            "value": val, "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"{n} query rows of '{cfg.name}' x {reps} reps ({el:.1f} s), {desc}"}
     else:
         res["cpu_baseline"] = None
     res["_case"] = case
