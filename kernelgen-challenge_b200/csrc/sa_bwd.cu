@@ -523,11 +523,9 @@ cudaError_t launch_bwd(const Params& f, const __nv_bfloat16* dout, __nv_bfloat16
     if (splits > max_parts) splits = static_cast<int>(max_parts > 1 ? max_parts : 1);
   }
   BwdParams bp{f, dout, dq, dq_rs, dkv, dsink, dkv_sb, dkv_sn, scale, splits, dq_acc};
-  if (splits == 1) {
+  if (splits == 1) {  // the kernel writes dq itself; dq_acc, if given, stays unused
     sa_bwd_kernel<false><<<static_cast<unsigned>(rows), NT, kSmemBytes, st>>>(bp);
-    e = cudaGetLastError();
-    if (e != cudaSuccess || dq_acc == nullptr) return e;
-    return cudaSuccess;  // (dq written by the kernel; dq_acc unused)
+    return cudaGetLastError();
   }
   sa_bwd_kernel<true><<<static_cast<unsigned>(rows * splits), NT, kSmemBytes, st>>>(bp);
   e = cudaGetLastError();
